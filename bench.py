@@ -1,0 +1,401 @@
+"""Benchmark of the hot path on B200: the deformable-attention sampler forward + backward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one "step"): config 2 of the baseline -- the Nano decoder cross-attention sampler at
+training shape, forward + backward: B=8 images per GPU, Lq=3900 (300 queries x 13 groups), one
+24x24 level, 16 heads x 16 channels, 2 points; value/weights/output bf16, locations fp32.
+Inputs are seeded synthetic tensors with the config's distributions.  Metric: queries per second
+(B * Lq per step per GPU), whole job.  Under torchrun each rank runs its own batch of 8 (weak
+scaling; the sampler has no cross-GPU exchange) and the step time is the max over ranks.
+
+Device timing: inputs resident in HBM, a ring of input/output sets larger than L2 so no step
+reads another step's data from L2, each step one CUDA-graph replay of the two library calls,
+CUDA events around K steps.  ``e2e``: the public API (``ms_deform_attn_core_rows`` + autograd)
+from pinned host buffers, host->device copies of the step's inputs and device->host copies of
+the output and all three gradients inside the timed region.
+
+``--impl reference`` times the CPU restatement of the reference's sampler (``oracle/msda.py``,
+float32) on the host cores with a process pool over the images of the same workload: JAX, the
+reference's runtime, is not installable here, so the reference's XLA-CPU path cannot run.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+# Config 2 geometry.
+B, LQ, H, D, P = 8, 3900, 16, 16, 2
+SHAPES = ((24, 24),)
+LV = 576
+METRIC = "ms_deform_attn fwd+bwd queries/s (config 2: Nano train shape, bf16)"
+UNIT = "queries/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def algorithmic_bytes():
+    """Unique bytes read once + written once per launch (value/w/out/grads bf16, loc fp32)."""
+    value = B * H * LV * D * 2
+    loc = B * LQ * H * 1 * P * 2 * 4
+    attn = B * LQ * H * P * 2
+    out = B * LQ * H * D * 2
+    fwd = value + loc + attn + out
+    bwd = value + loc + attn + out + value + loc + attn  # reads value, loc, w, grad_out; writes grads
+    return fwd, bwd
+
+
+def make_inputs(seed, torch, device):
+    rng = np.random.default_rng(seed)
+    value = rng.standard_normal((B * H, LV, D)).astype(np.float32)
+    loc = rng.uniform(-0.05, 1.05, (B, LQ, H, 1, P, 2)).astype(np.float32)
+    logits = rng.standard_normal((B, LQ, H, P)).astype(np.float32)
+    attn = np.exp(logits - logits.max(-1, keepdims=True))
+    attn = (attn / attn.sum(-1, keepdims=True)).astype(np.float32)
+    grad = rng.standard_normal((B, LQ, H * D)).astype(np.float32)
+    t = lambda x, dt: torch.tensor(x, device=device).to(dt)  # noqa: E731
+    return (t(value, torch.bfloat16), t(loc, torch.float32), t(attn, torch.bfloat16), t(grad, torch.bfloat16))
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.file = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.file.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return None
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax = float(parts[2])
+                except ValueError:
+                    continue
+                for name, flag in zip(names, parts[5:9]):
+                    if flag.lower() == "active":
+                        reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline_sample(steps_budget_s=20.0):
+    """The oracle (float32) forward + backward on one image of the workload, single thread."""
+    from oracle import msda as O
+
+    rng = np.random.default_rng(1)
+    value = rng.standard_normal((H, LV, D)).astype(np.float32)
+    loc = rng.uniform(-0.05, 1.05, (LQ, H, 1, P, 2)).astype(np.float32)
+    attn = np.full((LQ, H, P), 1.0 / P, np.float32)
+    grad = rng.standard_normal((LQ, H * D)).astype(np.float32)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.forward_image(value, SHAPES, loc, attn, np.float32)
+        O.backward_image(value, SHAPES, loc, attn, grad, np.float32)
+        reps += 1
+        if time.perf_counter() - t0 > min(steps_budget_s, 10.0) or reps >= 20:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": LQ / dt, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"oracle/msda.py float32 fwd+bwd on 1 of {B} images ({LQ} queries), {reps} reps"}
+
+
+def _reference_image(args):
+    seed, b = args
+    from oracle import msda as O
+
+    rng = np.random.default_rng(seed * 100 + b)
+    value = rng.standard_normal((H, LV, D)).astype(np.float32)
+    loc = rng.uniform(-0.05, 1.05, (LQ, H, 1, P, 2)).astype(np.float32)
+    attn = np.full((LQ, H, P), 1.0 / P, np.float32)
+    grad = rng.standard_normal((LQ, H * D)).astype(np.float32)
+    O.forward_image(value, SHAPES, loc, attn, np.float32)
+    O.backward_image(value, SHAPES, loc, attn, grad, np.float32)
+    return b
+
+
+def run_reference(args):
+    """CPU reference arm: the oracle port over all host cores (process pool over images)."""
+    import multiprocessing as mp
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cores = max(1, min(os.cpu_count() or 1, B))
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        for s in range(args.warmup):
+            pool.map(_reference_image, [(s, b) for b in range(B)])
+        t0 = time.perf_counter()
+        for s in range(args.steps):
+            pool.map(_reference_image, [(1000 + s, b) for b in range(B)])
+        dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = B * LQ / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 sampler fwd+bwd", "batch": B, "len_query": LQ, "heads": H, "head_dim": D,
+                   "levels": [list(s) for s in SHAPES], "points": P},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"full workload ({B} images x {LQ} queries) per step, float32 NumPy restatement "
+                                   "of the reference sampler (JAX not installable: XLA-CPU path unavailable)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    from rfdetr_jax_b200 import _native as N
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    lib = N.lib()
+    stream = torch.cuda.Stream(device)
+    fwd_bytes, bwd_bytes = algorithmic_bytes()
+    per_set = 2 * (fwd_bytes + bwd_bytes)
+    ring = max(4, int(np.ceil(3 * L2_BYTES / per_set)))
+    sets = []
+    for r in range(ring):
+        value, loc, attn, grad = make_inputs(1 + r + 97 * rank, torch, device)
+        out = torch.empty((B, LQ, H * D), dtype=torch.bfloat16, device=device)
+        gv = torch.empty_like(value)
+        gl = torch.empty_like(loc)
+        ga = torch.empty_like(attn)
+        ws_bytes = lib.rfdetr_msda_backward_workspace_size(N.BF16, B, H, D, LV)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+        sets.append((value, loc, attn, grad, out, gv, gl, ga, ws, ws_bytes))
+    shapes = N.int64_array([24, 24])
+
+    def fwd(s, st):
+        value, loc, attn, _, out = s[:5]
+        N.check(lib.rfdetr_msda_forward(st, value.data_ptr(), N.BF16, shapes, None, loc.data_ptr(), attn.data_ptr(),
+                                        N.BF16, out.data_ptr(), N.BF16, B, H, D, LQ, 1, P), "forward")
+
+    def bwd(s, st):
+        value, loc, attn, grad, _, gv, gl, ga, ws, ws_bytes = s
+        N.check(lib.rfdetr_msda_backward(st, value.data_ptr(), N.BF16, shapes, None, loc.data_ptr(),
+                                         attn.data_ptr(), N.BF16, grad.data_ptr(), N.BF16, gv.data_ptr(),
+                                         gl.data_ptr(), ga.data_ptr(), ws.data_ptr(), ws_bytes, B, H, D, LQ, 1, P),
+                "backward")
+
+    # Warm-up eagerly (sets kernel attributes), then capture one graph per input set and op.
+    with torch.cuda.stream(stream):
+        for s in sets:
+            fwd(s, stream.cuda_stream)
+            bwd(s, stream.cuda_stream)
+    stream.synchronize()
+    graphs = {"step": [], "fwd": [], "bwd": []}
+    for s in sets:
+        for kind in graphs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
+                cs = torch.cuda.current_stream().cuda_stream
+                if kind in ("step", "fwd"):
+                    fwd(s, cs)
+                if kind in ("step", "bwd"):
+                    bwd(s, cs)
+            graphs[kind].append(g)
+    torch.cuda.synchronize()
+
+    def timed(kind, steps, warmup):
+        gl_ = graphs[kind]
+        with torch.cuda.stream(stream):
+            for i in range(warmup):
+                gl_[i % ring].replay()
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(steps):
+                gl_[i % ring].replay()
+            end.record(stream)
+        end.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        ms = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms / steps
+
+    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    with ClockSampler(gpu_index) as clocks:
+        ms_step = timed("step", args.steps, args.warmup)
+        ms_fwd = timed("fwd", args.steps, args.warmup)
+        ms_bwd = timed("bwd", args.steps, args.warmup)
+    clock_summary = clocks.summary()
+
+    # End to end through the public API from pinned host memory.
+    host = [x.cpu().pin_memory() for x in sets[0][:4]]
+    h_out = torch.empty((B, LQ, H * D), dtype=torch.bfloat16).pin_memory()
+    h_gv = torch.empty_like(host[0]).pin_memory()
+    h_gl = torch.empty_like(host[1]).pin_memory()
+    h_ga = torch.empty_like(host[2]).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in host)
+    d2h = sum(x.numel() * x.element_size() for x in (h_out, h_gv, h_gl, h_ga))
+
+    def e2e_step():
+        v = host[0].to(device, non_blocking=True).requires_grad_(True)
+        loc = host[1].to(device, non_blocking=True).requires_grad_(True)
+        a = host[2].to(device, non_blocking=True).requires_grad_(True)
+        g = host[3].to(device, non_blocking=True)
+        out = pkg.ms_deform_attn_core_rows(v, SHAPES, loc, a, "cuda")
+        out.backward(g)
+        h_out.copy_(out.detach(), non_blocking=True)
+        h_gv.copy_(v.grad, non_blocking=True)
+        h_gl.copy_(loc.grad, non_blocking=True)
+        h_ga.copy_(a.grad, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            e2e_step()
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, min(args.steps, 20))
+    with torch.cuda.stream(stream):
+        e_start.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e_end.record(stream)
+    e_end.synchronize()
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    cpu = cpu_baseline_sample() if (rank == 0 and world == 1) else None
+
+    queries = B * LQ * world
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, peak_src = 6650.0, "fallback"
+    if os.path.exists(peaks_path):
+        with open(peaks_path) as f:
+            peak, peak_src = float(json.load(f)["hbm_gbs"]), "measured"
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("msda_backward_c2")
+    achieved = bwd_bytes / (ms_bwd * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": queries / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config2 sampler fwd+bwd (Nano decoder cross-attn, train shape)",
+                   "batch_per_gpu": B, "len_query": LQ, "heads": H, "head_dim": D,
+                   "levels": [list(s) for s in SHAPES], "points": P, "parallelism": f"dp{world} (independent shards)",
+                   "l2": f"ring of {ring} input/output sets ({ring * per_set / 2**20:.0f} MiB) > L2, no flush"},
+        "roofline": {"bound": "hbm", "kernel": "msda_backward (memset + kernel + fp32->bf16)", "achieved": achieved,
+                     "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": peak_src, "algorithmic_bytes": bwd_bytes, "ms_per_launch": ms_bwd},
+        "kernels": {"msda_forward": {"ms": ms_fwd, "GB/s": fwd_bytes / (ms_fwd * 1e-3) / 1e9,
+                                     "frac": fwd_bytes / (ms_fwd * 1e-3) / 1e9 / peak},
+                    "msda_backward": {"ms": ms_bwd, "GB/s": achieved, "frac": achieved / peak}},
+        "e2e": {"value": queries / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clock_summary,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for kind in graphs:
+        graphs[kind].clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

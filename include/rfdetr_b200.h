@@ -1,0 +1,158 @@
+/*
+ * rfdetr_b200 -- C ABI of the B200 (sm_100a) backend for RF-DETR-JAX's training hot path.
+ *
+ * Every entry point takes raw device pointers, explicit sizes, element-type codes and the
+ * CUDA stream to run on (passed as void*, it is a cudaStream_t), and returns an int status
+ * (RFDETR_OK = 0).  Calls are asynchronous on that stream, never synchronise the device and
+ * allocate no memory: scratch space comes from the caller as an explicit workspace.  They
+ * keep no state between calls, so one process may drive several devices from several threads
+ * (the device is the one current on the calling thread).  There is no CPU fallback: a build
+ * without a usable sm_100a device fails with RFDETR_ERR_CUDA.
+ *
+ * Layouts are the reference's own (row-major, innermost last).  Paths cited as file:line are
+ * inside the reference project (JESUSROYETH/rf-detr-jax).
+ */
+#ifndef RFDETR_B200_H
+#define RFDETR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types. */
+enum rfdetr_dtype { RFDETR_F32 = 0, RFDETR_BF16 = 1 };
+
+/* Status codes. */
+enum rfdetr_status {
+    RFDETR_OK = 0,
+    RFDETR_ERR_SHAPE = 1,     /* sizes inconsistent, negative or beyond a supported limit */
+    RFDETR_ERR_DTYPE = 2,     /* element type not supported for this argument */
+    RFDETR_ERR_ALIGN = 3,     /* a pointer is not aligned to its element type */
+    RFDETR_ERR_WORKSPACE = 4, /* workspace missing or smaller than the size query returned */
+    RFDETR_ERR_CUDA = 5,      /* a CUDA runtime call or kernel launch failed */
+    RFDETR_ERR_LIMIT = 6      /* a device loop reached its iteration cap (reported via status buffer) */
+};
+
+/* Human-readable text for a status code (static storage). */
+const char *rfdetr_status_string(int status);
+
+/* ABI version of this library; bumped on any signature change. */
+int rfdetr_abi_version(void);
+
+/* ---------------------------------------------------------------------------------------
+ * Multi-scale deformable attention sampler.
+ *
+ * Replaces ms_deform_attn_core_rows(value, spatial_shapes, sampling_locations,
+ * attention_weights, sampler)  -- src/rfdetr_jax/models/ops.py:208-292 -- as the new
+ * sampler "cuda", and its JAX-autodiff backward (the gather path's scatter-add,
+ * tests/test_ops.py:157-167; analytic formulas deform_pallas.py:97-120).
+ *
+ *   value               [B*H, Lv, D]        value_dtype (f32 | bf16), Lv = sum_l H_l*W_l
+ *   spatial_shapes      host int64 [L][2]   (H_l, W_l) per level
+ *   level_start_index   host int64 [L]      offsets of the levels in Lv, or NULL to derive
+ *                                           them from spatial_shapes (ops.py:265-267)
+ *   sampling_locations  [B, Lq, H, L, P, 2] f32, (x, y) in [0, 1] (ops.py:220)
+ *   attention_weights   [B, Lq, H, L*P]     weight_dtype (f32 | bf16)
+ *   output              [B, Lq, H*D]        bf16 if value and weights are both bf16, else f32
+ *                                           (result_type(value, weights), ops.py:260)
+ * Numerics: positions are computed in float32 in the reference's op order
+ * (2*loc-1, ((g+1)*W-1)/2; ops.py:83-84,270); interpolation and accumulation in float32.
+ * Limits: 1 <= L <= 16, D <= 256, all sizes < 2^31 elements per tensor.
+ * ------------------------------------------------------------------------------------- */
+int rfdetr_msda_forward(void *stream,
+                        const void *value, int value_dtype,
+                        const int64_t *spatial_shapes, const int64_t *level_start_index,
+                        const float *sampling_locations,
+                        const void *attention_weights, int weight_dtype,
+                        void *output, int output_dtype,
+                        int64_t batch, int64_t n_heads, int64_t head_dim, int64_t len_query,
+                        int64_t n_levels, int64_t n_points);
+
+/* Workspace bytes rfdetr_msda_backward needs (0 when value_dtype is f32). */
+size_t rfdetr_msda_backward_workspace_size(int value_dtype, int64_t batch, int64_t n_heads,
+                                           int64_t head_dim, int64_t len_value);
+
+/*
+ * Backward of rfdetr_msda_forward against grad_output ([B, Lq, H*D], the output's dtype):
+ *   grad_value               [B*H, Lv, D]        value_dtype   (overwritten)
+ *   grad_sampling_locations  [B, Lq, H, L, P, 2] f32           (overwritten)
+ *   grad_attention_weights   [B, Lq, H, L*P]     weight_dtype  (overwritten)
+ * grad_value is accumulated in float32 and rounded once.  Non-finite sampling locations
+ * give NaN location/weight gradients and add nothing to grad_value.
+ */
+int rfdetr_msda_backward(void *stream,
+                         const void *value, int value_dtype,
+                         const int64_t *spatial_shapes, const int64_t *level_start_index,
+                         const float *sampling_locations,
+                         const void *attention_weights, int weight_dtype,
+                         const void *grad_output, int grad_output_dtype,
+                         void *grad_value, float *grad_sampling_locations,
+                         void *grad_attention_weights,
+                         void *workspace, size_t workspace_bytes,
+                         int64_t batch, int64_t n_heads, int64_t head_dim, int64_t len_query,
+                         int64_t n_levels, int64_t n_points);
+
+/* ---------------------------------------------------------------------------------------
+ * Two-stage query selection.
+ *
+ * Replaces, per row r of logits [R, N, C] (R = groups*batch):
+ *   proposal_scores = logits.max(-1)                         (transformer.py:695)
+ *   values, indices = jax.lax.top_k(proposal_scores, k)      (transformer.py:696)
+ * Descending IEEE totalOrder (NaN first), equal scores keep the lower index first.
+ * C == 1 selects directly over a [R, N] score tensor.
+ *   scores_out  [R, N] f32 or NULL;  values_out [R, k] f32 or NULL;  indices_out [R, k] int32.
+ * Limits: 1 <= k <= N <= 16384.
+ * ------------------------------------------------------------------------------------- */
+int rfdetr_topk_select(void *stream, const float *logits, int64_t rows, int64_t positions,
+                       int64_t classes, int64_t k, float *scores_out, float *values_out,
+                       int32_t *indices_out);
+
+/*
+ * select_rows(values, indices) -- src/rfdetr_jax/models/layers.py:225-244:
+ *   out[r, i, :] = values[r, indices[r, i], :]
+ *   values [R, N, W] (element_bytes each), indices [R, K] int32, out [R, K, W].
+ * An index outside [0, N) writes a zero row and sets *status_out (device int32, may be NULL)
+ * to RFDETR_ERR_SHAPE.
+ */
+int rfdetr_select_rows(void *stream, const void *values, int64_t element_bytes, int64_t rows,
+                       int64_t positions, int64_t width, const int32_t *indices, int64_t k,
+                       void *out, int32_t *status_out);
+
+/* ---------------------------------------------------------------------------------------
+ * Matching cost -- build_cost_matrix for classes and boxes, src/rfdetr_jax/models/matcher.py:44-103,141
+ * (focal cost :36-41, GIoU utilities/box_ops.py:27-75):
+ *   cost[b,q,t] = cost_bbox * |pb - tb|_1 + cost_class * focal(logit[b,q,label[b,t]])
+ *                 + cost_giou * (-GIoU(pb, tb)),   or 1e4 where target_mask[b,t] == 0.
+ *   pred_logits [B, Q, C] (f32 | bf16), pred_boxes [B, Q, 4] (f32 | bf16, cxcywh),
+ *   target_labels [B, T] int32, target_boxes [B, T, 4] f32, target_mask [B, T] uint8,
+ *   cost [B, Q, T] f32.  Labels outside [0, C) produce NaN costs.
+ * ------------------------------------------------------------------------------------- */
+int rfdetr_match_cost(void *stream, const void *pred_logits, int logits_dtype,
+                      const void *pred_boxes, int boxes_dtype, const int32_t *target_labels,
+                      const float *target_boxes, const uint8_t *target_mask, float *cost,
+                      int64_t batch, int64_t queries, int64_t classes, int64_t targets,
+                      float cost_class, float cost_bbox, float cost_giou, float focal_alpha);
+
+/*
+ * Batched exact assignment -- hungarian_match / _solve_batch, matcher.py:144-208, i.e.
+ * scipy.optimize.linear_sum_assignment on every block cost[n, g*Qg:(g+1)*Qg, :sizes[n]]
+ * (Qg = queries / group_detr), with SciPy's tie-breaking, in float64.
+ *   cost [N, Q, T] f32, sizes [N] int32 (device), outputs [N, G*T]:
+ *   rows int32 (global query index), cols int32, valid uint8; slots g*T.. in ascending row
+ *   order, unused slots 0/0/0.  Non-finite block entries are replaced by max(finite)+1
+ *   (matcher.py:169-172).  *status_out (device int32, required) is set to RFDETR_ERR_LIMIT
+ *   if a solve hits its iteration cap (never for finite costs) -- read it when convenient.
+ * Limits: queries % group_detr == 0, T <= 1024, Qg <= 4096.
+ */
+int rfdetr_lsap_batched(void *stream, const float *cost, const int32_t *sizes, int64_t problems,
+                        int64_t queries, int64_t max_targets, int64_t group_detr, int32_t *rows,
+                        int32_t *cols, uint8_t *valid, int32_t *status_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RFDETR_B200_H */

@@ -1,0 +1,31 @@
+"""B200-native (sm_100a) backend for RF-DETR-JAX's training hot path.
+
+The package directory is ``rf-detr-jax_b200``; it is imported as ``rfdetr_jax_b200``
+(``__graft_entry__.load_package()`` registers it under that name).
+
+Components (each a thin host wrapper over ``librfdetr_b200.so``, see ``include/rfdetr_b200.h``):
+
+* :mod:`.ops`     -- multi-scale deformable attention, sampler ``"cuda"``, forward + backward;
+* :mod:`.topk`    -- two-stage query selection (class max + top-k) and ``select_rows``;
+* :mod:`.matcher` -- matching cost and exact batched assignment (SciPy-identical).
+"""
+
+from . import _native
+from .matcher import CriterionConfig, build_cost_matrix, hungarian_match
+from .ops import MSDeformAttnFunction, ms_deform_attn, ms_deform_attn_core, ms_deform_attn_core_rows
+from .topk import select_rows, top_k, two_stage_topk
+
+__all__ = [
+    "CriterionConfig",
+    "MSDeformAttnFunction",
+    "build_cost_matrix",
+    "hungarian_match",
+    "ms_deform_attn",
+    "ms_deform_attn_core",
+    "ms_deform_attn_core_rows",
+    "select_rows",
+    "top_k",
+    "two_stage_topk",
+]
+
+LIB_PATH = _native.LIB_PATH

@@ -1,0 +1,479 @@
+// Matching cost and batched exact assignment for sm_100a.
+//
+// Cost: build_cost_matrix for classes and boxes (src/rfdetr_jax/models/matcher.py:44-103,141;
+// focal term :36-41; GIoU src/rfdetr_jax/utilities/box_ops.py:27-75).
+//
+// Assignment: hungarian_match / _solve_batch (matcher.py:144-208), which calls
+// scipy.optimize.linear_sum_assignment per (image, group) block.  SciPy solves with Crouse's
+// shortest augmenting path (IEEE TAES 52(4), 2016) in float64; this kernel runs the same method
+// with the same tie rules, so its answer is SciPy's bit for bit:
+//   * a tall block (more queries than targets, the usual case) is solved transposed and reported
+//     in ascending query order;
+//   * rows are inserted in index order; each insertion scans the unscanned columns through a
+//     work list that starts in descending column order and drops a column by moving the list's
+//     last entry into its slot;
+//   * reduced cost ((minVal + c) - u[i]) - v[j]; the next column has the smallest tentative
+//     distance, ties going to an unassigned column (the later one in the work list), else to the
+//     earliest one in the work list.
+// One CTA solves one block: the column scan of each augmenting step is spread over the CTA's
+// threads and the arg-min is a CTA reduction under that tie order.  The block's costs are staged
+// in shared memory when they fit the per-CTA budget, otherwise read from L2.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace rfdetr {
+namespace {
+
+// ------------------------------------------------------------------------------------------
+// Cost
+// ------------------------------------------------------------------------------------------
+constexpr int kCostThreads = 256;
+constexpr int kTargetFields = 10;  // label, mask, cx, cy, w, h, x0, y0, x1, y1
+
+template <typename T> __device__ __forceinline__ float ldf(const T *p) { return to_f32(__ldg(p)); }
+
+template <typename TL, typename TB>
+__global__ void __launch_bounds__(kCostThreads)
+match_cost_kernel(const TL *__restrict__ logits, const TB *__restrict__ boxes, const int32_t *__restrict__ labels,
+                  const float *__restrict__ tboxes, const uint8_t *__restrict__ tmask, float *__restrict__ cost,
+                  int Q, int C, int T, int q_tile, float cost_class, float cost_bbox, float cost_giou,
+                  float alpha) {
+    extern __shared__ float tsm[];  // [kTargetFields][T]
+    const int b = blockIdx.y;
+    const int q0 = blockIdx.x * q_tile;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float cx = __ldg(tboxes + ((size_t)b * T + t) * 4 + 0);
+        const float cy = __ldg(tboxes + ((size_t)b * T + t) * 4 + 1);
+        const float w = __ldg(tboxes + ((size_t)b * T + t) * 4 + 2);
+        const float h = __ldg(tboxes + ((size_t)b * T + t) * 4 + 3);
+        const float wc = fmaxf(w, 0.f), hc = fmaxf(h, 0.f);  // box_ops.py:30-31 clip
+        tsm[0 * T + t] = __int_as_float(__ldg(labels + (size_t)b * T + t));
+        tsm[1 * T + t] = __ldg(tmask + (size_t)b * T + t) ? 1.f : 0.f;
+        tsm[2 * T + t] = cx;
+        tsm[3 * T + t] = cy;
+        tsm[4 * T + t] = w;
+        tsm[5 * T + t] = h;
+        tsm[6 * T + t] = cx - 0.5f * wc;
+        tsm[7 * T + t] = cy - 0.5f * hc;
+        tsm[8 * T + t] = cx + 0.5f * wc;
+        tsm[9 * T + t] = cy + 0.5f * hc;
+    }
+    __syncthreads();
+    const int q1 = min(q0 + q_tile, Q);
+    const int n = (q1 - q0) * T;
+    const float qnan = __int_as_float(0x7fc00000);
+    for (int e = threadIdx.x; e < n; e += blockDim.x) {
+        const int qi = e / T;
+        const int t = e - qi * T;
+        const size_t qrow = (size_t)b * Q + q0 + qi;
+        float out;
+        if (tsm[1 * T + t] == 0.f) {
+            out = 1e4f;  // matcher.py:141
+        } else {
+            const int label = __float_as_int(tsm[0 * T + t]);
+            // Focal classification cost (matcher.py:36-41) on the target's own logit.
+            float cls = qnan;
+            if (label >= 0 && label < C) {
+                const float x = ldf(logits + qrow * C + label);
+                const float e_ = expf(-fabsf(x));
+                const float l1p = log1pf(e_);
+                const float sp_pos = fmaxf(x, 0.f) + l1p;   // -log_sigmoid(-x)
+                const float sp_neg = fmaxf(-x, 0.f) + l1p;  // -log_sigmoid(x)
+                const float inv = 1.f / (1.f + e_);
+                const float p = x >= 0.f ? inv : e_ * inv;      // sigmoid(x)
+                const float pm = x >= 0.f ? e_ * inv : inv;     // 1 - sigmoid(x)
+                const float negative = (1.f - alpha) * (p * p) * sp_pos;
+                const float positive = alpha * (pm * pm) * sp_neg;
+                cls = positive - negative;
+            }
+            const float pcx = ldf(boxes + qrow * 4 + 0), pcy = ldf(boxes + qrow * 4 + 1);
+            const float pw = ldf(boxes + qrow * 4 + 2), ph = ldf(boxes + qrow * 4 + 3);
+            const float l1 = ((fabsf(pcx - tsm[2 * T + t]) + fabsf(pcy - tsm[3 * T + t])) +
+                              fabsf(pw - tsm[4 * T + t])) + fabsf(ph - tsm[5 * T + t]);
+            // GIoU (box_ops.py:46-75) on xyxy boxes.
+            const float pwc = fmaxf(pw, 0.f), phc = fmaxf(ph, 0.f);
+            const float ax0 = pcx - 0.5f * pwc, ay0 = pcy - 0.5f * phc;
+            const float ax1 = pcx + 0.5f * pwc, ay1 = pcy + 0.5f * phc;
+            const float bx0 = tsm[6 * T + t], by0 = tsm[7 * T + t];
+            const float bx1 = tsm[8 * T + t], by1 = tsm[9 * T + t];
+            const float area1 = (ax1 - ax0) * (ay1 - ay0);
+            const float area2 = (bx1 - bx0) * (by1 - by0);
+            const float iw = fmaxf(fminf(ax1, bx1) - fmaxf(ax0, bx0), 0.f);
+            const float ih = fmaxf(fminf(ay1, by1) - fmaxf(ay0, by0), 0.f);
+            const float inter = iw * ih;
+            const float uni = area1 + area2 - inter;
+            const float iou = inter / fmaxf(uni, 1e-7f);
+            const float ew = fmaxf(fmaxf(ax1, bx1) - fminf(ax0, bx0), 0.f);
+            const float eh = fmaxf(fmaxf(ay1, by1) - fminf(ay0, by0), 0.f);
+            const float area = ew * eh;
+            const float giou = iou - (area - uni) / fmaxf(area, 1e-7f);
+            out = cost_bbox * l1 + cost_class * cls + cost_giou * (-giou);
+        }
+        cost[qrow * T + t] = out;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Assignment
+// ------------------------------------------------------------------------------------------
+constexpr int kLsapThreads = 128;
+constexpr int kLsapWarps = kLsapThreads / 32;
+constexpr int kLsapMaxTargets = 1024;
+constexpr int kLsapMaxGroup = 4096;
+
+struct Cand {
+    double d;
+    int k;     // position in the work list, -1 = none
+    int free;  // column unassigned
+};
+
+// True if a beats b under SciPy's selection order (see file comment).
+__device__ __forceinline__ bool beats(const Cand &a, const Cand &b) {
+    if (a.k < 0) return false;
+    if (b.k < 0) return true;
+    if (a.d < b.d) return true;
+    if (a.d > b.d) return false;
+    if (a.free != b.free) return a.free != 0;
+    return a.free ? (a.k > b.k) : (a.k < b.k);
+}
+
+__device__ __forceinline__ Cand shfl_cand(const Cand &c, int o) {
+    Cand r;
+    r.d = __shfl_xor_sync(0xffffffffu, c.d, o);
+    r.k = __shfl_xor_sync(0xffffffffu, c.k, o);
+    r.free = __shfl_xor_sync(0xffffffffu, c.free, o);
+    return r;
+}
+
+struct LsapArgs {
+    const float *cost;
+    const int32_t *sizes;
+    int Q, T, G, Qg;
+    int smem_cost_floats;  // capacity of the shared cost stage (0 = never stage)
+    int32_t *rows, *cols;
+    uint8_t *valid;
+    int32_t *status;
+};
+
+__global__ void __launch_bounds__(kLsapThreads) lsap_kernel(const LsapArgs a) {
+    extern __shared__ __align__(16) unsigned char sm[];
+    const int tid = threadIdx.x;
+    const int prob = blockIdx.x;
+    const int n = prob / a.G, g = prob - (prob / a.G) * a.G;
+    const int Qg = a.Qg, T = a.T;
+    const int start = g * Qg;
+    const size_t obase = ((size_t)n * a.G + g) * T;
+    for (int k = tid; k < T; k += kLsapThreads) {
+        a.rows[obase + k] = 0;
+        a.cols[obase + k] = 0;
+        a.valid[obase + k] = 0;
+    }
+    int size = __ldg(a.sizes + n);
+    size = max(0, min(size, T));
+    if (size == 0) return;
+
+    const bool tr = size < Qg;  // solve transposed: rows = targets, columns = queries
+    const int nr = tr ? size : Qg;
+    const int nc = tr ? Qg : size;
+    const int M = max(Qg, T);
+
+    double *u = reinterpret_cast<double *>(sm);
+    double *v = u + M;
+    double *dist = v + M;
+    int *path = reinterpret_cast<int *>(dist + M);
+    int *col4row = path + M;
+    int *row4col = col4row + M;
+    int *todo = row4col + M;
+    unsigned char *rseen = reinterpret_cast<unsigned char *>(todo + M);
+    unsigned char *cseen = rseen + M;
+    Cand *red = reinterpret_cast<Cand *>(cseen + ((2 * M + 15) & ~15) - M);
+    __shared__ int s_i, s_sink, s_left, s_fail;
+    __shared__ double s_minv;
+    __shared__ float s_sentinel;
+    float *csm = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(red) + kLsapWarps * sizeof(Cand) + 16);
+    csm = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(csm) + 15) & ~(uintptr_t)15);
+
+    // Stage the block (queries x real targets), find non-finite entries and the finite max.
+    const float *gblock = a.cost + ((size_t)n * a.Q + start) * T;
+    const bool staged = (long long)Qg * size <= (long long)a.smem_cost_floats;
+    float fmax_local = -INFINITY;
+    int bad_local = 0;
+    for (int e = tid; e < Qg * size; e += kLsapThreads) {
+        const int qi = e / size, ti = e - (e / size) * size;
+        const float c = __ldg(gblock + (size_t)qi * T + ti);
+        if (staged) csm[e] = c;
+        if (isfinite(c)) fmax_local = fmaxf(fmax_local, c);
+        else bad_local = 1;
+    }
+    const int any_bad = __syncthreads_or(bad_local);
+    float sentinel = 0.f;
+    if (any_bad) {
+        // matcher.py:169-172: non-finite entries become max(finite) + 1 (float32), or 1.
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) fmax_local = fmaxf(fmax_local, __shfl_xor_sync(0xffffffffu, fmax_local, o));
+        __shared__ float s_wmax[kLsapWarps];
+        if ((tid & 31) == 0) s_wmax[tid >> 5] = fmax_local;
+        __syncthreads();
+        if (tid == 0) {
+            float m = -INFINITY;
+            for (int w = 0; w < kLsapWarps; ++w) m = fmaxf(m, s_wmax[w]);
+            s_sentinel = (m == -INFINITY) ? 1.f : __fadd_rn(m, 1.f);
+        }
+        __syncthreads();
+        sentinel = s_sentinel;
+        if (staged) {
+            for (int e = tid; e < Qg * size; e += kLsapThreads)
+                if (!isfinite(csm[e])) csm[e] = sentinel;
+        }
+    }
+    // Solver-orientation cost C(i, j) as float64.
+    auto cost_at = [&](int i, int j) -> double {
+        const int qi = tr ? j : i, ti = tr ? i : j;
+        float c;
+        if (staged) {
+            c = csm[qi * size + ti];
+        } else {
+            c = __ldg(gblock + (size_t)qi * T + ti);
+            if (any_bad && !isfinite(c)) c = sentinel;
+        }
+        return (double)c;
+    };
+
+    for (int j = tid; j < nc; j += kLsapThreads) {
+        v[j] = 0.0;
+        row4col[j] = -1;
+        path[j] = -1;
+    }
+    for (int i = tid; i < nr; i += kLsapThreads) {
+        u[i] = 0.0;
+        col4row[i] = -1;
+    }
+    if (tid == 0) s_fail = 0;
+    __syncthreads();
+
+    for (int cur = 0; cur < nr; ++cur) {
+        for (int j = tid; j < nc; j += kLsapThreads) {
+            dist[j] = INFINITY;
+            cseen[j] = 0;
+            todo[j] = nc - 1 - j;
+        }
+        for (int i = tid; i < nr; i += kLsapThreads) rseen[i] = 0;
+        if (tid == 0) {
+            s_i = cur;
+            s_sink = -1;
+            s_left = nc;
+            s_minv = 0.0;
+        }
+        __syncthreads();
+
+        for (int step = 0; step <= nc; ++step) {  // each step retires one column
+            const int i = s_i;
+            const int left = s_left;
+            const double minv = s_minv;
+            if (tid == 0) rseen[i] = 1;
+            const double ui = u[i];
+            Cand best;
+            best.d = INFINITY;
+            best.k = -1;
+            best.free = 0;
+            for (int k = tid; k < left; k += kLsapThreads) {
+                const int j = todo[k];
+                const double r = __dsub_rn(__dsub_rn(__dadd_rn(minv, cost_at(i, j)), ui), v[j]);
+                double d = dist[j];
+                if (r < d) {
+                    path[j] = i;
+                    dist[j] = r;
+                    d = r;
+                }
+                Cand c;
+                c.d = d;
+                c.k = k;
+                c.free = row4col[j] == -1;
+                if (beats(c, best)) best = c;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const Cand other = shfl_cand(best, o);
+                if (beats(other, best)) best = other;
+            }
+            if ((tid & 31) == 0) red[tid >> 5] = best;
+            __syncthreads();
+            if (tid == 0) {
+                Cand b = red[0];
+                for (int w = 1; w < kLsapWarps; ++w)
+                    if (beats(red[w], b)) b = red[w];
+                if (b.k < 0 || b.d == INFINITY) {
+                    s_fail = 1;
+                } else {
+                    const int j = todo[b.k];
+                    if (row4col[j] == -1) s_sink = j;
+                    else s_i = row4col[j];
+                    cseen[j] = 1;
+                    todo[b.k] = todo[left - 1];
+                    s_left = left - 1;
+                    s_minv = b.d;
+                }
+            }
+            __syncthreads();
+            if (s_fail || s_sink != -1) break;
+        }
+        if (s_sink == -1) s_fail = 1;  // the scan cap was reached (cannot happen for finite costs)
+        if (s_fail) break;
+
+        const double minv = s_minv;
+        for (int r = tid; r < nr; r += kLsapThreads)
+            if (rseen[r] && r != cur) u[r] = __dadd_rn(u[r], __dsub_rn(minv, dist[col4row[r]]));
+        for (int c = tid; c < nc; c += kLsapThreads)
+            if (cseen[c]) v[c] = __dsub_rn(v[c], __dsub_rn(minv, dist[c]));
+        if (tid == 0) {
+            u[cur] = __dadd_rn(u[cur], minv);
+            int j = s_sink;
+            for (int hop = 0; hop <= nr; ++hop) {
+                const int r = path[j];
+                row4col[j] = r;
+                const int t = col4row[r];
+                col4row[r] = j;
+                j = t;
+                if (r == cur) break;
+                if (hop == nr) s_fail = 1;
+            }
+        }
+        __syncthreads();
+        if (s_fail) break;
+    }
+
+    if (s_fail) {
+        if (tid == 0) atomicExch(a.status, (int)RFDETR_ERR_LIMIT);
+        return;
+    }
+    if (!tr) {
+        for (int i = tid; i < nr; i += kLsapThreads) {
+            a.rows[obase + i] = start + i;
+            a.cols[obase + i] = col4row[i];
+            a.valid[obase + i] = 1;
+        }
+        return;
+    }
+    // Transposed: report the assigned queries in ascending order (a block-wide compaction).
+    __shared__ int s_warp_count[kLsapWarps];
+    __shared__ int s_base;
+    if (tid == 0) s_base = 0;
+    __syncthreads();
+    for (int j0 = 0; j0 < nc; j0 += kLsapThreads) {
+        const int j = j0 + tid;
+        const bool on = j < nc && row4col[j] >= 0;
+        const unsigned bal = __ballot_sync(0xffffffffu, on);
+        const int lane = tid & 31, w = tid >> 5;
+        if (lane == 0) s_warp_count[w] = __popc(bal);
+        __syncthreads();
+        int before = s_base;
+        for (int k = 0; k < w; ++k) before += s_warp_count[k];
+        if (on) {
+            const int slot = before + __popc(bal & ((1u << lane) - 1u));
+            a.rows[obase + slot] = start + j;
+            a.cols[obase + slot] = row4col[j];
+            a.valid[obase + slot] = 1;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int total = 0;
+            for (int k = 0; k < kLsapWarps; ++k) total += s_warp_count[k];
+            s_base += total;
+        }
+        __syncthreads();
+    }
+}
+
+size_t lsap_state_bytes(int M) {
+    size_t b = 3 * (size_t)M * sizeof(double) + 4 * (size_t)M * sizeof(int);
+    b += ((2 * (size_t)M + 15) & ~(size_t)15);
+    b += kLsapWarps * sizeof(Cand) + 32;
+    return (b + 15) & ~(size_t)15;
+}
+
+}  // namespace
+}  // namespace rfdetr
+
+using namespace rfdetr;
+
+extern "C" int rfdetr_match_cost(void *stream, const void *pred_logits, int logits_dtype, const void *pred_boxes,
+                                 int boxes_dtype, const int32_t *target_labels, const float *target_boxes,
+                                 const uint8_t *target_mask, float *cost, int64_t batch, int64_t queries,
+                                 int64_t classes, int64_t targets, float cost_class, float cost_bbox,
+                                 float cost_giou, float focal_alpha) {
+    if ((logits_dtype != RFDETR_F32 && logits_dtype != RFDETR_BF16) ||
+        (boxes_dtype != RFDETR_F32 && boxes_dtype != RFDETR_BF16))
+        return RFDETR_ERR_DTYPE;
+    if (batch < 0 || queries < 0 || classes <= 0 || targets < 0 || batch > 65535 ||
+        batch * queries * (classes > targets ? classes : targets) > (1LL << 31) || targets > 4096)
+        return RFDETR_ERR_SHAPE;
+    if (batch == 0 || queries == 0 || targets == 0) return RFDETR_OK;
+    if (!pred_logits || !pred_boxes || !target_labels || !target_boxes || !target_mask || !cost)
+        return RFDETR_ERR_SHAPE;
+    const int ls = dtype_size(logits_dtype), bs = dtype_size(boxes_dtype);
+    if (!aligned(pred_logits, ls) || !aligned(pred_boxes, bs) || !aligned(target_labels, 4) ||
+        !aligned(target_boxes, 4) || !aligned(cost, 4))
+        return RFDETR_ERR_ALIGN;
+    const int T = (int)targets;
+    const int q_tile = std::max(1, (int)std::min<long long>(queries, std::max<long long>(1, 4096 / T)));
+    dim3 grid((unsigned)ceil_div(queries, q_tile), (unsigned)batch);
+    const size_t smem = (size_t)kTargetFields * T * sizeof(float);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define RFDETR_COST_LAUNCH(TL, TB)                                                                        \
+    match_cost_kernel<TL, TB><<<grid, kCostThreads, smem, s>>>(                                           \
+        static_cast<const TL *>(pred_logits), static_cast<const TB *>(pred_boxes), target_labels,        \
+        target_boxes, target_mask, cost, (int)queries, (int)classes, T, q_tile, cost_class, cost_bbox,  \
+        cost_giou, focal_alpha)
+    if (logits_dtype == RFDETR_F32 && boxes_dtype == RFDETR_F32) RFDETR_COST_LAUNCH(float, float);
+    else if (logits_dtype == RFDETR_F32) RFDETR_COST_LAUNCH(float, bf16);
+    else if (boxes_dtype == RFDETR_F32) RFDETR_COST_LAUNCH(bf16, float);
+    else RFDETR_COST_LAUNCH(bf16, bf16);
+#undef RFDETR_COST_LAUNCH
+    return launch_status();
+}
+
+extern "C" int rfdetr_lsap_batched(void *stream, const float *cost, const int32_t *sizes, int64_t problems,
+                                   int64_t queries, int64_t max_targets, int64_t group_detr, int32_t *rows,
+                                   int32_t *cols, uint8_t *valid, int32_t *status_out) {
+    if (problems < 0 || queries <= 0 || max_targets <= 0 || group_detr <= 0 || queries % group_detr != 0 ||
+        max_targets > kLsapMaxTargets || queries / group_detr > kLsapMaxGroup ||
+        problems * group_detr > 2147483647LL || problems * queries * max_targets > (1LL << 40))
+        return RFDETR_ERR_SHAPE;
+    if (problems == 0) return RFDETR_OK;
+    if (!cost || !sizes || !rows || !cols || !valid || !status_out) return RFDETR_ERR_SHAPE;
+    if (!aligned(cost, 4) || !aligned(sizes, 4) || !aligned(rows, 4) || !aligned(cols, 4) ||
+        !aligned(status_out, 4))
+        return RFDETR_ERR_ALIGN;
+    LsapArgs a;
+    a.cost = cost;
+    a.sizes = sizes;
+    a.Q = (int)queries;
+    a.T = (int)max_targets;
+    a.G = (int)group_detr;
+    a.Qg = (int)(queries / group_detr);
+    a.rows = rows;
+    a.cols = cols;
+    a.valid = valid;
+    a.status = status_out;
+    const int M = std::max(a.Qg, a.T);
+    const size_t state = lsap_state_bytes(M);
+    // Stage costs in shared memory up to a budget that still lets two CTAs share an SM; larger
+    // blocks are read from L2.
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    size_t budget = 100 * 1024;
+    if (const char *e = getenv("RFDETR_LSAP_STAGE_KB")) budget = (size_t)atoi(e) * 1024;
+    const size_t want = (size_t)a.Qg * a.T * sizeof(float);
+    size_t stage = std::min(want, budget > state ? budget - state : 0);
+    if (state + stage > (size_t)optin) stage = (size_t)optin > state ? (size_t)optin - state : 0;
+    a.smem_cost_floats = (int)(stage / sizeof(float));
+    const size_t smem = state + stage;
+    if (smem > (size_t)optin) return RFDETR_ERR_SHAPE;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(lsap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return RFDETR_ERR_CUDA;
+    lsap_kernel<<<(unsigned)(problems * group_detr), kLsapThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    return launch_status();
+}

@@ -1,0 +1,116 @@
+"""Matching cost and exact batched assignment on B200.
+
+Mirrors ``src/rfdetr_jax/models/matcher.py`` and the solver switch of
+``src/rfdetr_jax/models/criterion.py:79-90``:
+
+* :func:`build_cost_matrix` -- the class/L1/GIoU cost with ``1e4`` on padded targets
+  (``matcher.py:44-103,141``);
+* :func:`hungarian_match` -- ``(cost [..., B, Q, T], sizes [B], group_detr) -> (rows, cols,
+  valid)`` each ``[..., B, group_detr * T]`` (``matcher.py:182-208``), solved on the device with
+  SciPy's algorithm and tie rules, so the assignment equals the reference's host solve;
+* :class:`CriterionConfig` -- ``solve`` dispatch with ``matcher="cuda"``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as N
+
+
+def build_cost_matrix(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, target_labels: torch.Tensor,
+                      target_boxes: torch.Tensor, target_mask: torch.Tensor, cost_class: float, cost_bbox: float,
+                      cost_giou: float, focal_alpha: float, **unsupported) -> torch.Tensor:
+    """``[B, Q, T]`` float32 matching cost (reference ``matcher.py:44-141``, boxes and classes).
+
+    Keypoint and mask cost terms (``matcher.py:105-138``) are not part of this backend; passing
+    them raises ``NotImplementedError``.
+    """
+    extra = {k: v for k, v in unsupported.items() if v is not None and v != () and v != (0.0, 0.0)
+             and v != (0.0, 0.0, 0.0, 0.0)}
+    if extra:
+        raise NotImplementedError(f"cost terms not implemented by the cuda backend: {sorted(extra)}")
+    N.require_cuda(pred_logits, pred_boxes, target_labels, target_boxes, target_mask)
+    batch, queries, classes = pred_logits.shape
+    targets = target_labels.shape[1]
+    if pred_boxes.shape != (batch, queries, 4) or target_boxes.shape != (batch, targets, 4) \
+            or target_mask.shape != (batch, targets):
+        raise ValueError("inconsistent shapes for build_cost_matrix")
+    cost = torch.empty((batch, queries, targets), dtype=torch.float32, device=pred_logits.device)
+    logits = pred_logits.contiguous()
+    boxes = pred_boxes.contiguous()
+    labels = target_labels.to(torch.int32).contiguous()
+    tboxes = target_boxes.to(torch.float32).contiguous()
+    mask = target_mask.to(torch.uint8).contiguous()
+    status = N.lib().rfdetr_match_cost(
+        N.stream_of(logits), N.ptr(logits), N.dtype_code(logits.dtype), N.ptr(boxes), N.dtype_code(boxes.dtype),
+        N.ptr(labels), N.ptr(tboxes), N.ptr(mask), N.ptr(cost), batch, queries, classes, targets,
+        float(cost_class), float(cost_bbox), float(cost_giou), float(focal_alpha))
+    N.check(status, "rfdetr_match_cost")
+    return cost
+
+
+def hungarian_match(cost: torch.Tensor, sizes: torch.Tensor, group_detr: int, check: bool = True):
+    """Exact assignment of every (layer, image, group) block in one launch.
+
+    Args:
+        cost: ``[..., B, Q, T]``; cast to float32 as the reference does (``matcher.py:203``).
+        sizes: real target count per image ``[B]``.
+        group_detr: number of query groups; must divide ``Q``.
+        check: read the device status flag after the launch (synchronises the stream).
+
+    Returns:
+        ``(rows int32, cols int32, valid bool)``, each ``[..., B, group_detr * T]``.
+    """
+    N.require_cuda(cost, sizes)
+    leading = cost.shape[:-3]
+    batch, queries, max_targets = cost.shape[-3:]
+    if group_detr < 1 or queries % group_detr:
+        raise ValueError("group_detr must be positive and divide the query count")
+    folded = cost.detach().to(torch.float32).reshape(-1, queries, max_targets).contiguous()
+    folded_sizes = torch.broadcast_to(sizes.to(torch.int32), (*leading, batch)).reshape(-1).contiguous()
+    problems = folded.shape[0]
+    slots = group_detr * max_targets
+    rows = torch.empty((problems, slots), dtype=torch.int32, device=cost.device)
+    cols = torch.empty((problems, slots), dtype=torch.int32, device=cost.device)
+    valid = torch.empty((problems, slots), dtype=torch.uint8, device=cost.device)
+    status_buf = torch.zeros((1,), dtype=torch.int32, device=cost.device)
+    status = N.lib().rfdetr_lsap_batched(N.stream_of(folded), N.ptr(folded), N.ptr(folded_sizes), problems, queries,
+                                         max_targets, group_detr, N.ptr(rows), N.ptr(cols), N.ptr(valid),
+                                         N.ptr(status_buf))
+    N.check(status, "rfdetr_lsap_batched")
+    if check:
+        N.check(int(status_buf.item()), "rfdetr_lsap_batched (device status)")
+    shape = (*leading, batch, slots)
+    return rows.reshape(shape), cols.reshape(shape), valid.to(torch.bool).reshape(shape)
+
+
+MATCHERS = ("cuda", "hungarian")
+
+
+@dataclass(frozen=True)
+class CriterionConfig:
+    """The solver switch of the reference's ``CriterionConfig`` (``criterion.py:37-90``).
+
+    ``matcher="cuda"`` (and ``"hungarian"``, the reference's exact matcher, which here runs on the
+    device with identical results) solve exactly on the GPU inside the step: no host round trip,
+    so it also works per shard under data parallelism.
+    """
+
+    focal_alpha: float = 0.25
+    group_detr: int = 13
+    set_cost_class: float = 2.0
+    set_cost_bbox: float = 5.0
+    set_cost_giou: float = 2.0
+    matcher: str = "cuda"
+
+    def solve(self, cost: torch.Tensor, sizes: torch.Tensor, group_detr: int):
+        if self.matcher in MATCHERS:
+            return hungarian_match(cost, sizes, group_detr)
+        raise ValueError(f"unknown matcher {self.matcher!r}; expected 'cuda' or 'hungarian'")
+
+    def cost(self, pred_logits, pred_boxes, target_labels, target_boxes, target_mask):
+        return build_cost_matrix(pred_logits, pred_boxes, target_labels, target_boxes, target_mask,
+                                 self.set_cost_class, self.set_cost_bbox, self.set_cost_giou, self.focal_alpha)

@@ -1,0 +1,149 @@
+"""Parity of the CUDA matching cost (fp32 tolerance) and batched assignment (bit-exact vs SciPy,
+the reference's own solver, on the same float32 cost)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import load_golden, match_inputs
+from oracle import matcher as OM
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+COST_RTOL = 1e-5  # fp32 cost vs the float64 oracle: |err| <= 1e-5 + 1e-5 |ref|
+COST_ATOL = 1e-5
+
+
+def _t(x, dtype=None):
+    t = torch.tensor(x, device=DEV)
+    return t.to(dtype) if dtype is not None else t
+
+
+def _match(pkg, cost, sizes, groups):
+    rows, cols, valid = pkg.hungarian_match(_t(cost), _t(sizes), groups)
+    return rows.cpu().numpy(), cols.cpu().numpy(), valid.cpu().numpy()
+
+
+def _assert_same(got, want):
+    for g, w, n in zip(got, want, ("rows", "cols", "valid"), strict=True):
+        np.testing.assert_array_equal(g, w, err_msg=n)
+
+
+def test_golden(pkg):
+    d = load_golden("match_c4_small")
+    cost = pkg.build_cost_matrix(_t(d["pred_logits"]), _t(d["pred_boxes"]), _t(d["target_labels"]),
+                                 _t(d["target_boxes"]), _t(d["target_mask"]), 2.0, 5.0, 2.0, 0.25)
+    np.testing.assert_allclose(cost.cpu().numpy(), d["cost"], rtol=COST_RTOL, atol=COST_ATOL)
+    _assert_same(_match(pkg, d["cost"], d["sizes"], int(d["groups"])), (d["rows"], d["cols"], d["valid"]))
+
+
+def test_config4_full_step(pkg):
+    """Config 4 at training shape: 3 stacked layers x 8 images x 13 groups x 300 queries, T=100."""
+    groups, per_group, classes, max_targets, batch = 13, 300, 91, 100, 8
+    layers = []
+    for layer in range(3):
+        logits, boxes, labels, tboxes, mask, sizes = match_inputs(
+            10, batch, groups * per_group, classes, max_targets)
+        logits = np.random.default_rng(100 + layer).standard_normal(logits.shape).astype(np.float32)
+        layers.append((logits, boxes))
+    costs_gpu = torch.stack([pkg.build_cost_matrix(_t(lg), _t(bx), _t(labels), _t(tboxes), _t(mask), 2.0, 5.0, 2.0,
+                                                   0.25) for lg, bx in layers])
+    costs_ref = np.stack([OM.build_cost_matrix(lg, bx, labels, tboxes, mask) for lg, bx in layers])
+    np.testing.assert_allclose(costs_gpu.cpu().numpy(), costs_ref, rtol=COST_RTOL, atol=COST_ATOL)
+    # Bit-exact assignment on the same cost bits (the kernel's own cost).
+    cost_np = costs_gpu.cpu().numpy()
+    got = _match(pkg, cost_np, sizes, groups)
+    want = OM.hungarian_match(cost_np, sizes, groups)
+    _assert_same(got, want)
+    # And the end-to-end pipeline against the oracle's pipeline.
+    want_e2e = OM.hungarian_match(costs_ref, sizes, groups)
+    _assert_same(got, want_e2e)
+
+
+@pytest.mark.parametrize("kind", ["normal", "integer", "constant", "columns", "rows"])
+def test_tie_heavy(pkg, kind):
+    rng = np.random.default_rng(["normal", "integer", "constant", "columns", "rows"].index(kind))
+    n, groups, per_group, max_targets = 6, 3, 40, 12
+    shape = (n, groups * per_group, max_targets)
+    if kind == "normal":
+        cost = rng.standard_normal(shape).astype(np.float32)
+    elif kind == "integer":
+        cost = rng.integers(0, 3, shape).astype(np.float32)
+    elif kind == "constant":
+        cost = np.ones(shape, np.float32)
+    elif kind == "columns":
+        cost = np.repeat(rng.standard_normal((n, groups * per_group, 1)), max_targets, -1).astype(np.float32)
+    else:
+        cost = np.repeat(rng.standard_normal((n, 1, max_targets)), groups * per_group, 1).astype(np.float32)
+    sizes = rng.integers(0, max_targets + 1, n).astype(np.int32)
+    sizes[0], sizes[1] = 0, max_targets
+    _assert_same(_match(pkg, cost, sizes, groups), OM.hungarian_match(cost, sizes, groups))
+
+
+def test_square_and_wide_blocks(pkg):
+    """size == per_group (no transpose) and size > per_group (more targets than queries)."""
+    rng = np.random.default_rng(11)
+    for per_group, max_targets, size in ((10, 10, 10), (8, 12, 12), (8, 12, 9), (1, 3, 3), (5, 5, 1)):
+        cost = rng.standard_normal((2, 2 * per_group, max_targets)).astype(np.float32)
+        sizes = np.array([size, max(0, size - 1)], np.int32)
+        _assert_same(_match(pkg, cost, sizes, 2), OM.hungarian_match(cost, sizes, 2))
+
+
+def test_non_finite_costs(pkg):
+    """NaN/inf entries are replaced by max(finite)+1 before solving (matcher.py:169-172)."""
+    rng = np.random.default_rng(12)
+    cost = rng.standard_normal((4, 60, 9)).astype(np.float32)
+    cost[0, 3, 2] = np.nan
+    cost[1, :, 0] = np.inf
+    cost[2, 10, :] = -np.inf
+    cost[3, :30, :] = np.nan  # a whole block non-finite -> sentinel 1
+    sizes = np.array([9, 5, 9, 7], np.int32)
+    _assert_same(_match(pkg, cost, sizes, 2), OM.hungarian_match(cost, sizes, 2))
+
+
+def test_reference_matcher_cases(pkg):
+    """Restated reference tests: hand-solved 3x2 (test_matcher.py:103-111), folded leading axes
+    (:89-100), padded sentinel columns, groups independent and empty images
+    (test_criterion.py:67-106)."""
+    cost = np.array([[[[4.0, 1.0], [2.0, 3.0], [9.0, 9.0]]]], np.float32)
+    rows, cols, valid = _match(pkg, cost, np.array([2], np.int32), 1)
+    assert sorted(zip(rows[0, 0][valid[0, 0]].tolist(), cols[0, 0][valid[0, 0]].tolist())) == [(0, 1), (1, 0)]
+
+    rng = np.random.default_rng(3)
+    stacked = rng.standard_normal((3, 2, 30, 4)).astype(np.float32) * 3
+    stacked[..., 3:] = 1e4
+    sizes = np.array([3, 3], np.int32)
+    folded = _match(pkg, stacked, sizes, 2)
+    for layer in range(3):
+        alone = _match(pkg, stacked[layer], sizes, 2)
+        for f, a in zip(folded, alone, strict=True):
+            np.testing.assert_array_equal(f[layer], a)
+
+    logits, boxes, labels, tboxes, mask, sizes = match_inputs(1, 2, 20, 7, 4, sizes=[3, 1])
+    cost = pkg.build_cost_matrix(_t(logits), _t(boxes), _t(labels), _t(tboxes), _t(mask), 2.0, 5.0, 2.0, 0.25)
+    rows, cols, valid = (x.cpu().numpy() for x in pkg.hungarian_match(cost, _t(sizes), 4))
+    assert valid.sum(1).tolist() == [3 * 4, 1 * 4]
+    empty = np.zeros((1, 8, 3), np.float32)
+    rows, cols, valid = _match(pkg, empty, np.array([0], np.int32), 1)
+    assert not valid.any() and not rows.any() and not cols.any()
+
+
+def test_cost_dtypes_and_errors(pkg):
+    logits, boxes, labels, tboxes, mask, _ = match_inputs(2, 2, 50, 91, 10)
+    ref = OM.build_cost_matrix(logits.astype(np.float32), boxes, labels, tboxes, mask)
+    bl = torch.tensor(logits, device=DEV).bfloat16()
+    got = pkg.build_cost_matrix(bl, _t(boxes), _t(labels), _t(tboxes), _t(mask), 2.0, 5.0, 2.0, 0.25)
+    ref_bf = OM.build_cost_matrix(bl.float().cpu().numpy(), boxes, labels, tboxes, mask)
+    np.testing.assert_allclose(got.cpu().numpy(), ref_bf, rtol=COST_RTOL, atol=COST_ATOL)
+    assert np.abs(got.cpu().numpy() - ref).max() < 0.1
+    with pytest.raises(NotImplementedError):
+        pkg.build_cost_matrix(_t(logits), _t(boxes), _t(labels), _t(tboxes), _t(mask), 2.0, 5.0, 2.0, 0.25,
+                              pred_masks=_t(logits))
+    with pytest.raises(ValueError, match="divide"):
+        pkg.hungarian_match(_t(np.zeros((1, 10, 3), np.float32)), _t(np.array([1], np.int32)), 3)
+    cfg = pkg.CriterionConfig(matcher="auction")
+    with pytest.raises(ValueError, match="unknown matcher"):
+        cfg.solve(_t(np.zeros((1, 10, 3), np.float32)), _t(np.array([1], np.int32)), 1)

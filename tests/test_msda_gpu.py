@@ -1,0 +1,225 @@
+"""Parity of the CUDA sampler (forward and backward) against the CPU oracle and the goldens.
+
+Tolerances (the parity contract): fp32 outputs and gradients elementwise within
+1e-5 relative + 1e-6 absolute; bf16 within 2e-2 relative (max error against the tensor's scale
+and relative L2).  All calls go through the library's C ABI via the package's host wrappers.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_bf16_close, assert_fp32_close, load_golden, sampler_inputs
+from oracle import msda as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _run(pkg, value, shapes, loc, attn, grad, dtype):
+    """Forward + backward through the public API (autograd)."""
+    v = torch.tensor(value, device=DEV).to(dtype).requires_grad_(True)
+    l = torch.tensor(loc, device=DEV).requires_grad_(True)
+    a = torch.tensor(attn, device=DEV).to(dtype).requires_grad_(True)
+    out = pkg.ms_deform_attn_core_rows(v, shapes, l, a, "cuda")
+    out.backward(torch.tensor(grad, device=DEV).to(out.dtype))
+    torch.cuda.synchronize()
+    f = lambda t: t.detach().float().cpu().numpy()  # noqa: E731
+    return f(out), f(v.grad), f(l.grad), f(a.grad)
+
+
+def _check(got, want, bf16, tag):
+    names = ("out", "grad_value", "grad_loc", "grad_attn")
+    for g, w, n in zip(got, want, names, strict=True):
+        if bf16:
+            assert_bf16_close(g, w, f"{tag}:{n}")
+        else:
+            assert_fp32_close(g, w, f"{tag}:{n}")
+
+
+@pytest.mark.parametrize("name", ["msda_c1", "msda_c2_small", "msda_c3_small", "msda_edge"])
+def test_goldens(pkg, name):
+    d = load_golden(name)
+    bf16 = bool(d["bf16"])
+    got = _run(pkg, d["value"], d["shapes"], d["loc"], d["attn"], d["grad"], torch.bfloat16 if bf16 else torch.float32)
+    _check(got, (d["out"], d["grad_value"], d["grad_loc"], d["grad_attn"]), bf16, name)
+
+
+def test_config1_known_answers(pkg):
+    """The reference's known-answer tests (tests/test_ops.py:22-54) through the CUDA path."""
+    def core(value, shapes, loc, attn):
+        return pkg.ms_deform_attn_core_rows(torch.tensor(value, device=DEV), shapes, torch.tensor(loc, device=DEV),
+                                            torch.tensor(attn, device=DEV)).cpu().numpy()
+
+    v = np.array([[[1.0], [2.0], [3.0], [4.0]]], np.float32)
+    loc = np.array([0.25, 0.25, 0.75, 0.75], np.float32).reshape(1, 1, 1, 1, 2, 2)
+    assert core(v, ((2, 2),), loc, np.array([[[[1.0, 0.0]]]], np.float32))[0, 0, 0] == pytest.approx(1.0)
+    assert core(v, ((2, 2),), loc, np.array([[[[0.0, 1.0]]]], np.float32))[0, 0, 0] == pytest.approx(4.0)
+    far = np.full((1, 1, 1, 1, 1, 2), 3.0, np.float32)
+    assert core(np.ones((1, 4, 1), np.float32), ((2, 2),), far, np.ones((1, 1, 1, 1), np.float32))[0, 0, 0] == 0.0
+    mid = np.full((1, 1, 1, 1, 1, 2), 0.5, np.float32)
+    assert core(np.array([[[0.0], [4.0]]], np.float32), ((1, 2),), mid,
+                np.ones((1, 1, 1, 1), np.float32))[0, 0, 0] == pytest.approx(2.0)
+    mean = core(np.arange(4, dtype=np.float32).reshape(1, 4, 1), ((2, 2),),
+                np.array([[[[[[0.25, 0.25], [0.75, 0.75]]]]]], np.float32), np.full((1, 1, 1, 2), 0.5, np.float32))
+    assert mean[0, 0, 0] == pytest.approx(1.5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_reference_pallas_case(pkg, dtype):
+    """The reference's cross-sampler case (tests/test_ops.py:225-248): 2 levels, loc U(-0.1, 1.1)."""
+    rng = np.random.default_rng(3)
+    batch, queries, heads, levels, points, dim = 2, 70, 2, 2, 3, 8
+    shapes = ((8, 16), (4, 8))
+    total = sum(h * w for h, w in shapes)
+    value = rng.standard_normal((batch * heads, total, dim)).astype(np.float32)
+    loc = rng.uniform(-0.1, 1.1, (batch, queries, heads, levels, points, 2)).astype(np.float32)
+    attn = rng.uniform(0, 1, (batch, queries, heads, levels * points)).astype(np.float32)
+    grad = rng.standard_normal((batch, queries, heads * dim)).astype(np.float32)
+    bf16 = dtype == torch.bfloat16
+    if bf16:
+        value, attn, grad = O.bf16_round(value), O.bf16_round(attn), O.bf16_round(grad)
+    want = (O.ms_deform_attn_forward(value, shapes, loc, attn),) + O.ms_deform_attn_backward(
+        value, shapes, loc, attn, grad)
+    _check(_run(pkg, value, shapes, loc, attn, grad, dtype), want, bf16, f"pallas-case-{dtype}")
+
+
+@pytest.mark.parametrize(
+    ("cfg", "dtype"),
+    [("c2", torch.bfloat16), ("c3", torch.float32), ("c3", torch.bfloat16), ("c1", torch.float32)],
+)
+def test_full_config_parity(pkg, cfg, dtype):
+    """Configs 1-3 at their benchmark sizes against the float64 oracle."""
+    if cfg == "c1":
+        args = dict(seed=0, batch=2, len_query=300, heads=16, shapes=((24, 24),), points=2, dim=16)
+    elif cfg == "c2":
+        args = dict(seed=1, batch=8, len_query=3900, heads=16, shapes=((24, 24),), points=2, dim=16, lo=-0.05,
+                    hi=1.05)
+    else:
+        args = dict(seed=2, batch=4, len_query=900, heads=8, shapes=((80, 80), (40, 40), (20, 20), (10, 10)),
+                    points=4, dim=32, sigma=2.0)
+    value, loc, attn, grad = sampler_inputs(**args)
+    bf16 = dtype == torch.bfloat16
+    if bf16:
+        value, attn, grad = O.bf16_round(value), O.bf16_round(attn), O.bf16_round(grad)
+    shapes = args["shapes"]
+    want = (O.ms_deform_attn_forward(value, shapes, loc, attn),) + O.ms_deform_attn_backward(
+        value, shapes, loc, attn, grad)
+    got = _run(pkg, value, shapes, loc, attn, grad, dtype)
+    _check(got, want, bf16, f"{cfg}-{dtype}")
+    if bf16:
+        # Tighter than the contract: float32 internals leave only the final bf16 rounding.
+        for g, w, n in zip(got, want, ("out", "grad_value", "grad_loc", "grad_attn"), strict=True):
+            rel = np.linalg.norm(g - w) / np.linalg.norm(w)
+            assert rel < 6e-3, f"{cfg}:{n} relative L2 {rel:.2e}"
+
+
+def test_adjoint_identity_full_size(pkg):
+    """Size-independent property at config 2: the sampler is linear in value and in the weights,
+    so <g, f(v, a)> = <dL/dv, v> = <dL/da, a> for L = <g, f>."""
+    value, loc, attn, grad = sampler_inputs(1, 8, 3900, 16, ((24, 24),), 2, 16, lo=-0.05, hi=1.05)
+    v = torch.tensor(value, device=DEV, requires_grad=True)
+    a = torch.tensor(attn, device=DEV, requires_grad=True)
+    l = torch.tensor(loc, device=DEV)
+    g = torch.tensor(grad, device=DEV)
+    out = pkg.ms_deform_attn_core_rows(v, ((24, 24),), l, a)
+    out.backward(g)
+    lhs = float((out.detach().double() * g.double()).sum())
+    via_v = float((v.grad.double() * v.detach().double()).sum())
+    via_a = float((a.grad.double() * a.detach().double()).sum())
+    assert via_v == pytest.approx(lhs, rel=1e-5)
+    assert via_a == pytest.approx(lhs, rel=1e-5)
+
+
+def test_non_finite_locations(pkg):
+    value, loc, attn, grad = sampler_inputs(4, 1, 6, 2, ((4, 5),), 2, 8)
+    loc[0, 1, 0, 0, 0, 0] = np.nan
+    loc[0, 3, 1, 0, 1, 1] = np.inf
+    got = _run(pkg, value, ((4, 5),), loc, attn, grad, torch.float32)
+    want = (O.ms_deform_attn_forward(value, ((4, 5),), loc, attn),) + O.ms_deform_attn_backward(
+        value, ((4, 5),), loc, attn, grad)
+    for g, w in zip(got, want, strict=True):
+        np.testing.assert_array_equal(np.isnan(g), np.isnan(w))
+        finite = ~np.isnan(w)
+        assert_fp32_close(g[finite], w[finite])
+
+
+def test_integer_pixel_positions(pkg):
+    """Locations exactly on pixel centres / edges (floor decisions and one-sided gradients)."""
+    value, _, attn, grad = sampler_inputs(6, 1, 64, 2, ((6, 6),), 2, 8)
+    rng = np.random.default_rng(6)
+    # loc = (k + 0.5) / W puts ix exactly on integer k; include -0.5 and W-0.5 edges.
+    k = rng.integers(-1, 7, (1, 64, 2, 1, 2, 2)).astype(np.float32)
+    loc = ((k + np.float32(0.5)) / np.float32(6)).astype(np.float32)
+    got = _run(pkg, value, ((6, 6),), loc, attn, grad, torch.float32)
+    want = (O.ms_deform_attn_forward(value, ((6, 6),), loc, attn),) + O.ms_deform_attn_backward(
+        value, ((6, 6),), loc, attn, grad)
+    _check(got, want, False, "integer-positions")
+
+
+@pytest.mark.parametrize("dim", [1, 2, 3, 4, 24, 64])
+def test_head_dims(pkg, dim):
+    shapes = ((7, 5), (3, 4))
+    value, loc, attn, grad = sampler_inputs(dim, 2, 13, 3, shapes, 2, dim, lo=-0.2, hi=1.2)
+    want = (O.ms_deform_attn_forward(value, shapes, loc, attn),) + O.ms_deform_attn_backward(
+        value, shapes, loc, attn, grad)
+    _check(_run(pkg, value, shapes, loc, attn, grad, torch.float32), want, False, f"dim{dim}")
+
+
+def test_mixed_dtypes(pkg):
+    """bf16 value with fp32 weights gives fp32 output (result_type, ops.py:260)."""
+    shapes = ((9, 9),)
+    value, loc, attn, grad = sampler_inputs(8, 2, 40, 4, shapes, 2, 16)
+    value = O.bf16_round(value)
+    v = torch.tensor(value, device=DEV).bfloat16().requires_grad_(True)
+    a = torch.tensor(attn, device=DEV).requires_grad_(True)
+    l = torch.tensor(loc, device=DEV).requires_grad_(True)
+    out = pkg.ms_deform_attn_core_rows(v, shapes, l, a)
+    assert out.dtype == torch.float32
+    out.backward(torch.tensor(grad, device=DEV))
+    want_out = O.ms_deform_attn_forward(value, shapes, loc, attn)
+    gv, gl, ga = O.ms_deform_attn_backward(value, shapes, loc, attn, grad)
+    assert_fp32_close(out.detach().cpu().numpy(), want_out, "mixed:out", rtol=1e-5, atol=1e-5)
+    assert v.grad.dtype == torch.bfloat16 and a.grad.dtype == torch.float32
+    assert_bf16_close(v.grad.float().cpu().numpy(), gv, "mixed:grad_value")
+    assert_fp32_close(a.grad.cpu().numpy(), ga, "mixed:grad_attn", rtol=1e-5, atol=1e-5)
+    assert_fp32_close(l.grad.cpu().numpy(), gl, "mixed:grad_loc", rtol=1e-5, atol=1e-5)
+
+
+def test_unaligned_views_and_entry_points(pkg):
+    """Offset (unaligned) value storage, the [B, H, D, Lv] entry point and the drop-in signature."""
+    shapes = ((6, 7), (3, 3))
+    value, loc, attn, _ = sampler_inputs(9, 2, 11, 2, shapes, 3, 8)
+    want = O.ms_deform_attn_forward(value, shapes, loc, attn)
+    store = torch.zeros(value.size + 1, device=DEV)
+    store[1:] = torch.tensor(value.ravel(), device=DEV)
+    v = store[1:].view(value.shape)  # 4-byte aligned only
+    out = pkg.ms_deform_attn_core_rows(v, shapes, torch.tensor(loc, device=DEV), torch.tensor(attn, device=DEV))
+    assert_fp32_close(out.cpu().numpy(), want, "unaligned")
+    nchw = torch.tensor(value, device=DEV).view(2, 2, -1, 8).permute(0, 1, 3, 2)
+    out2 = pkg.ms_deform_attn_core(nchw, shapes, torch.tensor(loc, device=DEV), torch.tensor(attn, device=DEV))
+    assert_fp32_close(out2.cpu().numpy(), want, "core")
+    out3 = pkg.ms_deform_attn(torch.tensor(value, device=DEV), torch.tensor(shapes), torch.tensor([0, 42]),
+                              torch.tensor(loc, device=DEV), torch.tensor(attn, device=DEV))
+    assert_fp32_close(out3.cpu().numpy(), want, "drop-in")
+    with pytest.raises(ValueError, match="level_start_index"):
+        pkg.ms_deform_attn(torch.tensor(value, device=DEV), shapes, [0, 41], torch.tensor(loc, device=DEV),
+                           torch.tensor(attn, device=DEV))
+
+
+def test_error_behaviour(pkg):
+    value, loc, attn, _ = sampler_inputs(0, 1, 4, 2, ((3, 3),), 1, 4)
+    v, l, a = (torch.tensor(x, device=DEV) for x in (value, loc, attn))
+    with pytest.raises(ValueError, match="unknown sampler"):
+        pkg.ms_deform_attn_core_rows(v, ((3, 3),), l, a, "gather")
+    with pytest.raises(ValueError):
+        pkg.ms_deform_attn_core_rows(v[:, :8], ((3, 3),), l, a)
+    with pytest.raises(ValueError):
+        pkg.ms_deform_attn_core_rows(v, ((3, 3),), l.double(), a)
+    with pytest.raises(ValueError):
+        pkg.ms_deform_attn_core_rows(v.half(), ((3, 3),), l, a.half())
+    empty = pkg.ms_deform_attn_core_rows(v, ((3, 3),), l[:, :0], a[:, :0])
+    assert empty.shape == (1, 0, 8)

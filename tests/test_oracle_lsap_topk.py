@@ -1,0 +1,129 @@
+"""Pins the CPU matcher and selection oracles (CPU only).
+
+* ``oracle/lsap.c`` (the restatement of SciPy's solver) must agree bit-for-bit with SciPy --
+  the reference's own solver (``matcher.py:173``) -- on random and tie-heavy matrices, tall, wide
+  and square.
+* ``oracle.matcher.solve_batch`` must reproduce the reference's slot layout and its tests
+  (``tests/test_matcher.py``, ``tests/test_criterion.py:67-106``).
+* ``oracle.topk`` must follow ``jax.lax.top_k``'s contract and the committed goldens.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+from scipy.optimize import linear_sum_assignment
+
+from helpers import load_golden, match_inputs
+from oracle import matcher as OM
+from oracle import topk as OT
+
+
+@pytest.mark.parametrize("kind", ["normal", "integer", "constant", "repeated_rows", "repeated_cols"])
+def test_c_restatement_is_bit_exact_with_scipy(kind):
+    rng = np.random.default_rng(["normal", "integer", "constant", "repeated_rows", "repeated_cols"].index(kind))
+    for _ in range(300):
+        nr, nc = int(rng.integers(1, 45)), int(rng.integers(1, 45))
+        if kind == "normal":
+            c = rng.standard_normal((nr, nc)).astype(np.float32)
+        elif kind == "integer":
+            c = rng.integers(0, 4, (nr, nc)).astype(np.float32)
+        elif kind == "constant":
+            c = np.full((nr, nc), 2.5, np.float32)
+        elif kind == "repeated_rows":
+            c = np.repeat(rng.standard_normal((1, nc)), nr, 0).astype(np.float32)
+        else:
+            c = np.repeat(rng.standard_normal((nr, 1)), nc, 1).astype(np.float32)
+        r1, c1 = linear_sum_assignment(c)
+        r2, c2 = OM.lsap_c(c)
+        np.testing.assert_array_equal(r1, r2)
+        np.testing.assert_array_equal(c1, c2)
+
+
+def test_c_restatement_on_config4_blocks():
+    logits, boxes, labels, tboxes, mask, sizes = match_inputs(3, 2, 600, 91, 100)
+    cost = OM.build_cost_matrix(logits, boxes, labels, tboxes, mask)
+    a = OM.hungarian_match(cost, sizes, 2, solver=OM.lsap_scipy)
+    b = OM.hungarian_match(cost, sizes, 2, solver=OM.lsap_c)
+    for x, y in zip(a, b, strict=True):
+        np.testing.assert_array_equal(x, y)
+
+
+def test_solve_batch_reference_cases():
+    # Hand-solved 3x2 (reference tests/test_matcher.py:103-111).
+    rows, cols, valid = OM.hungarian_match(np.array([[[[4.0, 1.0], [2.0, 3.0], [9.0, 9.0]]]], np.float32),
+                                           np.array([2]), 1)
+    assert sorted(zip(rows[0, 0][valid[0, 0]].tolist(), cols[0, 0][valid[0, 0]].tolist())) == [(0, 1), (1, 0)]
+    # Each target matched once; groups independent; empty image (tests/test_criterion.py:67-106).
+    logits, boxes, labels, tboxes, mask, sizes = match_inputs(1, 2, 20, 7, 4, sizes=[3, 1])
+    cost = OM.build_cost_matrix(logits, boxes, labels, tboxes, mask)
+    rows, cols, valid = OM.hungarian_match(cost, sizes, 1)
+    for image, size in enumerate(sizes):
+        assert valid[image].sum() == size
+        assert len(set(rows[image][valid[image]].tolist())) == size
+        assert sorted(cols[image][valid[image]].tolist()) == list(range(size))
+    _, _, valid = OM.hungarian_match(cost, sizes, 4)
+    assert valid.sum(1).tolist() == [12, 4]
+    _, _, valid = OM.hungarian_match(np.zeros((1, 8, 3), np.float32), np.array([0]), 1)
+    assert not valid.any()
+
+
+def test_sanitize_matches_reference_rule():
+    block = np.array([[1.0, np.nan], [np.inf, -2.0]], np.float32)
+    out = OM.sanitize_block(block)
+    np.testing.assert_array_equal(out, np.array([[1.0, 2.0], [2.0, -2.0]], np.float32))
+    np.testing.assert_array_equal(OM.sanitize_block(np.full((2, 2), np.nan, np.float32)), np.ones((2, 2)))
+
+
+def test_cost_matches_a_torch_restatement():
+    """The float64 cost oracle against an independent torch float64 evaluation of the same terms."""
+    import torch
+
+    logits, boxes, labels, tboxes, mask, _ = match_inputs(4, 2, 50, 91, 12)
+    cost = OM.build_cost_matrix(logits, boxes, labels, tboxes, mask)
+    lg = torch.tensor(logits, dtype=torch.float64)
+    gathered = torch.gather(lg, 2, torch.tensor(labels, dtype=torch.int64)[:, None, :].expand(-1, 50, -1))
+    p = torch.sigmoid(gathered)
+    focal = 0.25 * (1 - p) ** 2 * -torch.nn.functional.logsigmoid(gathered) \
+        - 0.75 * p ** 2 * -torch.nn.functional.logsigmoid(-gathered)
+    pb, tb = torch.tensor(boxes, dtype=torch.float64), torch.tensor(tboxes, dtype=torch.float64)
+    l1 = (pb[:, :, None] - tb[:, None]).abs().sum(-1)
+
+    def xyxy(b):
+        cx, cy, w, h = b.unbind(-1)
+        w, h = w.clamp(min=0), h.clamp(min=0)
+        return torch.stack([cx - w / 2, cy - h / 2, cx + w / 2, cy + h / 2], -1)
+
+    a, b = xyxy(pb)[:, :, None], xyxy(tb)[:, None]
+    inter = ((torch.minimum(a[..., 2:], b[..., 2:]) - torch.maximum(a[..., :2], b[..., :2])).clamp(min=0)).prod(-1)
+    area = lambda x: (x[..., 2] - x[..., 0]) * (x[..., 3] - x[..., 1])  # noqa: E731
+    union = area(a) + area(b) - inter
+    hull = ((torch.maximum(a[..., 2:], b[..., 2:]) - torch.minimum(a[..., :2], b[..., :2])).clamp(min=0)).prod(-1)
+    giou = inter / union.clamp(min=1e-7) - (hull - union) / hull.clamp(min=1e-7)
+    want = torch.where(torch.tensor(mask)[:, None, :], 5 * l1 + 2 * focal - 2 * giou, torch.tensor(1e4,
+                                                                                                   dtype=torch.float64))
+    np.testing.assert_allclose(cost, want.numpy().astype(np.float32), rtol=1e-6, atol=1e-6)
+
+
+def test_topk_contract():
+    scores = np.array([[5.0, 4.0, 4.0, 1.0, 0.5, 0.1]], np.float32)
+    values, idx = OT.top_k(scores, 3)
+    np.testing.assert_array_equal(idx, [[0, 1, 2]])
+    row = np.array([[1.0, np.nan, -np.inf, -0.0, 0.0, np.inf]], np.float32)
+    _, idx = OT.top_k(row, 6)
+    np.testing.assert_array_equal(idx, [[1, 5, 0, 4, 3, 2]])
+    with pytest.raises(ValueError):
+        OT.top_k(scores, 7)
+
+
+def test_goldens_reproduce():
+    d = load_golden("topk_c4_small")
+    s, v, i = OT.two_stage_select(d["logits"], 300)
+    np.testing.assert_array_equal(i, d["indices"])
+    m = load_golden("match_c4_small")
+    cost = OM.build_cost_matrix(m["pred_logits"], m["pred_boxes"], m["target_labels"], m["target_boxes"],
+                                m["target_mask"])
+    np.testing.assert_array_equal(cost, m["cost"])
+    rows, cols, valid = OM.hungarian_match(m["cost"], m["sizes"], int(m["groups"]), solver=OM.lsap_c)
+    np.testing.assert_array_equal(rows, m["rows"])
+    np.testing.assert_array_equal(cols, m["cols"])

@@ -1,0 +1,148 @@
+"""Pins the CPU sampler oracle (CPU only).
+
+Two independent anchors:
+
+* the reference's own known-answer tests, restated (``tests/test_ops.py:22-54`` of the
+  reference): pixel centres read exactly, out-of-bounds reads zero, midpoint interpolation,
+  and the core's mean over uniformly weighted points;
+* ``torch.nn.functional.grid_sample(bilinear, zeros, align_corners=False)`` -- the upstream op
+  the reference's sampler reimplements (``ops.py:14-16``) -- forward and autograd backward,
+  in float64.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import msda as O
+
+
+def _torch_msda(value, shapes, loc, attn):
+    """Upstream-style MSDA built from ``grid_sample`` (float64 autograd reference)."""
+    batch, len_query, heads, levels, points, _ = loc.shape
+    n, _, dim = value.shape
+    samples = []
+    start = 0
+    for level, (h, w) in enumerate(shapes):
+        v = value[:, start:start + h * w].transpose(1, 2).reshape(n, dim, h, w)
+        grid = (2 * loc[:, :, :, level] - 1).permute(0, 2, 1, 3, 4).reshape(n, len_query, points, 2)
+        samples.append(torch.nn.functional.grid_sample(v, grid, mode="bilinear", padding_mode="zeros",
+                                                       align_corners=False))
+        start += h * w
+    sampled = torch.stack(samples, dim=-2).flatten(-2)  # [N, D, Lq, L*P]
+    weights = attn.permute(0, 2, 1, 3).reshape(n, 1, len_query, levels * points)
+    out = (sampled * weights).sum(-1)  # [N, D, Lq]
+    return out.view(batch, heads, dim, len_query).permute(0, 3, 1, 2).reshape(batch, len_query, heads * dim)
+
+
+def _case(seed, batch, len_query, heads, shapes, points, dim, lo=-0.1, hi=1.1):
+    rng = np.random.default_rng(seed)
+    total = sum(h * w for h, w in shapes)
+    value = rng.standard_normal((batch * heads, total, dim)).astype(np.float32)
+    loc = rng.uniform(lo, hi, (batch, len_query, heads, len(shapes), points, 2)).astype(np.float32)
+    attn = rng.uniform(0, 1, (batch, len_query, heads, len(shapes) * points)).astype(np.float32)
+    grad = rng.standard_normal((batch, len_query, heads * dim)).astype(np.float32)
+    return value, loc, attn, grad
+
+
+def test_reads_pixel_centres():
+    """Reference ``test_ops.py:22-29``: a sample at a pixel centre returns that pixel."""
+    value = np.array([[[1.0], [2.0], [3.0], [4.0]]], np.float32)  # 2x2 map, one channel
+    # grid -0.5/+0.5 on a 2-wide axis are the centres; loc = (grid + 1) / 2.
+    loc = np.array([0.25, 0.25, 0.75, 0.75], np.float32).reshape(1, 1, 1, 1, 2, 2)
+    out = O.ms_deform_attn_forward(value, ((2, 2),), loc, np.array([[[[1.0, 0.0]]]], np.float32))
+    assert out[0, 0, 0] == pytest.approx(1.0)
+    out = O.ms_deform_attn_forward(value, ((2, 2),), loc, np.array([[[[0.0, 1.0]]]], np.float32))
+    assert out[0, 0, 0] == pytest.approx(4.0)
+
+
+def test_zero_pads_outside():
+    """Reference ``test_ops.py:32-36``: far out-of-bounds samples contribute zero."""
+    value = np.ones((1, 4, 1), np.float32)
+    loc = np.full((1, 1, 1, 1, 1, 2), 3.0, np.float32)  # grid 5.0
+    assert O.ms_deform_attn_forward(value, ((2, 2),), loc, np.ones((1, 1, 1, 1), np.float32))[0, 0, 0] == 0.0
+
+
+def test_interpolates_linearly():
+    """Reference ``test_ops.py:39-43``: midway between pixel centres averages them."""
+    value = np.array([[[0.0], [4.0]]], np.float32)  # 1x2 map
+    loc = np.full((1, 1, 1, 1, 1, 2), 0.5, np.float32)  # grid (0, 0)
+    out = O.ms_deform_attn_forward(value, ((1, 2),), loc, np.ones((1, 1, 1, 1), np.float32))
+    assert out[0, 0, 0] == pytest.approx(2.0)
+
+
+def test_core_mean_of_points():
+    """Reference ``test_ops.py:46-54``: uniform weights give the mean of the sampled points."""
+    value = np.arange(4, dtype=np.float32).reshape(1, 4, 1)
+    loc = np.array([[[[[[0.25, 0.25], [0.75, 0.75]]]]]], np.float32)
+    out = O.ms_deform_attn_forward(value, ((2, 2),), loc, np.full((1, 1, 1, 2), 0.5, np.float32))
+    assert out.shape == (1, 1, 1)
+    assert out[0, 0, 0] == pytest.approx(1.5)
+
+
+@pytest.mark.parametrize(
+    ("batch", "len_query", "heads", "shapes", "points", "dim"),
+    [
+        (2, 70, 2, ((8, 16), (4, 8)), 3, 8),   # the reference's pallas-vs-gather case (test_ops.py:225-248)
+        (2, 11, 4, ((7, 5),), 3, 8),            # the reference's matmul-vs-gather case (test_ops.py:112-124)
+        (1, 9, 3, ((6, 6), (3, 3), (2, 1)), 2, 5),
+    ],
+)
+def test_matches_grid_sample_forward_and_backward(batch, len_query, heads, shapes, points, dim):
+    value, loc, attn, grad = _case(7, batch, len_query, heads, shapes, points, dim)
+    tv = torch.tensor(value, dtype=torch.float64, requires_grad=True)
+    tl = torch.tensor(loc, dtype=torch.float64, requires_grad=True)
+    ta = torch.tensor(attn, dtype=torch.float64, requires_grad=True)
+    out_t = _torch_msda(tv, shapes, tl, ta)
+    out_t.backward(torch.tensor(grad, dtype=torch.float64))
+
+    # grid_sample derives float64 coordinates from the float64 locations; the oracle derives
+    # float32 ones, as the reference does (ops.py:80-84).  The difference is one float32
+    # rounding of the position, ~1e-7 relative, hence the fp32-level tolerance.  The location
+    # gradient is piecewise constant in the position, so it agrees except on the measure-zero
+    # set where the two floor() calls could differ.
+    out_o = O.ms_deform_attn_forward(value, shapes, loc, attn)
+    np.testing.assert_allclose(out_o, out_t.detach().numpy(), rtol=1e-5, atol=2e-6)
+    gv, gl, ga = O.ms_deform_attn_backward(value, shapes, loc, attn, grad)
+    np.testing.assert_allclose(gv, tv.grad.numpy(), rtol=1e-5, atol=2e-6)
+    np.testing.assert_allclose(ga, ta.grad.numpy(), rtol=1e-5, atol=2e-6)
+    np.testing.assert_allclose(gl, tl.grad.numpy(), rtol=1e-5, atol=2e-6)
+
+
+def test_float32_accumulation_tracks_float64():
+    value, loc, attn, grad = _case(1, 2, 40, 4, ((9, 7),), 2, 16)
+    shapes = ((9, 7),)
+    exact = O.ms_deform_attn_forward(value, shapes, loc, attn)
+    fast = O.ms_deform_attn_forward(value, shapes, loc, attn, compute=np.float32)
+    np.testing.assert_allclose(fast, exact, rtol=1e-5, atol=1e-6)
+    for a, b in zip(O.ms_deform_attn_backward(value, shapes, loc, attn, grad, compute=np.float32),
+                    O.ms_deform_attn_backward(value, shapes, loc, attn, grad), strict=True):
+        np.testing.assert_allclose(a, b, rtol=1e-4, atol=1e-5)
+
+
+def test_non_finite_locations_give_nan():
+    value, loc, attn, grad = _case(2, 1, 4, 1, ((3, 3),), 1, 2)
+    loc[0, 1, 0, 0, 0, 0] = np.nan
+    loc[0, 2, 0, 0, 0, 1] = np.inf
+    out = O.ms_deform_attn_forward(value, ((3, 3),), loc, attn)
+    assert np.isnan(out[0, 1]).all() and np.isnan(out[0, 2]).all()
+    assert np.isfinite(out[0, 0]).all() and np.isfinite(out[0, 3]).all()
+    gv, gl, ga = O.ms_deform_attn_backward(value, ((3, 3),), loc, attn, grad)
+    assert np.isfinite(gv).all()
+    assert np.isnan(gl[0, 1]).all() and np.isnan(ga[0, 1]).all()
+
+
+def test_bf16_round_matches_torch():
+    x = np.random.default_rng(0).standard_normal(10000).astype(np.float32) * 10
+    expected = torch.tensor(x).to(torch.bfloat16).to(torch.float32).numpy()
+    np.testing.assert_array_equal(O.bf16_round(x), expected)
+
+
+def test_rejects_bad_shapes():
+    value, loc, attn, _ = _case(0, 1, 2, 2, ((2, 2),), 1, 4)
+    with pytest.raises(ValueError):
+        O.ms_deform_attn_forward(value[:, :3], ((2, 2),), loc, attn)
+    with pytest.raises(ValueError):
+        O.ms_deform_attn_forward(value, ((2, 2), (1, 1)), loc, attn)

@@ -1,0 +1,97 @@
+"""Parity of the CUDA two-stage selection (class max + top-k) and select_rows: bit-exact."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import load_golden
+from oracle import topk as OT
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _select(pkg, logits, k):
+    s, v, i = pkg.two_stage_topk(torch.tensor(logits, device=DEV), k)
+    return s.cpu().numpy(), v.cpu().numpy(), i.cpu().numpy()
+
+
+def test_golden(pkg):
+    d = load_golden("topk_c4_small")
+    s, v, i = _select(pkg, d["logits"], 300)
+    np.testing.assert_array_equal(i, d["indices"])
+    np.testing.assert_array_equal(v.view(np.uint32), d["values"].view(np.uint32))
+    np.testing.assert_array_equal(s.view(np.uint32), d["scores"].view(np.uint32))
+    s, v, i = _select(pkg, d["tie_logits"], 300)
+    np.testing.assert_array_equal(i, d["tie_indices"])
+    np.testing.assert_array_equal(v, d["tie_values"])
+
+
+def test_config4_training_shape(pkg):
+    """Config 4 at training shape: 13 groups x 8 images x 576 proposals x 91 classes."""
+    logits = np.random.default_rng(4).standard_normal((13, 8, 576, 91)).astype(np.float32)
+    s, v, i = _select(pkg, logits, 300)
+    ws, wv, wi = OT.two_stage_select(logits, 300)
+    np.testing.assert_array_equal(i, wi)
+    np.testing.assert_array_equal(v, wv)
+    np.testing.assert_array_equal(s, ws)
+    assert i.dtype == np.int32
+
+
+def test_ties_keep_lower_index_first(pkg):
+    """jax.lax.top_k order: equal scores come out in ascending index order."""
+    scores = np.array([[5.0, 4.0, 4.0, 1.0, 0.5, 0.1, 4.0, 4.0]], np.float32)
+    v, i = pkg.top_k(torch.tensor(scores, device=DEV), 5)
+    np.testing.assert_array_equal(i.cpu().numpy(), [[0, 1, 2, 6, 7]])
+    constant = np.zeros((3, 1000), np.float32)
+    _, i = pkg.top_k(torch.tensor(constant, device=DEV), 300)
+    np.testing.assert_array_equal(i.cpu().numpy(), np.tile(np.arange(300), (3, 1)))
+
+
+def test_special_values(pkg):
+    """NaN first, then +inf ... -inf; +0 above -0 (IEEE totalOrder)."""
+    row = np.array([1.0, -np.inf, np.nan, 0.0, -0.0, np.inf, -1.0, 2.0], np.float32)
+    v, i = pkg.top_k(torch.tensor(row[None], device=DEV), 8)
+    wv, wi = OT.top_k(row[None], 8)
+    np.testing.assert_array_equal(i.cpu().numpy(), wi)
+    np.testing.assert_array_equal(np.isnan(v.cpu().numpy()), np.isnan(wv))
+    logits = np.random.default_rng(5).standard_normal((2, 40, 7)).astype(np.float32)
+    logits[0, 3, 2] = np.nan
+    logits[1, 5, :] = -np.inf
+    s, _, i = _select(pkg, logits, 40)
+    ws, _, wi = OT.two_stage_select(logits, 40)
+    np.testing.assert_array_equal(i, wi)
+    np.testing.assert_array_equal(np.isnan(s), np.isnan(ws))
+
+
+@pytest.mark.parametrize(("positions", "classes", "k"), [(1, 1, 1), (7, 3, 7), (576, 91, 1), (1000, 1, 999),
+                                                          (5000, 2, 300), (16384, 1, 16384)])
+def test_sizes(pkg, positions, classes, k):
+    logits = np.random.default_rng(positions).integers(-50, 50, (3, positions, classes)).astype(np.float32)
+    s, v, i = _select(pkg, logits, k)
+    ws, wv, wi = OT.two_stage_select(logits, k)
+    np.testing.assert_array_equal(i, wi)
+    np.testing.assert_array_equal(v, wv)
+
+
+def test_select_rows(pkg):
+    rng = np.random.default_rng(7)
+    for dtype, width in ((torch.float32, 256), (torch.bfloat16, 256), (torch.float32, 5), (torch.bfloat16, 3)):
+        values = torch.tensor(rng.standard_normal((13, 2, 576, width)), device=DEV).to(dtype)
+        idx = torch.tensor(rng.integers(0, 576, (13, 2, 300)), device=DEV, dtype=torch.int32)
+        got = pkg.select_rows(values, idx)
+        want = torch.take_along_dim(values, idx.long()[..., None], dim=2)
+        assert torch.equal(got, want)
+    with pytest.raises(ValueError, match="out of bounds"):
+        pkg.select_rows(values, torch.full((13, 2, 4), 576, device=DEV, dtype=torch.int32))
+
+
+def test_errors(pkg):
+    x = torch.zeros((2, 10), device=DEV)
+    with pytest.raises(ValueError):
+        pkg.top_k(x, 11)
+    with pytest.raises(ValueError):
+        pkg.top_k(x.double(), 3)
