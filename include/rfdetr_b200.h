@@ -33,7 +33,8 @@ enum rfdetr_status {
     RFDETR_ERR_ALIGN = 3,     /* a pointer is not aligned to its element type */
     RFDETR_ERR_WORKSPACE = 4, /* workspace missing or smaller than the size query returned */
     RFDETR_ERR_CUDA = 5,      /* a CUDA runtime call or kernel launch failed */
-    RFDETR_ERR_LIMIT = 6      /* a device loop reached its iteration cap (reported via status buffer) */
+    RFDETR_ERR_LIMIT = 6,     /* a device loop reached its iteration cap (reported via status buffer) */
+    RFDETR_ERR_CAPACITY = 7   /* problem larger than the no-alloc entry point's static scratch */
 };
 
 /* Human-readable text for a status code (static storage). */
@@ -94,6 +95,37 @@ int rfdetr_msda_backward(void *stream,
                          void *workspace, size_t workspace_bytes,
                          int64_t batch, int64_t n_heads, int64_t head_dim, int64_t len_query,
                          int64_t n_levels, int64_t n_points);
+
+/*
+ * rfdetr_msda_backward without a workspace argument, for callers that cannot allocate device
+ * memory at the point of the call: a host framework whose allocator owns all device memory and
+ * hands its custom calls no scratch buffer (an XLA FFI handler registered without a scratch
+ * allocator, for instance), or latency-critical code that must not allocate after start-up.
+ * There is no counterpart in the reference (its backward is JAX autodiff).
+ *
+ * The bf16 path's float32 accumulator lives in a static device array of the library
+ * (RFDETR_MSDA_NOALLOC_SCRATCH_BYTES, 8 MiB; every GPU that loads the library holds it until the
+ * process exits), so batch * n_heads * Lv * head_dim must not exceed 2,097,152 elements for bf16
+ * values; larger problems return RFDETR_ERR_CAPACITY without launching anything.  Float32 values
+ * need no scratch and have no extra limit.  The entry point itself allocates nothing.
+ *
+ * The first call on each device looks up the array's device address (cudaGetSymbolAddress, with
+ * that device current); make that first call before any stream capture.  Every call on a device
+ * shares the one array: the call clears it before use, but calls whose work overlaps on the GPU
+ * (different streams, or different host threads, on the same device) race on it and must be
+ * serialised by the caller.  Arguments and results are those of rfdetr_msda_backward.
+ */
+#define RFDETR_MSDA_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+int rfdetr_msda_backward_noalloc(void *stream,
+                                 const void *value, int value_dtype,
+                                 const int64_t *spatial_shapes, const int64_t *level_start_index,
+                                 const float *sampling_locations,
+                                 const void *attention_weights, int weight_dtype,
+                                 const void *grad_output, int grad_output_dtype,
+                                 void *grad_value, float *grad_sampling_locations,
+                                 void *grad_attention_weights,
+                                 int64_t batch, int64_t n_heads, int64_t head_dim, int64_t len_query,
+                                 int64_t n_levels, int64_t n_points);
 
 /* ---------------------------------------------------------------------------------------
  * Two-stage query selection.

@@ -26,6 +26,7 @@ ERR_ALIGN = 3
 ERR_WORKSPACE = 4
 ERR_CUDA = 5
 ERR_LIMIT = 6
+ERR_CAPACITY = 7
 
 _lock = threading.Lock()
 _lib = None
@@ -45,6 +46,8 @@ SIGNATURES = {
     "rfdetr_msda_backward_workspace_size": (ctypes.c_size_t, [_int, _i64, _i64, _i64, _i64]),
     "rfdetr_msda_backward": (_int, [_vp, _vp, _int, _c_int64_p, _c_int64_p, _vp, _vp, _int, _vp, _int,
                                     _vp, _vp, _vp, _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64, _i64, _i64]),
+    "rfdetr_msda_backward_noalloc": (_int, [_vp, _vp, _int, _c_int64_p, _c_int64_p, _vp, _vp, _int, _vp, _int,
+                                            _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64]),
     "rfdetr_topk_select": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "rfdetr_select_rows": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "rfdetr_match_cost": (_int, [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
@@ -85,7 +88,7 @@ def check(status: int, what: str) -> None:
     if status == OK:
         return
     text = f"{what}: {status_text(status)} (status {status})"
-    if status in (ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_WORKSPACE):
+    if status in (ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_WORKSPACE, ERR_CAPACITY):
         raise ValueError(text)
     raise RuntimeError(text)
 

@@ -30,6 +30,7 @@ extern "C" const char *rfdetr_status_string(int status) {
         case RFDETR_ERR_WORKSPACE: return "workspace missing or too small";
         case RFDETR_ERR_CUDA: return "CUDA runtime error";
         case RFDETR_ERR_LIMIT: return "device loop reached its iteration cap";
+        case RFDETR_ERR_CAPACITY: return "problem exceeds the no-alloc entry point's static scratch (8 MiB)";
         default: return "unknown status";
     }
 }

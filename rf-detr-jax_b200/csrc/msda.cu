@@ -21,6 +21,7 @@
 // produced in the same pass from team-reduced dot products.
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 #include <cstdlib>
 #include <cstring>
 
@@ -756,4 +757,56 @@ extern "C" int rfdetr_msda_backward(void *stream, const void *value, int value_d
         return launch_status();
     }
     return RFDETR_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Backward without a workspace argument (see rfdetr_msda_backward_noalloc in the header).
+// The float32 accumulator of the bf16 path lives in this static device array.  In host code
+// the name is only a host-side stand-in, so its device address is looked up per device with
+// cudaGetSymbolAddress and passed to the kernels like a caller's workspace.
+// ------------------------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchBytes = RFDETR_MSDA_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void *g_noalloc_address[kNoAllocMaxDevices] = {nullptr};
+}  // namespace
+
+static __device__ __align__(256) float g_msda_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+extern "C" int rfdetr_msda_backward_noalloc(void *stream, const void *value, int value_dtype,
+                                            const int64_t *spatial_shapes, const int64_t *level_start_index,
+                                            const float *sampling_locations, const void *attention_weights,
+                                            int weight_dtype, const void *grad_output, int grad_output_dtype,
+                                            void *grad_value, float *grad_sampling_locations,
+                                            void *grad_attention_weights, int64_t batch, int64_t n_heads,
+                                            int64_t head_dim, int64_t len_query, int64_t n_levels,
+                                            int64_t n_points) {
+    void *scratch = nullptr;
+    size_t scratch_bytes = 0;
+    if (value_dtype == RFDETR_BF16) {
+        Geom g;
+        const int st = validate(spatial_shapes, level_start_index, batch, n_heads, head_dim, len_query, n_levels,
+                                n_points, g);
+        if (st) return st;
+        const size_t need = rfdetr_msda_backward_workspace_size(value_dtype, batch, n_heads, head_dim, g.Lv);
+        if (need > kNoAllocScratchBytes) return RFDETR_ERR_CAPACITY;
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return RFDETR_ERR_CUDA;
+        {
+            std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+            if (!g_noalloc_address[dev]) {
+                void *address = nullptr;
+                if (cudaGetSymbolAddress(&address, g_msda_noalloc_scratch) != cudaSuccess || !address)
+                    return RFDETR_ERR_CUDA;
+                g_noalloc_address[dev] = address;
+            }
+            scratch = g_noalloc_address[dev];
+        }
+        scratch_bytes = kNoAllocScratchBytes;
+    }
+    return rfdetr_msda_backward(stream, value, value_dtype, spatial_shapes, level_start_index, sampling_locations,
+                                attention_weights, weight_dtype, grad_output, grad_output_dtype, grad_value,
+                                grad_sampling_locations, grad_attention_weights, scratch, scratch_bytes, batch,
+                                n_heads, head_dim, len_query, n_levels, n_points);
 }

@@ -1,0 +1,82 @@
+"""The workspace-free backward entry point, ``rfdetr_msda_backward_noalloc``, against the
+regular one.
+
+Some callers cannot hand the library a device workspace: a framework whose allocator owns all
+device memory and gives its custom calls no scratch buffer, or code that must not allocate after
+start-up.  For them the bf16 backward keeps its float32 accumulator in a static device array of
+the library instead of a caller-provided workspace.  This test calls both entry points through
+the C ABI on config-2 inputs and checks that two consecutive no-alloc calls each reproduce the
+workspace call within the bf16 tolerance the other tests use (the array keeps the previous
+call's contents, so the second call also checks that it is cleared), and that a problem larger
+than the array is refused without a launch.  It lives in its own file, collected last.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_bf16_close, assert_fp32_close, sampler_inputs
+from oracle import msda as O
+
+pytestmark = pytest.mark.gpu
+
+B, LQ, H, D, P = 8, 3900, 16, 16, 2
+SHAPES = ((24, 24),)
+
+
+def _buffers(dev):
+    value, loc, attn, grad = sampler_inputs(21, B, LQ, H, SHAPES, P, D, lo=-0.05, hi=1.05)
+    t = lambda x, dt: torch.tensor(x, device=dev).to(dt)  # noqa: E731
+    return (t(value, torch.bfloat16), t(loc, torch.float32), t(attn, torch.bfloat16), t(grad, torch.bfloat16))
+
+
+def _grads(dev, value, loc, attn):
+    return torch.empty_like(value), torch.empty_like(loc), torch.empty_like(attn)
+
+
+def test_noalloc_backward_matches_workspace_backward(pkg):
+    N = pkg._native
+    lib = N.lib()
+    dev = torch.device("cuda:0")
+    value, loc, attn, grad = _buffers(dev)
+    shapes = N.int64_array([24, 24])
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    gv, gl, ga = _grads(dev, value, loc, attn)
+    ws_bytes = lib.rfdetr_msda_backward_workspace_size(N.BF16, B, H, D, 576)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    N.check(lib.rfdetr_msda_backward(stream, value.data_ptr(), N.BF16, shapes, None, loc.data_ptr(),
+                                     attn.data_ptr(), N.BF16, grad.data_ptr(), N.BF16, gv.data_ptr(), gl.data_ptr(),
+                                     ga.data_ptr(), ws.data_ptr(), ws_bytes, B, H, D, LQ, 1, P), "backward")
+    torch.cuda.synchronize()
+    want = [x.float().cpu().numpy() for x in (gv, gl, ga)]
+
+    for call in range(2):
+        nv, nl, na = _grads(dev, value, loc, attn)
+        N.check(lib.rfdetr_msda_backward_noalloc(stream, value.data_ptr(), N.BF16, shapes, None, loc.data_ptr(),
+                                                 attn.data_ptr(), N.BF16, grad.data_ptr(), N.BF16, nv.data_ptr(),
+                                                 nl.data_ptr(), na.data_ptr(), B, H, D, LQ, 1, P),
+                f"backward_noalloc call {call}")
+        torch.cuda.synchronize()
+        got = [x.float().cpu().numpy() for x in (nv, nl, na)]
+        assert_bf16_close(got[0], want[0], f"call {call}: grad_value")
+        assert_fp32_close(got[1], want[1], f"call {call}: grad_loc")
+        assert_bf16_close(got[2], want[2], f"call {call}: grad_attn")
+
+    # Both agree with the oracle too (the bf16 contract).
+    v = value.float().cpu().numpy()
+    ref = O.ms_deform_attn_backward(v[: 2 * H], SHAPES, loc[:2].cpu().numpy(), attn[:2].float().cpu().numpy(),
+                                    grad[:2].float().cpu().numpy())
+    assert_bf16_close(got[0][: 2 * H], ref[0], "oracle: grad_value")
+
+
+def test_noalloc_refuses_problems_beyond_its_scratch(pkg):
+    N = pkg._native
+    lib = N.lib()
+    # 64 images x 16 heads x 576 positions x 16 channels = 9.4M floats > 2,097,152.
+    status = lib.rfdetr_msda_backward_noalloc(None, None, N.BF16, N.int64_array([24, 24]), None, None, None,
+                                              N.BF16, None, N.BF16, None, None, None, 64, 16, 16, 3900, 1, 2)
+    assert status == N.ERR_CAPACITY
+    assert "static scratch" in N.status_text(status)
