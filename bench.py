@@ -91,6 +91,17 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def wait_first_sample(self, timeout_s=10.0):
+        """Block until nvidia-smi has written its first line (it takes a moment to start)."""
+        if self.proc is None:
+            return
+        t0 = time.time()
+        while time.time() - t0 < timeout_s:
+            self.file.flush()
+            if os.path.exists(self.path) and os.path.getsize(self.path) > 0:
+                return
+            time.sleep(0.05)
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -264,12 +275,9 @@ def run_ours(args):
             graphs[kind].append(g)
     torch.cuda.synchronize()
 
-    def timed(kind, steps, warmup):
+    def timed_once(kind, steps):
+        """One timed region of exactly `steps` graph replays; ms per step, max over ranks."""
         gl_ = graphs[kind]
-        with torch.cuda.stream(stream):
-            for i in range(warmup):
-                gl_[i % ring].replay()
-        stream.synchronize()
         barrier()
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -288,12 +296,32 @@ def run_ours(args):
             ms = float(t.item())
         return ms / steps
 
+    def timed(kind, steps, warmup, min_seconds):
+        """Warm up, then repeat the K-step timed region until `min_seconds` of device time have
+        passed (so the clock sampler sees the load); returns the median ms per step and the
+        number of repetitions.  Every rank runs the same number of repetitions."""
+        gl_ = graphs[kind]
+        with torch.cuda.stream(stream):
+            for i in range(warmup):
+                gl_[i % ring].replay()
+        stream.synchronize()
+        first = timed_once(kind, steps)
+        reps = max(1, min(2000, int(min_seconds * 1e3 / max(first * steps, 1e-3))))
+        if world > 1:
+            t = torch.tensor([reps], device=device, dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            reps = int(t.item())
+        samples = [timed_once(kind, steps) for _ in range(reps)]
+        return statistics.median(samples), reps
+
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else local
     with ClockSampler(gpu_index) as clocks:
-        ms_step = timed("step", args.steps, args.warmup)
-        ms_fwd = timed("fwd", args.steps, args.warmup)
-        ms_bwd = timed("bwd", args.steps, args.warmup)
+        clocks.wait_first_sample()
+        min_s = float(os.environ.get("RFDETR_BENCH_MIN_SECONDS", "2.0"))
+        ms_step, reps_step = timed("step", args.steps, args.warmup, min_s)
+        ms_fwd, _ = timed("fwd", args.steps, args.warmup, min_s / 4)
+        ms_bwd, _ = timed("bwd", args.steps, args.warmup, min_s / 4)
     clock_summary = clocks.summary()
 
     # End to end through the public API from pinned host memory.
@@ -359,8 +387,10 @@ def run_ours(args):
         "config": {"workload": "config2 sampler fwd+bwd (Nano decoder cross-attn, train shape)",
                    "batch_per_gpu": B, "len_query": LQ, "heads": H, "head_dim": D,
                    "levels": [list(s) for s in SHAPES], "points": P, "parallelism": f"dp{world} (independent shards)",
-                   "l2": f"ring of {ring} input/output sets ({ring * per_set / 2**20:.0f} MiB) > L2, no flush"},
-        "roofline": {"bound": "hbm", "kernel": "msda_backward (memset + kernel + fp32->bf16)", "achieved": achieved,
+                   "l2": f"ring of {ring} input/output sets ({ring * per_set / 2**20:.0f} MiB) > L2, no flush",
+                   "timing": f"median of {reps_step} timed regions of exactly {args.steps} steps, "
+                             "one CUDA-graph replay per step"},
+        "roofline": {"bound": "hbm", "kernel": "msda_backward_bins_kernel", "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "peak_source": peak_src, "algorithmic_bytes": bwd_bytes, "ms_per_launch": ms_bwd},
         "kernels": {"msda_forward": {"ms": ms_fwd, "GB/s": fwd_bytes / (ms_fwd * 1e-3) / 1e9,
@@ -368,7 +398,7 @@ def run_ours(args):
                     "msda_backward": {"ms": ms_bwd, "GB/s": achieved, "frac": achieved / peak}},
         "e2e": {"value": queries / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 2 * args.steps,
         "clocks": clock_summary,
     }
     if cpu is not None:

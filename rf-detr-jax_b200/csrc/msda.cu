@@ -63,12 +63,14 @@ __device__ __forceinline__ void load_levels(LevelTable &t, const Geom &g) {
 // ops.py:270 (grids = 2*loc - 1) and ops.py:83-84 (ix = ((gx + 1) * W - 1) / 2): one IEEE
 // float32 rounding per step and no FMA contraction, so floor(ix) agrees with the reference
 // bit for bit.  The division by two is exact, hence the multiply.
+// Two of the steps are fused without changing a bit: 2*loc is exact, so fma(2, loc, -1) rounds
+// once like 2*loc - 1; halving is exact, so fma(u, 0.5, -0.5) = round(u - 1) / 2.
 __device__ __forceinline__ void sample_coords(float lx, float ly, float wf, float hf, float &ix,
                                               float &iy) {
-    const float gx = __fsub_rn(__fmul_rn(2.f, lx), 1.f);
-    const float gy = __fsub_rn(__fmul_rn(2.f, ly), 1.f);
-    ix = __fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(gx, 1.f), wf), 1.f), 0.5f);
-    iy = __fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(gy, 1.f), hf), 1.f), 0.5f);
+    const float gx = __fmaf_rn(2.f, lx, -1.f);
+    const float gy = __fmaf_rn(2.f, ly, -1.f);
+    ix = __fmaf_rn(__fmul_rn(__fadd_rn(gx, 1.f), wf), 0.5f, -0.5f);
+    iy = __fmaf_rn(__fmul_rn(__fadd_rn(gy, 1.f), hf), 0.5f, -0.5f);
 }
 
 // Bilinear taps of one sample (ops.py:85-106): fractional weights, the top-left corner and a
@@ -633,6 +635,737 @@ int dispatch_backward(const Geom &g, Plan &p, const Tune &tune, const void *valu
 bool dtype_ok(int d) { return d == RFDETR_F32 || d == RFDETR_BF16; }
 int out_dtype(int vd, int wd) { return (vd == RFDETR_BF16 && wd == RFDETR_BF16) ? RFDETR_BF16 : RFDETR_F32; }
 
+// ------------------------------------------------------------------------------------------
+// Slab-resident forward.  Used when the value rows of a head group fit in shared memory and the
+// location/weight rows of a (query, head group) are 4-byte-granular segments.  The slabs are
+// copied once per CTA with cp.async; location/weight tiles of `tq` queries are double-buffered
+// with cp.async so their HBM latency overlaps the previous tile's gathers.  Taps are branch-free:
+// all four corners are read at the reference's clipped indices (ops.py:103-106) and out-of-range
+// corners get weight 0 (ops.py:123-128), which also reproduces the reference's NaN/inf
+// propagation from value entries.
+// ------------------------------------------------------------------------------------------
+constexpr int kSlabThreads = 512;
+
+__device__ __forceinline__ void cp_async_bytes(void *smem_dst, const void *gmem_src, int bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem_dst);
+    if (bytes == 16) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem_src) : "memory");
+    } else if (bytes == 8) {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(s), "l"(gmem_src) : "memory");
+    } else {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem_src) : "memory");
+    }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+__device__ __forceinline__ float2 bf16x2_lo_hi(unsigned u) {
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+struct SlabPlan {
+    int hsub, tq, q_per_cta, gl, ga;  // gl/ga: granule bytes for location / weight segments
+    size_t slab_bytes, tile_bytes, smem;
+};
+
+// Branch-free taps of one sample: clipped corner positions (element offsets in units of rows)
+// and the attention-weighted, masked bilinear coefficients.  `ok` is false for non-finite
+// positions (the reference yields NaN there).
+struct FlatTaps {
+    int p00, p10, p01, p11;
+    float c00, c10, c01, c11;
+    bool ok;
+};
+
+// floor(x) as an int and as a float for |x| < 2^22 without the XU pipe: adding 1.5 * 2^23
+// rounds to the nearest integer (exactly representable there), and a rounded-up result steps
+// down by one.  Callers clamp x into a small range first.
+__device__ __forceinline__ void floor_split(float x, int &xi, float &xf) {
+    const float t = __fadd_rn(x, 12582912.f);
+    const float r = __fsub_rn(t, 12582912.f);
+    const int i = __float_as_int(t) - 0x4B400000;
+    const bool up = r > x;
+    xf = up ? r - 1.f : r;
+    xi = up ? i - 1 : i;
+}
+
+// Fractional weights, clipped corner indices and 0/1 masks of one axis.  Clamping x into
+// [-2, size + 1] changes neither the in-bounds corners nor their weights.
+struct Axis {
+    float w0, w1, m0, m1;
+    int c0, c1;
+};
+__device__ __forceinline__ Axis axis_taps(float x, float sizef, int size) {
+    Axis a;
+    const float xc = fminf(fmaxf(x, -2.f), sizef + 1.f);
+    int i0;
+    float f0;
+    floor_split(xc, i0, f0);
+    a.w1 = xc - f0;
+    a.w0 = 1.f - a.w1;
+    a.m0 = (unsigned)i0 < (unsigned)size ? 1.f : 0.f;
+    a.m1 = (unsigned)(i0 + 1) < (unsigned)size ? 1.f : 0.f;
+    a.c0 = min(max(i0, 0), size - 1);
+    a.c1 = min(max(i0 + 1, 0), size - 1);
+    return a;
+}
+
+__device__ __forceinline__ FlatTaps flat_taps(float lx, float ly, float a, float Wf, float Hf, int W, int H) {
+    FlatTaps t;
+    float ix, iy;
+    sample_coords(lx, ly, Wf, Hf, ix, iy);
+    t.ok = fabsf(ix) <= 3.0e38f && fabsf(iy) <= 3.0e38f;
+    const Axis ax = axis_taps(ix, Wf, W), ay = axis_taps(iy, Hf, H);
+    const float ax0 = a * (ax.w0 * ax.m0), ax1 = a * (ax.w1 * ax.m1);
+    const float ay0 = ay.w0 * ay.m0, ay1 = ay.w1 * ay.m1;
+    t.c00 = ax0 * ay0;
+    t.c10 = ax1 * ay0;
+    t.c01 = ax0 * ay1;
+    t.c11 = ax1 * ay1;
+    t.p00 = ay.c0 * W + ax.c0;
+    t.p10 = ay.c0 * W + ax.c1;
+    t.p01 = ay.c1 * W + ax.c0;
+    t.p11 = ay.c1 * W + ax.c1;
+    return t;
+}
+
+// Accumulates coef * value-chunk into acc.  bf16: 8 channels (one 16-byte row chunk) into four
+// packed float pairs; f32: 4 channels into doubles.
+template <typename TV> struct SlabAcc;
+template <> struct SlabAcc<bf16> {
+    static constexpr int VEC = 8;
+    float2 v[4];
+    __device__ __forceinline__ void zero() {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = make_float2(0.f, 0.f);
+    }
+    __device__ __forceinline__ void add(float c, const uint4 &r) {
+        const float2 cc = make_float2(c, c);
+        v[0] = __ffma2_rn(cc, bf16x2_lo_hi(r.x), v[0]);
+        v[1] = __ffma2_rn(cc, bf16x2_lo_hi(r.y), v[1]);
+        v[2] = __ffma2_rn(cc, bf16x2_lo_hi(r.z), v[2]);
+        v[3] = __ffma2_rn(cc, bf16x2_lo_hi(r.w), v[3]);
+    }
+    __device__ __forceinline__ void poison() {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = make_float2(__int_as_float(0x7fc00000), __int_as_float(0x7fc00000));
+    }
+    __device__ __forceinline__ void to_float(float *f) const {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            f[2 * i] = v[i].x;
+            f[2 * i + 1] = v[i].y;
+        }
+    }
+};
+template <> struct SlabAcc<float> {
+    static constexpr int VEC = 4;
+    double v[4];
+    __device__ __forceinline__ void zero() {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = 0.0;
+    }
+    __device__ __forceinline__ void add(float c, const uint4 &r) {
+        const double cd = c;
+        v[0] = fma(cd, (double)__uint_as_float(r.x), v[0]);
+        v[1] = fma(cd, (double)__uint_as_float(r.y), v[1]);
+        v[2] = fma(cd, (double)__uint_as_float(r.z), v[2]);
+        v[3] = fma(cd, (double)__uint_as_float(r.w), v[3]);
+    }
+    __device__ __forceinline__ void poison() {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = (double)__int_as_float(0x7fc00000);
+    }
+    __device__ __forceinline__ void to_float(float *f) const {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f[i] = (float)v[i];
+    }
+};
+
+// Issues the cp.async copies of one tile's location and weight segments.  Granule counts per
+// query are powers of two (hsub, LP, sizes and granules all are), so indices split by shifts.
+template <typename TW, int LP>
+__device__ __forceinline__ void issue_tile(const float *loc, const TW *attn, float *sloc, TW *sattn, const Geom &g,
+                                           int b, int h0, int hsub, int qa, int nq, int gl, int ga) {
+    const int lbytes = hsub * LP * 8, abytes = hsub * LP * (int)sizeof(TW);
+    const int ls = 31 - __clz(lbytes / gl), as = 31 - __clz(abytes / ga);
+    const size_t row0 = ((size_t)b * g.Lq + qa) * g.H + h0;
+    const size_t rstride = (size_t)g.H;
+    for (int i = threadIdx.x; i < (nq << ls); i += blockDim.x) {
+        const int qi = i >> ls, j = i & ((1 << ls) - 1);
+        cp_async_bytes(reinterpret_cast<char *>(sloc) + (size_t)qi * lbytes + j * gl,
+                       reinterpret_cast<const char *>(loc + (row0 + qi * rstride) * LP * 2) + j * gl, gl);
+    }
+    for (int i = threadIdx.x; i < (nq << as); i += blockDim.x) {
+        const int qi = i >> as, j = i & ((1 << as) - 1);
+        cp_async_bytes(reinterpret_cast<char *>(sattn) + (size_t)qi * abytes + j * ga,
+                       reinterpret_cast<const char *>(attn + (row0 + qi * rstride) * LP) + j * ga, ga);
+    }
+}
+
+template <typename TV, typename TW, int LP>
+__global__ void __launch_bounds__(kSlabThreads, 2)
+msda_forward_slab_kernel(const TV *__restrict__ value, const float *__restrict__ loc, const TW *__restrict__ attn,
+                         typename OutOf<TV, TW>::T *__restrict__ out, const Geom g, const SlabPlan sp) {
+    using TO = typename OutOf<TV, TW>::T;
+    using Acc = SlabAcc<TV>;
+    constexpr int VEC = Acc::VEC;
+    extern __shared__ __align__(16) unsigned char smem[];
+
+    const int hsub = sp.hsub;
+    const int hshift = 31 - __clz(hsub);
+    const int groups_per_image = g.H >> hshift;
+    const int b = blockIdx.y / groups_per_image;
+    const int h0 = (blockIdx.y - b * groups_per_image) << hshift;
+    const int q0 = blockIdx.x * sp.q_per_cta;
+    const int q1 = min(q0 + sp.q_per_cta, g.Lq);
+
+    // Stage the head group's value slabs (contiguous in [B*H, Lv, D]).
+    const size_t slab_elems = (size_t)g.Lv * g.D;
+    const TV *vsrc = value + ((size_t)b * g.H + h0) * slab_elems;
+    const int n16 = (int)(sp.slab_bytes * hsub / 16);
+    for (int i = threadIdx.x; i < n16; i += blockDim.x)
+        cp_async_bytes(smem + (size_t)i * 16, reinterpret_cast<const char *>(vsrc) + (size_t)i * 16, 16);
+    unsigned char *tiles = smem + ((sp.slab_bytes * hsub + 15) & ~(size_t)15);
+    const size_t lbytes = (size_t)sp.tq * hsub * LP * 8;
+    const size_t abytes = (((size_t)sp.tq * hsub * LP * sizeof(TW)) + 15) & ~(size_t)15;
+    float *const sloc0 = reinterpret_cast<float *>(tiles);
+    float *const sloc1 = reinterpret_cast<float *>(tiles + lbytes + abytes);
+    TW *const sattn0 = reinterpret_cast<TW *>(tiles + lbytes);
+    TW *const sattn1 = reinterpret_cast<TW *>(tiles + 2 * lbytes + abytes);
+    const int ntiles = (q1 - q0 + sp.tq - 1) / sp.tq;
+    if (ntiles > 0) issue_tile<TW, LP>(loc, attn, sloc0, sattn0, g, b, h0, hsub, q0, min(sp.tq, q1 - q0), sp.gl, sp.ga);
+    cp_async_commit();
+
+    // Per-sample level geometry, held in registers (LP is a compile-time constant).
+    int kw[LP], kh[LP];
+    float kwf[LP], khf[LP];
+    unsigned koff[LP];
+    const unsigned rowbytes = (unsigned)(g.D * sizeof(TV));
+#pragma unroll
+    for (int k = 0; k < LP; ++k) {
+        const int l = k / g.P;
+        kw[k] = g.lw[l];
+        kh[k] = g.lh[l];
+        kwf[k] = (float)kw[k];
+        khf[k] = (float)kh[k];
+        koff[k] = (unsigned)g.ls[l] * rowbytes;
+    }
+
+    const int team = g.D / VEC;  // power of two, <= 32
+    const int tshift = 31 - __clz(team);
+    const int lane_t = threadIdx.x & (team - 1);
+    const int tix = threadIdx.x >> tshift;
+    const int nteams = blockDim.x >> tshift;
+    const unsigned slab_base = (unsigned)__cvta_generic_to_shared(smem) + lane_t * 16u;
+    const int hd = g.H * g.D;
+
+    for (int t = 0; t < ntiles; ++t) {
+        const int qa = q0 + t * sp.tq;
+        const int nq = min(sp.tq, q1 - qa);
+        if (t + 1 < ntiles) {
+            const int qn = qa + sp.tq;
+            issue_tile<TW, LP>(loc, attn, (t & 1) ? sloc0 : sloc1, (t & 1) ? sattn0 : sattn1, g, b, h0, hsub, qn,
+                               min(sp.tq, q1 - qn), sp.gl, sp.ga);
+            cp_async_commit();
+            cp_async_wait_one();
+        } else {
+            cp_async_wait_all();
+        }
+        __syncthreads();
+        const float2 *tl = reinterpret_cast<const float2 *>((t & 1) ? sloc1 : sloc0);
+        const TW *ta = (t & 1) ? sattn1 : sattn0;
+        TO *otile = out + ((size_t)b * g.Lq + qa) * hd + (size_t)h0 * g.D + lane_t * VEC;
+        const int items = nq << hshift;
+        for (int it = tix; it < items; it += nteams) {
+            const int qi = it >> hshift, hs = it & (hsub - 1);
+            const float2 *lp = tl + it * LP;
+            const TW *ap = ta + it * LP;
+            const unsigned hbase = slab_base + (unsigned)hs * (unsigned)sp.slab_bytes;
+            Acc acc;
+            acc.zero();
+            bool finite = true;
+#pragma unroll
+            for (int k = 0; k < LP; ++k) {
+                const float2 xy = lp[k];
+                const FlatTaps tp = flat_taps(xy.x, xy.y, to_f32(ap[k]), kwf[k], khf[k], kw[k], kh[k]);
+                finite = finite && tp.ok;
+                const unsigned lbase = hbase + koff[k];
+                uint4 r00, r10, r01, r11;
+                asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(r00.x), "=r"(r00.y), "=r"(r00.z), "=r"(r00.w) : "r"(lbase + tp.p00 * rowbytes));
+                asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(r10.x), "=r"(r10.y), "=r"(r10.z), "=r"(r10.w) : "r"(lbase + tp.p10 * rowbytes));
+                asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(r01.x), "=r"(r01.y), "=r"(r01.z), "=r"(r01.w) : "r"(lbase + tp.p01 * rowbytes));
+                asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(r11.x), "=r"(r11.y), "=r"(r11.z), "=r"(r11.w) : "r"(lbase + tp.p11 * rowbytes));
+                acc.add(tp.c00, r00);
+                acc.add(tp.c10, r10);
+                acc.add(tp.c01, r01);
+                acc.add(tp.c11, r11);
+            }
+            if (!finite) acc.poison();
+            float o[VEC];
+            acc.to_float(o);
+            store_vec<TO, VEC>(otile + (unsigned)(qi * hd + hs * g.D), o);
+        }
+        __syncthreads();
+    }
+}
+
+// Plans the slab path; returns false when its preconditions do not hold.
+template <typename TV, typename TW>
+bool plan_forward_slab(const Geom &g, const void *value, const float *loc, const void *attn, const void *out,
+                       int optin, SlabPlan &sp) {
+    const int es = (int)sizeof(TV), esw = (int)sizeof(TW);
+    const int LP = g.L * g.P;
+    if (!(LP == 1 || LP == 2 || LP == 4 || LP == 8)) return false;
+    if ((g.D * es) % 16 != 0) return false;
+    const int team = g.D * es / 16;
+    if (team > 32 || (team & (team - 1))) return false;
+    if (!aligned(value, 16) || !aligned(out, 16)) return false;
+    const size_t slab = (size_t)g.Lv * g.D * es;
+    if (slab % 16 != 0) return false;
+    const Tune tune = read_tune("RFDETR_MSDA_SLAB_FWD");
+    if (tune.stage == 0) return false;
+    const size_t budget = 100 * 1024;
+    int best = 0;
+    for (int hsub = 1; hsub <= g.H && hsub <= 32; hsub *= 2) {
+        if (g.H % hsub) break;
+        if ((size_t)hsub * slab > budget) break;
+        best = hsub;
+        if ((size_t)hsub * slab * 2 > 80 * 1024) break;  // stop growing once the group is ~40 KB
+    }
+    if (tune.hsub > 0) best = tune.hsub;
+    if (best == 0 || g.H % best) return false;
+    sp.hsub = best;
+    // Granules for the location / weight segments of one (query, head group).
+    auto granule = [](long long seg_bytes, long long row_stride_bytes, long long head_off_bytes,
+                      const void *base) -> int {
+        for (int gsz = 16; gsz >= 4; gsz >>= 1) {
+            if (seg_bytes % gsz == 0 && row_stride_bytes % gsz == 0 && head_off_bytes % gsz == 0 && aligned(base, gsz))
+                return gsz;
+        }
+        return 0;
+    };
+    const long long lseg = (long long)sp.hsub * LP * 8, aseg = (long long)sp.hsub * LP * esw;
+    sp.gl = granule(lseg, (long long)g.H * LP * 8, lseg, loc);
+    sp.ga = granule(aseg, (long long)g.H * LP * esw, aseg, attn);
+    if (!sp.gl || !sp.ga) return false;
+    sp.tq = tune.threads > 0 ? tune.threads : 128;  // overloads the threads field as tile queries
+    sp.slab_bytes = slab;
+    const size_t lbytes = (size_t)sp.tq * sp.hsub * LP * 8;
+    const size_t abytes = (((size_t)sp.tq * sp.hsub * LP * esw) + 15) & ~(size_t)15;
+    sp.tile_bytes = lbytes + abytes;
+    sp.smem = ((slab * sp.hsub + 15) & ~(size_t)15) + 2 * sp.tile_bytes;
+    if (sp.smem > (size_t)optin) return false;
+    return true;
+}
+
+template <typename TV, typename TW, int LP>
+int launch_forward_slab(const Geom &g, SlabPlan &sp, const void *value, const float *loc, const void *attn,
+                        void *out, cudaStream_t stream, int waves) {
+    auto kernel = msda_forward_slab_kernel<TV, TW, LP>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp.smem) != cudaSuccess)
+        return RFDETR_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kSlabThreads, sp.smem) != cudaSuccess)
+        return RFDETR_ERR_CUDA;
+    per_sm = std::max(per_sm, 1);
+    const long long groups = (long long)g.B * (g.H / sp.hsub);
+    const long long target = (long long)num_sms() * per_sm * std::max(waves, 1);
+    long long per_group = std::max<long long>(1, target / std::max<long long>(groups, 1));
+    long long qpc = (g.Lq + per_group - 1) / per_group;
+    qpc = ((qpc + sp.tq - 1) / sp.tq) * sp.tq;
+    sp.q_per_cta = (int)std::max<long long>(qpc, sp.tq);
+    if (groups > 65535) return RFDETR_ERR_SHAPE;
+    dim3 grid((unsigned)ceil_div(g.Lq, sp.q_per_cta), (unsigned)groups);
+    kernel<<<grid, kSlabThreads, sp.smem, stream>>>(static_cast<const TV *>(value), loc, static_cast<const TW *>(attn),
+                                                    static_cast<typename OutOf<TV, TW>::T *>(out), g, sp);
+    return launch_status();
+}
+
+// Returns -1 when the slab path does not apply.
+template <typename TV, typename TW>
+int try_forward_slab(const Geom &g, const void *value, const float *loc, const void *attn, void *out,
+                     cudaStream_t stream) {
+    SlabPlan sp;
+    if (!plan_forward_slab<TV, TW>(g, value, loc, attn, out, max_smem_optin(), sp)) return -1;
+    const int waves = std::max(1, read_tune("RFDETR_MSDA_SLAB_FWD").waves);
+    switch (g.L * g.P) {
+        case 1: return launch_forward_slab<TV, TW, 1>(g, sp, value, loc, attn, out, stream, waves);
+        case 2: return launch_forward_slab<TV, TW, 2>(g, sp, value, loc, attn, out, stream, waves);
+        case 4: return launch_forward_slab<TV, TW, 4>(g, sp, value, loc, attn, out, stream, waves);
+        case 8: return launch_forward_slab<TV, TW, 8>(g, sp, value, loc, attn, out, stream, waves);
+        default: return -1;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Slab-resident backward for bf16 values ("owner computes").  One CTA owns the value rows of
+// one (image, head) and all its queries, processed in chunks of `tq` queries:
+//   P1: each team handles one (query) item: it reads the 4 corner rows of every sample from the
+//       shared-memory slab, forms the corner dot products G_c = g . v_c, reduces them across the
+//       team and writes grad_weight and grad_location; then it files one record
+//       (coefficient a*w_c, item) per in-bounds corner into the bin of that value position
+//       (an integer shared-memory atomic hands out the slot).
+//   P2: the owner of each (position, 8-channel chunk) walks its bin and accumulates
+//       coefficient x grad_output row chunk in registers.
+// Bins hold `cap` records; a record that finds its bin full is added directly into a float32
+// shared-memory overflow slab instead (slow but exact).  After the last chunk each owner adds its
+// overflow entries and writes its grad_value chunk once, rounded to bf16: no workspace, no
+// atomics on the value gradient in the common case, no second pass.
+// ------------------------------------------------------------------------------------------
+constexpr int kBinThreads = 512;
+
+struct BinPlan {
+    int tq, cap, gl, ga, gg;  // tile queries, bin capacity, granule bytes of loc / attn / grad_out
+    size_t slab_bytes, smem;
+};
+
+template <typename TW, typename TG, int LP>
+__device__ __forceinline__ void issue_bwd_tile(const float *loc, const TW *attn, const TG *gout, float *sloc, TW *sattn,
+                                               TG *sg, const Geom &g, int b, int h, int qa, int nq, int gl, int ga,
+                                               int gg) {
+    const int lbytes = LP * 8, abytes = LP * (int)sizeof(TW), gbytes = g.D * (int)sizeof(TG);
+    const int ls = 31 - __clz(lbytes / gl), as = 31 - __clz(abytes / ga), gs = 31 - __clz(gbytes / gg);
+    const size_t row0 = ((size_t)b * g.Lq + qa) * g.H + h;
+    const size_t rstride = (size_t)g.H;
+    for (int i = threadIdx.x; i < (nq << ls); i += blockDim.x) {
+        const int qi = i >> ls, j = i & ((1 << ls) - 1);
+        cp_async_bytes(reinterpret_cast<char *>(sloc) + (size_t)qi * lbytes + j * gl,
+                       reinterpret_cast<const char *>(loc + (row0 + qi * rstride) * LP * 2) + j * gl, gl);
+    }
+    for (int i = threadIdx.x; i < (nq << as); i += blockDim.x) {
+        const int qi = i >> as, j = i & ((1 << as) - 1);
+        cp_async_bytes(reinterpret_cast<char *>(sattn) + (size_t)qi * abytes + j * ga,
+                       reinterpret_cast<const char *>(attn + (row0 + qi * rstride) * LP) + j * ga, ga);
+    }
+    for (int i = threadIdx.x; i < (nq << gs); i += blockDim.x) {
+        const int qi = i >> gs, j = i & ((1 << gs) - 1);
+        cp_async_bytes(reinterpret_cast<char *>(sg) + (size_t)qi * gbytes + j * gg,
+                       reinterpret_cast<const char *>(gout + (row0 + qi * rstride) * g.D) + j * gg, gg);
+    }
+}
+
+// Dot of 8 bf16 value channels with 8 float gradient channels (packed pairs).
+__device__ __forceinline__ float dot8(const uint4 &v, const float2 *gp) {
+    float2 s = __fmul2_rn(bf16x2_lo_hi(v.x), gp[0]);
+    s = __ffma2_rn(bf16x2_lo_hi(v.y), gp[1], s);
+    s = __ffma2_rn(bf16x2_lo_hi(v.z), gp[2], s);
+    s = __ffma2_rn(bf16x2_lo_hi(v.w), gp[3], s);
+    return s.x + s.y;
+}
+
+template <typename TG>
+__device__ __forceinline__ void load_g8(unsigned saddr, float2 *gp) {
+    if constexpr (sizeof(TG) == 2) {
+        uint4 r;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(saddr));
+        gp[0] = bf16x2_lo_hi(r.x);
+        gp[1] = bf16x2_lo_hi(r.y);
+        gp[2] = bf16x2_lo_hi(r.z);
+        gp[3] = bf16x2_lo_hi(r.w);
+    } else {
+        float4 a, c;
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(a.x), "=f"(a.y), "=f"(a.z), "=f"(a.w) : "r"(saddr));
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(c.x), "=f"(c.y), "=f"(c.z), "=f"(c.w) : "r"(saddr + 16));
+        gp[0] = make_float2(a.x, a.y);
+        gp[1] = make_float2(a.z, a.w);
+        gp[2] = make_float2(c.x, c.y);
+        gp[3] = make_float2(c.z, c.w);
+    }
+}
+
+__device__ __forceinline__ uint4 lds128(unsigned addr) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
+    return r;
+}
+
+template <typename TW, int LP, int OWN>
+__global__ void __launch_bounds__(kBinThreads, 1)
+msda_backward_bins_kernel(const bf16 *__restrict__ value, const float *__restrict__ loc, const TW *__restrict__ attn,
+                          const typename OutOf<bf16, TW>::T *__restrict__ grad_out, bf16 *__restrict__ grad_value,
+                          float *__restrict__ grad_loc, TW *__restrict__ grad_attn, const Geom g, const BinPlan bp) {
+    using TG = typename OutOf<bf16, TW>::T;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int bh = blockIdx.x;  // b * H + h
+    const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
+    const int Lv = g.Lv, D = g.D;
+    const unsigned rowbytes = (unsigned)(D * 2);
+    const int chunks = D / 8;  // 8-channel chunks per row == team size
+
+    // Shared-memory layout.
+    unsigned char *p = smem;
+    unsigned char *slab = p;
+    p += (bp.slab_bytes + 15) & ~(size_t)15;
+    const size_t lbytes = (size_t)bp.tq * LP * 8;
+    const size_t abytes = ((size_t)bp.tq * LP * sizeof(TW) + 15) & ~(size_t)15;
+    const size_t gbytes = (size_t)bp.tq * D * sizeof(TG);
+    float *const sloc0 = reinterpret_cast<float *>(p);
+    TW *const sattn0 = reinterpret_cast<TW *>(p + lbytes);
+    TG *const sg0 = reinterpret_cast<TG *>(p + lbytes + abytes);
+    p += lbytes + abytes + gbytes;
+    float *const sloc1 = reinterpret_cast<float *>(p);
+    TW *const sattn1 = reinterpret_cast<TW *>(p + lbytes);
+    TG *const sg1 = reinterpret_cast<TG *>(p + lbytes + abytes);
+    p += lbytes + abytes + gbytes;
+    uint2 *bins = reinterpret_cast<uint2 *>(p);
+    p += (size_t)Lv * bp.cap * sizeof(uint2);
+    int *counts = reinterpret_cast<int *>(p);
+    p += ((size_t)Lv * sizeof(int) + 15) & ~(size_t)15;
+    float *ovf = reinterpret_cast<float *>(p);
+
+    // Stage the slab, clear counts and the overflow slab.
+    const bf16 *vsrc = value + (size_t)bh * Lv * D;
+    const int n16 = (int)(bp.slab_bytes / 16);
+    for (int i = threadIdx.x; i < n16; i += blockDim.x)
+        cp_async_bytes(slab + (size_t)i * 16, reinterpret_cast<const char *>(vsrc) + (size_t)i * 16, 16);
+    for (int i = threadIdx.x; i < Lv; i += blockDim.x) counts[i] = 0;
+    for (int i = threadIdx.x; i < Lv * D; i += blockDim.x) ovf[i] = 0.f;
+    const int ntiles = (g.Lq + bp.tq - 1) / bp.tq;
+    if (ntiles > 0)
+        issue_bwd_tile<TW, TG, LP>(loc, attn, grad_out, sloc0, sattn0, sg0, g, b, h, 0, min(bp.tq, g.Lq), bp.gl,
+                                   bp.ga, bp.gg);
+    cp_async_commit();
+
+    int kw[LP], kh[LP];
+    float kwf[LP], khf[LP];
+    unsigned koff[LP], kpos[LP];
+#pragma unroll
+    for (int k = 0; k < LP; ++k) {
+        const int l = k / g.P;
+        kw[k] = g.lw[l];
+        kh[k] = g.lh[l];
+        kwf[k] = (float)kw[k];
+        khf[k] = (float)kh[k];
+        kpos[k] = (unsigned)g.ls[l];
+        koff[k] = kpos[k] * rowbytes;
+    }
+    const int team = chunks;
+    const int tshift = 31 - __clz(team);
+    const int lane_t = threadIdx.x & (team - 1);
+    const int tix = threadIdx.x >> tshift;
+    const int nteams = blockDim.x >> tshift;
+    const unsigned slab_s = (unsigned)__cvta_generic_to_shared(slab) + lane_t * 16u;
+    const float qnan = __int_as_float(0x7fc00000);
+
+    // Owner accumulators: owner-lane o = position * chunks + chunk, o = threadIdx.x + j * blockDim.
+    float2 acc[OWN][4];
+#pragma unroll
+    for (int j = 0; j < OWN; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[j][i] = make_float2(0.f, 0.f);
+    const int owners = Lv * chunks;
+
+    for (int t = 0; t < ntiles; ++t) {
+        const int qa = t * bp.tq;
+        const int nq = min(bp.tq, g.Lq - qa);
+        if (t + 1 < ntiles) {
+            const int qn = qa + bp.tq;
+            const bool odd = (t & 1) != 0;
+            issue_bwd_tile<TW, TG, LP>(loc, attn, grad_out, odd ? sloc0 : sloc1, odd ? sattn0 : sattn1, odd ? sg0 : sg1,
+                                       g, b, h, qn, min(bp.tq, g.Lq - qn), bp.gl, bp.ga, bp.gg);
+            cp_async_commit();
+            cp_async_wait_one();
+        } else {
+            cp_async_wait_all();
+        }
+        __syncthreads();
+        const bool odd = (t & 1) != 0;
+        const float2 *tl = reinterpret_cast<const float2 *>(odd ? sloc1 : sloc0);
+        const TW *ta = odd ? sattn1 : sattn0;
+        const TG *tg = odd ? sg1 : sg0;
+        const unsigned tg_s = (unsigned)__cvta_generic_to_shared(tg);
+
+        // P1: one item (query) per team; every lane of a warp runs the same trip count.
+        for (int base = 0; base < nq; base += nteams) {
+            const int it = base + tix;
+            const bool live = it < nq;
+            const int iq = live ? it : 0;
+            float2 gp[4];
+            load_g8<TG>(tg_s + (unsigned)(iq * D * (int)sizeof(TG)) + lane_t * 8u * (unsigned)sizeof(TG), gp);
+            const size_t row = ((size_t)b * g.Lq + qa + iq) * g.H + h;
+#pragma unroll
+            for (int k = 0; k < LP; ++k) {
+                const float2 xy = tl[iq * LP + k];
+                const float a = to_f32(ta[iq * LP + k]);
+                const int W = kw[k];
+                float ix, iy;
+                sample_coords(xy.x, xy.y, kwf[k], khf[k], ix, iy);
+                const bool ok = fabsf(ix) <= 3.0e38f && fabsf(iy) <= 3.0e38f;
+                const Axis ax = axis_taps(ix, kwf[k], W), ay = axis_taps(iy, khf[k], kh[k]);
+                const float wx0 = ax.w0, wx1 = ax.w1, wy0 = ay.w0, wy1 = ay.w1;
+                const float mx0 = ax.m0, mx1 = ax.m1, my0 = ay.m0, my1 = ay.m1;
+                const int p00 = ay.c0 * W + ax.c0, p10 = ay.c0 * W + ax.c1;
+                const int p01 = ay.c1 * W + ax.c0, p11 = ay.c1 * W + ax.c1;
+                const unsigned lb = slab_s + koff[k];
+                float G00 = dot8(lds128(lb + p00 * rowbytes), gp);
+                float G10 = dot8(lds128(lb + p10 * rowbytes), gp);
+                float G01 = dot8(lds128(lb + p01 * rowbytes), gp);
+                float G11 = dot8(lds128(lb + p11 * rowbytes), gp);
+                for (int o = team >> 1; o > 0; o >>= 1) {
+                    G00 += __shfl_xor_sync(0xffffffffu, G00, o);
+                    G10 += __shfl_xor_sync(0xffffffffu, G10, o);
+                    G01 += __shfl_xor_sync(0xffffffffu, G01, o);
+                    G11 += __shfl_xor_sync(0xffffffffu, G11, o);
+                }
+                // Masked corner terms (out-of-range corners contribute nothing).
+                const float m00 = mx0 * my0, m10 = mx1 * my0, m01 = mx0 * my1, m11 = mx1 * my1;
+                const float e00 = m00 * G00, e10 = m10 * G10, e01 = m01 * G01, e11 = m11 * G11;
+                if (live && lane_t == 0) {
+                    const float ds = wy0 * (wx0 * e00 + wx1 * e10) + wy1 * (wx0 * e01 + wx1 * e11);
+                    const float dx = wy0 * (e10 - e00) + wy1 * (e11 - e01);
+                    const float dy = wx0 * (e01 - e00) + wx1 * (e11 - e10);
+                    const size_t s_idx = row * LP + k;
+                    grad_attn[s_idx] = from_f32<TW>(ok ? ds : qnan);
+                    float2 gl;
+                    gl.x = ok ? kwf[k] * (a * dx) : qnan;
+                    gl.y = ok ? khf[k] * (a * dy) : qnan;
+                    reinterpret_cast<float2 *>(grad_loc)[s_idx] = gl;
+                }
+                if (live && ok) {
+                    // File the in-bounds corners: corner c is filed by lane (c mod team).
+                    const float ax0 = a * wx0, ax1 = a * wx1;
+                    const float cf[4] = {ax0 * wy0 * m00, ax1 * wy0 * m10, ax0 * wy1 * m01, ax1 * wy1 * m11};
+                    const int pp[4] = {p00, p10, p01, p11};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        if ((c & (team - 1)) != lane_t || cf[c] == 0.f) continue;
+                        const int pos = (int)kpos[k] + pp[c];
+                        const int slot = atomicAdd(&counts[pos], 1);
+                        if (slot < bp.cap) {
+                            bins[(size_t)pos * bp.cap + slot] = make_uint2(__float_as_uint(cf[c]), (unsigned)iq);
+                        } else {
+                            const TG *grow = tg + (size_t)iq * D;
+                            for (int d = 0; d < D; ++d) atomicAdd(&ovf[(size_t)pos * D + d], cf[c] * to_f32(grow[d]));
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();
+
+        // P2: owners walk their bins.
+#pragma unroll
+        for (int j = 0; j < OWN; ++j) {
+            const int o = threadIdx.x + j * blockDim.x;
+            if (o < owners) {
+                const int pos = o >> tshift, ch = o & (chunks - 1);
+                const int n = min(counts[pos], bp.cap);
+                const uint2 *bin = bins + (size_t)pos * bp.cap;
+                for (int e = 0; e < n; ++e) {
+                    const uint2 rec = bin[e];
+                    const float c = __uint_as_float(rec.x);
+                    float2 gq[4];
+                    load_g8<TG>(tg_s + (rec.y * (unsigned)D + ch * 8u) * (unsigned)sizeof(TG), gq);
+                    const float2 cc = make_float2(c, c);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[j][i] = __ffma2_rn(cc, gq[i], acc[j][i]);
+                }
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < Lv; i += blockDim.x) counts[i] = 0;
+    }
+    __syncthreads();
+
+    // Owners add the overflow slab and write their grad_value chunk once.
+#pragma unroll
+    for (int j = 0; j < OWN; ++j) {
+        const int o = threadIdx.x + j * blockDim.x;
+        if (o < owners) {
+            const int pos = o >> tshift, ch = o & (chunks - 1);
+            const float *ov = ovf + (size_t)pos * D + ch * 8;
+            float f[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                f[2 * i] = acc[j][i].x + ov[2 * i];
+                f[2 * i + 1] = acc[j][i].y + ov[2 * i + 1];
+            }
+            store_vec<bf16, 8>(grad_value + ((size_t)bh * Lv + pos) * D + ch * 8, f);
+        }
+    }
+}
+
+template <typename TW>
+bool plan_backward_bins(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
+                        const void *grad_value, int optin, BinPlan &bp, int &own) {
+    using TG = typename OutOf<bf16, TW>::T;
+    const int LP = g.L * g.P;
+    if (!(LP == 1 || LP == 2 || LP == 4 || LP == 8)) return false;
+    if (g.D % 8 != 0 || g.D / 8 > 32 || ((g.D / 8) & (g.D / 8 - 1))) return false;
+    if (!aligned(value, 16) || !aligned(grad_value, 16)) return false;
+    const Tune tune = read_tune("RFDETR_MSDA_BINS");
+    if (tune.stage == 0) return false;
+    bp.slab_bytes = (size_t)g.Lv * g.D * 2;
+    const int chunks = g.D / 8;
+    own = (g.Lv * chunks + kBinThreads - 1) / kBinThreads;
+    if (own > 4) return false;
+    auto granule = [](long long seg, long long stride, const void *base) -> int {
+        for (int gsz = 16; gsz >= 4; gsz >>= 1)
+            if (seg % gsz == 0 && stride % gsz == 0 && aligned(base, gsz)) return gsz;
+        return 0;
+    };
+    bp.gl = granule((long long)LP * 8, (long long)LP * 8, loc);
+    bp.ga = granule((long long)LP * sizeof(TW), (long long)LP * sizeof(TW), attn);
+    bp.gg = granule((long long)g.D * sizeof(TG), (long long)g.D * sizeof(TG), gout);
+    if (!bp.gl || !bp.ga || !bp.gg) return false;
+    bp.tq = tune.threads > 0 ? tune.threads : 512;
+    bp.cap = tune.hsub > 0 ? tune.hsub : 24;
+    const size_t lbytes = (size_t)bp.tq * LP * 8;
+    const size_t abytes = ((size_t)bp.tq * LP * sizeof(TW) + 15) & ~(size_t)15;
+    const size_t gbytes = (size_t)bp.tq * g.D * sizeof(TG);
+    bp.smem = ((bp.slab_bytes + 15) & ~(size_t)15) + 2 * (lbytes + abytes + gbytes) +
+              (size_t)g.Lv * bp.cap * 8 + (((size_t)g.Lv * 4 + 15) & ~(size_t)15) + (size_t)g.Lv * g.D * 4;
+    return bp.smem <= (size_t)optin;
+}
+
+template <typename TW, int LP, int OWN>
+int launch_backward_bins(const Geom &g, const BinPlan &bp, const void *value, const float *loc, const void *attn,
+                         const void *gout, void *gv, float *gl, void *ga, cudaStream_t stream) {
+    auto kernel = msda_backward_bins_kernel<TW, LP, OWN>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bp.smem) != cudaSuccess)
+        return RFDETR_ERR_CUDA;
+    kernel<<<(unsigned)(g.B * g.H), kBinThreads, bp.smem, stream>>>(
+        static_cast<const bf16 *>(value), loc, static_cast<const TW *>(attn),
+        static_cast<const typename OutOf<bf16, TW>::T *>(gout), static_cast<bf16 *>(gv), gl, static_cast<TW *>(ga), g,
+        bp);
+    return launch_status();
+}
+
+template <typename TW, int LP>
+int dispatch_bins_own(const Geom &g, const BinPlan &bp, int own, const void *value, const float *loc, const void *attn,
+                      const void *gout, void *gv, float *gl, void *ga, cudaStream_t s) {
+    switch (own) {
+        case 1: return launch_backward_bins<TW, LP, 1>(g, bp, value, loc, attn, gout, gv, gl, ga, s);
+        case 2: return launch_backward_bins<TW, LP, 2>(g, bp, value, loc, attn, gout, gv, gl, ga, s);
+        case 3: return launch_backward_bins<TW, LP, 3>(g, bp, value, loc, attn, gout, gv, gl, ga, s);
+        case 4: return launch_backward_bins<TW, LP, 4>(g, bp, value, loc, attn, gout, gv, gl, ga, s);
+        default: return -1;
+    }
+}
+
+// bf16 values only; returns -1 when the bins path does not apply.
+template <typename TW>
+int try_backward_bins(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout, void *gv,
+                      float *gl, void *ga, cudaStream_t s) {
+    BinPlan bp;
+    int own = 0;
+    if (g.B * g.H > 2147483647 / 1 || !plan_backward_bins<TW>(g, value, loc, attn, gout, gv, max_smem_optin(), bp, own))
+        return -1;
+    switch (g.L * g.P) {
+        case 1: return dispatch_bins_own<TW, 1>(g, bp, own, value, loc, attn, gout, gv, gl, ga, s);
+        case 2: return dispatch_bins_own<TW, 2>(g, bp, own, value, loc, attn, gout, gv, gl, ga, s);
+        case 4: return dispatch_bins_own<TW, 4>(g, bp, own, value, loc, attn, gout, gv, gl, ga, s);
+        case 8: return dispatch_bins_own<TW, 8>(g, bp, own, value, loc, attn, gout, gv, gl, ga, s);
+        default: return -1;
+    }
+}
+
 }  // namespace
 }  // namespace rfdetr
 
@@ -655,6 +1388,19 @@ extern "C" int rfdetr_msda_forward(void *stream, const void *value, int value_dt
     if (!value || !sampling_locations || !attention_weights || !output) return RFDETR_ERR_SHAPE;
     const int vs = dtype_size(value_dtype), ws = dtype_size(weight_dtype), os = dtype_size(output_dtype);
     if (!aligned(sampling_locations, 8) || !aligned(attention_weights, ws)) return RFDETR_ERR_ALIGN;
+    {
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        int st2 = -1;
+        if (value_dtype == RFDETR_BF16 && weight_dtype == RFDETR_BF16)
+            st2 = try_forward_slab<bf16, bf16>(g, value, sampling_locations, attention_weights, output, s);
+        else if (value_dtype == RFDETR_BF16)
+            st2 = try_forward_slab<bf16, float>(g, value, sampling_locations, attention_weights, output, s);
+        else if (weight_dtype == RFDETR_BF16)
+            st2 = try_forward_slab<float, bf16>(g, value, sampling_locations, attention_weights, output, s);
+        else
+            st2 = try_forward_slab<float, float>(g, value, sampling_locations, attention_weights, output, s);
+        if (st2 >= 0) return st2;
+    }
     const void *ptrs[2] = {value, output};
     const int es[2] = {vs, os};
     Plan p;
@@ -707,6 +1453,17 @@ extern "C" int rfdetr_msda_backward(void *stream, const void *value, int value_d
     const int os = dtype_size(grad_output_dtype);
     const size_t nvalue = (size_t)g.B * g.H * g.Lv * g.D;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (value_dtype == RFDETR_BF16 && g.Lq > 0 && aligned(sampling_locations, 8) && aligned(grad_sampling_locations, 8) &&
+        aligned(attention_weights, ws) && aligned(grad_attention_weights, ws)) {
+        int st2 = -1;
+        if (weight_dtype == RFDETR_BF16)
+            st2 = try_backward_bins<bf16>(g, value, sampling_locations, attention_weights, grad_output, grad_value,
+                                          grad_sampling_locations, grad_attention_weights, s);
+        else
+            st2 = try_backward_bins<float>(g, value, sampling_locations, attention_weights, grad_output, grad_value,
+                                           grad_sampling_locations, grad_attention_weights, s);
+        if (st2 >= 0) return st2;
+    }
     if (value_dtype == RFDETR_BF16 && !aligned(grad_value, 16)) return RFDETR_ERR_ALIGN;
     if (value_dtype == RFDETR_F32 && !aligned(grad_value, 16)) return RFDETR_ERR_ALIGN;
     float *gacc;

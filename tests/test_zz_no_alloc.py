@@ -72,6 +72,47 @@ def test_noalloc_backward_matches_workspace_backward(pkg):
     assert_bf16_close(got[0][: 2 * H], ref[0], "oracle: grad_value")
 
 
+@pytest.mark.parametrize("weights_dtype", [torch.bfloat16, torch.float32])
+def test_noalloc_uses_its_static_scratch(pkg, weights_dtype):
+    """A shape served by the accumulate-in-scratch kernels (6 samples per head, 8 channels), so the
+    static array is what holds the float32 accumulator; two calls in a row."""
+    N = pkg._native
+    lib = N.lib()
+    dev = torch.device("cuda:0")
+    shapes = ((8, 16), (4, 8))
+    b, lq, h, p, d = 2, 70, 8, 3, 8
+    value, loc, attn, grad = sampler_inputs(23, b, lq, h, shapes, p, d, lo=-0.1, hi=1.1)
+    v = torch.tensor(value, device=dev).bfloat16()
+    l = torch.tensor(loc, device=dev)
+    a = torch.tensor(attn, device=dev).to(weights_dtype)
+    out_dtype = torch.bfloat16 if weights_dtype == torch.bfloat16 else torch.float32
+    g = torch.tensor(grad, device=dev).to(out_dtype)
+    flat = N.int64_array([8, 16, 4, 8])
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    lv = 8 * 16 + 4 * 8
+    wd = N.dtype_code(weights_dtype)
+    od = N.dtype_code(out_dtype)
+
+    gv, gl, ga = torch.empty_like(v), torch.empty_like(l), torch.empty_like(a)
+    ws_bytes = lib.rfdetr_msda_backward_workspace_size(N.BF16, b, h, d, lv)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    N.check(lib.rfdetr_msda_backward(stream, v.data_ptr(), N.BF16, flat, None, l.data_ptr(), a.data_ptr(), wd,
+                                     g.data_ptr(), od, gv.data_ptr(), gl.data_ptr(), ga.data_ptr(), ws.data_ptr(),
+                                     ws_bytes, b, h, d, lq, 2, p), "backward")
+    torch.cuda.synchronize()
+    want = [x.float().cpu().numpy() for x in (gv, gl, ga)]
+    for call in range(2):
+        nv, nl, na = torch.empty_like(v), torch.empty_like(l), torch.empty_like(a)
+        N.check(lib.rfdetr_msda_backward_noalloc(stream, v.data_ptr(), N.BF16, flat, None, l.data_ptr(), a.data_ptr(),
+                                                 wd, g.data_ptr(), od, nv.data_ptr(), nl.data_ptr(), na.data_ptr(), b,
+                                                 h, d, lq, 2, p), f"backward_noalloc call {call}")
+        torch.cuda.synchronize()
+        got = [x.float().cpu().numpy() for x in (nv, nl, na)]
+        assert_bf16_close(got[0], want[0], f"call {call}: grad_value")
+        assert_bf16_close(got[1], want[1], f"call {call}: grad_loc")
+        assert_bf16_close(got[2], want[2], f"call {call}: grad_attn")
+
+
 def test_noalloc_refuses_problems_beyond_its_scratch(pkg):
     N = pkg._native
     lib = N.lib()
