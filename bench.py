@@ -390,7 +390,7 @@ def run_ours(args):
                    "l2": f"ring of {ring} input/output sets ({ring * per_set / 2**20:.0f} MiB) > L2, no flush",
                    "timing": f"median of {reps_step} timed regions of exactly {args.steps} steps, "
                              "one CUDA-graph replay per step"},
-        "roofline": {"bound": "hbm", "kernel": "msda_backward_bins_kernel", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": "msda_backward_owner_kernel", "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "peak_source": peak_src, "algorithmic_bytes": bwd_bytes, "ms_per_launch": ms_bwd},
         "kernels": {"msda_forward": {"ms": ms_fwd, "GB/s": fwd_bytes / (ms_fwd * 1e-3) / 1e9,

@@ -1028,8 +1028,9 @@ struct BinPlan {
 template <typename TW, typename TG, int LP>
 __device__ __forceinline__ void issue_bwd_tile(const float *loc, const TW *attn, const TG *gout, float *sloc, TW *sattn,
                                                TG *sg, const Geom &g, int b, int h, int qa, int nq, int gl, int ga,
-                                               int gg) {
+                                               int gg, int gstride = 0) {
     const int lbytes = LP * 8, abytes = LP * (int)sizeof(TW), gbytes = g.D * (int)sizeof(TG);
+    const int gdst = gstride > 0 ? gstride : gbytes;
     const int ls = 31 - __clz(lbytes / gl), as = 31 - __clz(abytes / ga), gs = 31 - __clz(gbytes / gg);
     const size_t row0 = ((size_t)b * g.Lq + qa) * g.H + h;
     const size_t rstride = (size_t)g.H;
@@ -1045,7 +1046,7 @@ __device__ __forceinline__ void issue_bwd_tile(const float *loc, const TW *attn,
     }
     for (int i = threadIdx.x; i < (nq << gs); i += blockDim.x) {
         const int qi = i >> gs, j = i & ((1 << gs) - 1);
-        cp_async_bytes(reinterpret_cast<char *>(sg) + (size_t)qi * gbytes + j * gg,
+        cp_async_bytes(reinterpret_cast<char *>(sg) + (size_t)qi * gdst + j * gg,
                        reinterpret_cast<const char *>(gout + (row0 + qi * rstride) * g.D) + j * gg, gg);
     }
 }
@@ -1366,6 +1367,401 @@ int try_backward_bins(const Geom &g, const void *value, const float *loc, const 
     }
 }
 
+// ------------------------------------------------------------------------------------------
+// Backward for bf16 values, "owner computes" variant.  Every (position, 16-channel segment) of
+// an (image, head) slab has one owner thread that keeps that value row in registers (float32)
+// and its float32 value-gradient accumulator in registers for the whole launch.  Per tile of
+// queries:
+//   file   -- one thread per sample derives its four corners (clipped positions, masked
+//             coefficients) and files a record {coefficient, sample*4 + corner} for each
+//             in-range corner in the position's bin (slot from an integer shared-memory atomic);
+//   own    -- each owner walks its bin: acc += coef * g[query] and G = <value[pos], g[query]>,
+//             the corner's dot product, which it writes back to the record's sample slot;
+//   finish -- one thread per sample folds its four corner dots into the weight and location
+//             gradients (the sample's taps are recomputed from the staged locations).
+// No thread gathers value rows, no float atomics are used, and grad_value is written once.
+// "finish" of tile t runs in the same phase as "file" of tile t+1, so a tile costs two block
+// barriers; tiles are prefetched two ahead with cp.async.  A bin that fills up is drained by
+// repeating file/own for the corners that did not fit (bounded by the largest bin), so any
+// sampling pattern is handled exactly.
+// Out-of-range corners carry weight 0 (ops.py:123-128): they add nothing to grad_value and
+// their m * G term is 0 unless the clipped value row or the gradient row holds a non-finite
+// entry, where the reference's product is NaN -- per-row flags reproduce exactly that.
+// One 576-thread CTA per slab (up to 576 owners: Lv * D/16 <= 576), one CTA per SM, so the
+// owner state stays in registers without spills and the bins hold 512-query tiles.
+// ------------------------------------------------------------------------------------------
+constexpr int kOwnMaxThreads = 576;
+
+struct OwnPlan {
+    int tq, cap, threads, gl, ga, gg;
+    unsigned o_loc, loc_sz, o_attn, attn_sz, o_gst, gst_sz, o_G, o_cnt, o_vbad, o_coef, o_idx;
+    size_t smem;
+};
+
+struct OwnTaps {
+    float wx0, wx1, wy0, wy1, m00, m10, m01, m11;
+    int p00, p10, p01, p11;
+    bool ok;
+};
+
+__device__ __forceinline__ OwnTaps own_taps(float2 xy, float Wf, float Hf, int W, int H) {
+    OwnTaps t;
+    float ix, iy;
+    sample_coords(xy.x, xy.y, Wf, Hf, ix, iy);
+    t.ok = fabsf(ix) <= 3.0e38f && fabsf(iy) <= 3.0e38f;
+    const Axis ax = axis_taps(ix, Wf, W), ay = axis_taps(iy, Hf, H);
+    t.wx0 = ax.w0;
+    t.wx1 = ax.w1;
+    t.wy0 = ay.w0;
+    t.wy1 = ay.w1;
+    t.m00 = ax.m0 * ay.m0;
+    t.m10 = ax.m1 * ay.m0;
+    t.m01 = ax.m0 * ay.m1;
+    t.m11 = ax.m1 * ay.m1;
+    t.p00 = ay.c0 * W + ax.c0;
+    t.p10 = ay.c0 * W + ax.c1;
+    t.p01 = ay.c1 * W + ax.c0;
+    t.p11 = ay.c1 * W + ax.c1;
+    return t;
+}
+
+// Coefficients of the four corners (attention weight x bilinear weight x mask) and whether a
+// corner is filed: in range, or carrying a non-finite coefficient (the reference's NaN).
+__device__ __forceinline__ void own_coefs(const OwnTaps &t, float a, float cf[4], bool filed[4]) {
+    const float ax0 = a * t.wx0, ax1 = a * t.wx1;
+    cf[0] = ax0 * t.wy0 * t.m00;
+    cf[1] = ax1 * t.wy0 * t.m10;
+    cf[2] = ax0 * t.wy1 * t.m01;
+    cf[3] = ax1 * t.wy1 * t.m11;
+    filed[0] = t.m00 != 0.f || cf[0] != 0.f;
+    filed[1] = t.m10 != 0.f || cf[1] != 0.f;
+    filed[2] = t.m01 != 0.f || cf[2] != 0.f;
+    filed[3] = t.m11 != 0.f || cf[3] != 0.f;
+}
+
+__device__ __forceinline__ float4 lds128f(unsigned addr) {
+    float4 r;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "r"(addr));
+    return r;
+}
+
+// True when any of the 2n floats is inf or NaN (x * 0 is NaN exactly for those).
+template <int N>
+__device__ __forceinline__ bool any_nonfinite(const float2 *x) {
+    const float2 z = make_float2(0.f, 0.f);
+    float2 s = __fmul2_rn(x[0], z);
+#pragma unroll
+    for (int i = 1; i < N; ++i) s = __ffma2_rn(x[i], z, s);
+    const float r = s.x + s.y;
+    return r != r;
+}
+
+template <typename TW, int LP, int SEG>
+__global__ void __launch_bounds__(kOwnMaxThreads, 1)
+msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restrict__ loc, const TW *__restrict__ attn,
+                           const typename OutOf<bf16, TW>::T *__restrict__ grad_out, bf16 *__restrict__ grad_value,
+                           float *__restrict__ grad_loc, TW *__restrict__ grad_attn, const Geom g, const OwnPlan op) {
+    using TG = typename OutOf<bf16, TW>::T;
+    constexpr int D = 16 * SEG;
+    constexpr int LPS = LP == 1 ? 0 : LP == 2 ? 1 : LP == 4 ? 2 : 3;
+    // Staged gradient rows are padded by 16 bytes so rows that differ in their low three bits
+    // start in different bank groups.
+    constexpr unsigned GSTRIDE = (unsigned)(D * sizeof(TG)) + 16u;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int lvl_i[LP][3];
+    __shared__ float lvl_f[LP][2];
+    const int bh = blockIdx.x;
+    const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
+    const int Lv = g.Lv, cap = op.cap;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int qbeg = 0, qend = g.Lq;
+    const float qnan = __int_as_float(0x7fc00000);
+
+    float *const sG = reinterpret_cast<float *>(smem + op.o_G);
+    int *const counts = reinterpret_cast<int *>(smem + op.o_cnt);
+    unsigned char *const vbad = smem + op.o_vbad;
+    float *const bcoef = reinterpret_cast<float *>(smem + op.o_coef);
+    unsigned short *const bidx = reinterpret_cast<unsigned short *>(smem + op.o_idx);
+    auto locb = [&](int i) { return reinterpret_cast<float2 *>(smem + op.o_loc + i * op.loc_sz); };
+    auto attnb = [&](int i) { return reinterpret_cast<TW *>(smem + op.o_attn + i * op.attn_sz); };
+    auto gstb = [&](int i) { return reinterpret_cast<TG *>(smem + op.o_gst + i * op.gst_sz); };
+
+    if (tid < LP) {
+        const int l = tid / g.P;
+        lvl_i[tid][0] = g.lw[l];
+        lvl_i[tid][1] = g.lh[l];
+        lvl_i[tid][2] = g.ls[l];
+        lvl_f[tid][0] = (float)g.lw[l];
+        lvl_f[tid][1] = (float)g.lh[l];
+    }
+    for (int i = tid; i < Lv; i += nthr) counts[i] = 0;
+    const int nqc = max(qend - qbeg, 0);
+    const int ntiles = (nqc + op.tq - 1) / op.tq;
+    auto issue = [&](int t) {
+        const int q0 = qbeg + t * op.tq;
+        issue_bwd_tile<TW, TG, LP>(loc, attn, grad_out, reinterpret_cast<float *>(locb(t % 3)), attnb(t % 3),
+                                   gstb(t % 3), g, b, h, q0, min(op.tq, qend - q0), op.gl, op.ga, op.gg, (int)GSTRIDE);
+    };
+    if (ntiles > 0) issue(0);
+    cp_async_commit();
+    if (ntiles > 1) issue(1);
+    cp_async_commit();
+
+    // Owner state: this thread's value row segment and accumulator.
+    const int owners = Lv * SEG;
+    const bool is_owner = tid < owners;
+    const int pos = tid / SEG, seg = tid & (SEG - 1);
+    float2 vv[8], acc[8];
+    if (is_owner) {
+        const uint4 *vp = reinterpret_cast<const uint4 *>(value + ((size_t)bh * Lv + pos) * D + seg * 16);
+        const uint4 r0 = __ldg(vp), r1 = __ldg(vp + 1);
+        vv[0] = bf16x2_lo_hi(r0.x); vv[1] = bf16x2_lo_hi(r0.y); vv[2] = bf16x2_lo_hi(r0.z); vv[3] = bf16x2_lo_hi(r0.w);
+        vv[4] = bf16x2_lo_hi(r1.x); vv[5] = bf16x2_lo_hi(r1.y); vv[6] = bf16x2_lo_hi(r1.z); vv[7] = bf16x2_lo_hi(r1.w);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vv[i] = make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
+    {
+        bool bad = any_nonfinite<8>(vv);
+        if constexpr (SEG > 1) bad |= __shfl_xor_sync(0xffffffffu, (int)bad, 1) != 0;
+        if (is_owner && seg == 0) vbad[pos] = bad ? 1 : 0;
+    }
+    cp_async_wait_one();
+    __syncthreads();
+
+    // Files the corners of sample s selected by `want` (bit c = corner c); returns those whose
+    // bin was full.
+    auto file = [&](const float2 *tl, const TW *ta, int s, unsigned want) -> unsigned {
+        const int k = s & (LP - 1);
+        const OwnTaps t = own_taps(tl[s], lvl_f[k][0], lvl_f[k][1], lvl_i[k][0], lvl_i[k][1]);
+        if (!t.ok) return 0u;
+        float cf[4];
+        bool filed[4];
+        own_coefs(t, to_f32(ta[s]), cf, filed);
+        const int base = lvl_i[k][2];
+        const int pp[4] = {base + t.p00, base + t.p10, base + t.p01, base + t.p11};
+        unsigned failed = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            if (!((want >> c) & 1u) || !filed[c]) continue;
+            const int slot = atomicAdd(&counts[pp[c]], 1);
+            if (slot < cap) {
+                bcoef[slot * Lv + pp[c]] = cf[c];
+                bidx[slot * Lv + pp[c]] = (unsigned short)(s * 4 + c);
+            } else {
+                failed |= 1u << c;
+            }
+        }
+        return failed;
+    };
+
+    // Owners drain their bins (and reset their counts for the next round).
+    auto own = [&](const TG *gs) {
+        const unsigned gs_s = (unsigned)__cvta_generic_to_shared(gs);
+        int n = 0;
+        if (is_owner) n = min(counts[pos], cap);
+        if constexpr (SEG > 1) __syncwarp();
+        if (is_owner && seg == 0) counts[pos] = 0;
+        const unsigned team = SEG > 1 ? (3u << ((tid & 31) & ~1)) : 0u;
+        const unsigned gseg = gs_s + (unsigned)seg * (16u * (unsigned)sizeof(TG));
+        for (int e = 0; e < n; ++e) {
+            const float c = bcoef[e * Lv + pos];
+            const unsigned idx = bidx[e * Lv + pos];
+            const unsigned ga = gseg + (idx >> (2 + LPS)) * GSTRIDE;
+            float2 q[8];
+            if constexpr (sizeof(TG) == 2) {
+                const uint4 u0 = lds128(ga), u1 = lds128(ga + 16u);
+                q[0] = bf16x2_lo_hi(u0.x); q[1] = bf16x2_lo_hi(u0.y); q[2] = bf16x2_lo_hi(u0.z); q[3] = bf16x2_lo_hi(u0.w);
+                q[4] = bf16x2_lo_hi(u1.x); q[5] = bf16x2_lo_hi(u1.y); q[6] = bf16x2_lo_hi(u1.z); q[7] = bf16x2_lo_hi(u1.w);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 f = lds128f(ga + 16u * i);
+                    q[2 * i] = make_float2(f.x, f.y);
+                    q[2 * i + 1] = make_float2(f.z, f.w);
+                }
+            }
+            const float2 cc = make_float2(c, c);
+            float2 d = __fmul2_rn(vv[0], q[0]);
+#pragma unroll
+            for (int i = 1; i < 8; ++i) d = __ffma2_rn(vv[i], q[i], d);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = __ffma2_rn(cc, q[i], acc[i]);
+            float dot = d.x + d.y;
+            if constexpr (SEG > 1) dot += __shfl_xor_sync(team, dot, 1);
+            if (seg == 0) sG[idx] = dot;
+        }
+    };
+
+    // Weight and location gradients of the samples of a drained tile.
+    auto finish = [&](int tb, int qa, int nq) {
+        const float2 *tl = locb(tb % 3);
+        const TW *ta = attnb(tb % 3);
+        const unsigned char *gsb = reinterpret_cast<const unsigned char *>(gstb(tb % 3));
+        for (int s = tid; s < nq * LP; s += nthr) {
+            const int k = s & (LP - 1), iq = s >> LPS;
+            const float Wf = lvl_f[k][0], Hf = lvl_f[k][1];
+            const OwnTaps t = own_taps(tl[s], Wf, Hf, lvl_i[k][0], lvl_i[k][1]);
+            const float a = to_f32(ta[s]);
+            float cf[4];
+            bool filed[4];
+            own_coefs(t, a, cf, filed);
+            const float4 G = *reinterpret_cast<const float4 *>(sG + 4 * s);
+            float e[4] = {t.m00 * G.x, t.m10 * G.y, t.m01 * G.z, t.m11 * G.w};
+            if (!(filed[0] && filed[1] && filed[2] && filed[3])) {
+                bool gbad = false;
+                for (int j = 0; j < D; ++j)
+                    gbad |= !(fabsf(to_f32(reinterpret_cast<const TG *>(gsb + iq * GSTRIDE)[j])) <= 3.4028235e38f);
+                const int base = lvl_i[k][2];
+                const int pp[4] = {base + t.p00, base + t.p10, base + t.p01, base + t.p11};
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (!filed[c]) e[c] = (gbad || vbad[pp[c]]) ? qnan : 0.f;
+            }
+            const float ds = t.wy0 * (t.wx0 * e[0] + t.wx1 * e[1]) + t.wy1 * (t.wx0 * e[2] + t.wx1 * e[3]);
+            const float dx = t.wy0 * (e[1] - e[0]) + t.wy1 * (e[3] - e[2]);
+            const float dy = t.wx0 * (e[2] - e[0]) + t.wx1 * (e[3] - e[1]);
+            const size_t s_idx = (((size_t)b * g.Lq + qa + iq) * g.H + h) * LP + k;
+            grad_attn[s_idx] = from_f32<TW>(t.ok ? ds : qnan);
+            float2 gl;
+            gl.x = t.ok ? Wf * (a * dx) : qnan;
+            gl.y = t.ok ? Hf * (a * dy) : qnan;
+            reinterpret_cast<float2 *>(grad_loc)[s_idx] = gl;
+        }
+    };
+
+    for (int t = 0; t < ntiles; ++t) {
+        const int qa = qbeg + t * op.tq;
+        const int nq = min(op.tq, qend - qa);
+        const float2 *tl = locb(t % 3);
+        const TW *ta = attnb(t % 3);
+        // Phase A: finish the previous tile, file this tile's corners.
+        if (t > 0) finish(t - 1, qa - op.tq, op.tq);
+        unsigned pending = 0;
+        {
+            int i = 0;
+            for (int s = tid; s < nq * LP; s += nthr, ++i) pending |= file(tl, ta, s, 0xFu) << (4 * i);
+        }
+        bool again = __syncthreads_or(pending != 0u);
+        // Phase B: prefetch two tiles ahead, drain the bins.
+        if (t + 2 < ntiles) issue(t + 2);
+        cp_async_commit();
+        own(gstb(t % 3));
+        for (int round = 0; again && round < 65536; ++round) {  // full bins: refile what did not fit
+            __syncthreads();
+            unsigned left = 0;
+            int i = 0;
+            for (int s = tid; s < nq * LP; s += nthr, ++i) {
+                const unsigned want = (pending >> (4 * i)) & 0xFu;
+                if (want) left |= file(tl, ta, s, want) << (4 * i);
+            }
+            pending = left;
+            again = __syncthreads_or(pending != 0u);
+            own(gstb(t % 3));
+        }
+        cp_async_wait_one();
+        __syncthreads();
+    }
+    if (ntiles > 0) {
+        const int t = ntiles - 1;
+        finish(t, qbeg + t * op.tq, qend - (qbeg + t * op.tq));
+    }
+
+    if (is_owner) {
+        float f[16];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            f[2 * j] = acc[j].x;
+            f[2 * j + 1] = acc[j].y;
+        }
+        store_vec<bf16, 16>(grad_value + ((size_t)bh * Lv + pos) * D + seg * 16, f);
+    }
+}
+
+template <typename TW>
+bool plan_backward_owner(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
+                         const void *grad_value, int optin, OwnPlan &op) {
+    using TG = typename OutOf<bf16, TW>::T;
+    const int LP = g.L * g.P;
+    if (!(LP == 1 || LP == 2 || LP == 4 || LP == 8)) return false;
+    if (g.D != 16 && g.D != 32) return false;
+    const int owners = g.Lv * (g.D / 16);
+    if (owners > kOwnMaxThreads) return false;
+    if (!aligned(value, 16) || !aligned(grad_value, 16)) return false;
+    const Tune tune = read_tune("RFDETR_MSDA_OWN");
+    if (tune.stage == 0) return false;
+    auto granule = [](long long seg, long long stride, const void *base) -> int {
+        for (int gsz = 16; gsz >= 4; gsz >>= 1)
+            if (seg % gsz == 0 && stride % gsz == 0 && aligned(base, gsz)) return gsz;
+        return 0;
+    };
+    op.gl = granule((long long)LP * 8, (long long)LP * 8, loc);
+    op.ga = granule((long long)LP * sizeof(TW), (long long)LP * sizeof(TW), attn);
+    op.gg = granule((long long)g.D * sizeof(TG), (long long)g.D * sizeof(TG), gout);
+    if (!op.gl || !op.ga || !op.gg) return false;
+    op.threads = std::max(64, (owners + 31) & ~31);
+    op.cap = tune.hsub > 0 ? tune.hsub : 24;
+    op.tq = tune.threads > 0 ? tune.threads : 512;
+    const int per_thread = 8;  // pending-corner masks hold eight samples per thread
+    op.tq = std::min(op.tq, per_thread * op.threads / LP);
+    if (op.tq < 1 || (size_t)op.tq * LP * 4 > 65536) return false;
+    auto r16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
+    size_t o = 0;
+    op.loc_sz = (unsigned)r16((size_t)op.tq * LP * 8);
+    op.o_loc = (unsigned)o; o += 3 * (size_t)op.loc_sz;
+    op.attn_sz = (unsigned)r16((size_t)op.tq * LP * sizeof(TW));
+    op.o_attn = (unsigned)o; o += 3 * (size_t)op.attn_sz;
+    op.gst_sz = (unsigned)r16((size_t)op.tq * (g.D * sizeof(TG) + 16));
+    op.o_gst = (unsigned)o; o += 3 * (size_t)op.gst_sz;
+    op.o_G = (unsigned)o; o += r16((size_t)op.tq * LP * 16);
+    op.o_cnt = (unsigned)o; o += r16((size_t)g.Lv * 4);
+    op.o_vbad = (unsigned)o; o += r16((size_t)g.Lv);
+    op.o_coef = (unsigned)o;
+    size_t bins = r16((size_t)op.cap * g.Lv * 4);
+    op.o_idx = (unsigned)(o + bins);
+    bins += r16((size_t)op.cap * g.Lv * 2);
+    o += bins;
+    op.smem = o;
+    return op.smem <= (size_t)optin;
+}
+
+template <typename TW, int LP, int SEG>
+int launch_backward_owner(const Geom &g, const OwnPlan &op, const void *value, const float *loc, const void *attn,
+                          const void *gout, void *gv, float *gl, void *ga, cudaStream_t stream) {
+    auto kernel = msda_backward_owner_kernel<TW, LP, SEG>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)op.smem) != cudaSuccess)
+        return RFDETR_ERR_CUDA;
+    kernel<<<(unsigned)(g.B * g.H), op.threads, op.smem, stream>>>(
+        static_cast<const bf16 *>(value), loc, static_cast<const TW *>(attn),
+        static_cast<const typename OutOf<bf16, TW>::T *>(gout), static_cast<bf16 *>(gv), gl, static_cast<TW *>(ga), g,
+        op);
+    return launch_status();
+}
+
+template <typename TW, int LP>
+int dispatch_owner_seg(const Geom &g, const OwnPlan &op, const void *value, const float *loc, const void *attn,
+                       const void *gout, void *gv, float *gl, void *ga, cudaStream_t s) {
+    return g.D == 16 ? launch_backward_owner<TW, LP, 1>(g, op, value, loc, attn, gout, gv, gl, ga, s)
+                     : launch_backward_owner<TW, LP, 2>(g, op, value, loc, attn, gout, gv, gl, ga, s);
+}
+
+// bf16 values only; returns -1 when the owner path does not apply.
+template <typename TW>
+int try_backward_owner(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
+                       void *gv, float *gl, void *ga, cudaStream_t s) {
+    OwnPlan op;
+    if (!plan_backward_owner<TW>(g, value, loc, attn, gout, gv, max_smem_optin(), op)) return -1;
+    switch (g.L * g.P) {
+        case 1: return dispatch_owner_seg<TW, 1>(g, op, value, loc, attn, gout, gv, gl, ga, s);
+        case 2: return dispatch_owner_seg<TW, 2>(g, op, value, loc, attn, gout, gv, gl, ga, s);
+        case 4: return dispatch_owner_seg<TW, 4>(g, op, value, loc, attn, gout, gv, gl, ga, s);
+        case 8: return dispatch_owner_seg<TW, 8>(g, op, value, loc, attn, gout, gv, gl, ga, s);
+        default: return -1;
+    }
+}
+
 }  // namespace
 }  // namespace rfdetr
 
@@ -1456,6 +1852,13 @@ extern "C" int rfdetr_msda_backward(void *stream, const void *value, int value_d
     if (value_dtype == RFDETR_BF16 && g.Lq > 0 && aligned(sampling_locations, 8) && aligned(grad_sampling_locations, 8) &&
         aligned(attention_weights, ws) && aligned(grad_attention_weights, ws)) {
         int st2 = -1;
+        if (weight_dtype == RFDETR_BF16)
+            st2 = try_backward_owner<bf16>(g, value, sampling_locations, attention_weights, grad_output, grad_value,
+                                           grad_sampling_locations, grad_attention_weights, s);
+        else
+            st2 = try_backward_owner<float>(g, value, sampling_locations, attention_weights, grad_output, grad_value,
+                                            grad_sampling_locations, grad_attention_weights, s);
+        if (st2 >= 0) return st2;
         if (weight_dtype == RFDETR_BF16)
             st2 = try_backward_bins<bf16>(g, value, sampling_locations, attention_weights, grad_output, grad_value,
                                           grad_sampling_locations, grad_attention_weights, s);
