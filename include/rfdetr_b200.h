@@ -43,6 +43,14 @@ const char *rfdetr_status_string(int status);
 /* ABI version of this library; bumped on any signature change. */
 int rfdetr_abi_version(void);
 
+/* Reads and clears the device fault word.  Kernels that wait on hardware barriers (the TMA
+ * tile loads of the sampler backward) bound every wait; a wait that gives up sets this word and
+ * the kernel finishes with undefined outputs instead of hanging.  Synchronises `stream`.
+ * Returns RFDETR_OK when no wait gave up since the last call, RFDETR_ERR_LIMIT when one did,
+ * RFDETR_ERR_CUDA when the copy fails.  No reference counterpart: the reference's sampler runs
+ * under XLA, which has no device-side waits. */
+int rfdetr_take_device_fault(void *stream);
+
 /* ---------------------------------------------------------------------------------------
  * Multi-scale deformable attention sampler.
  *

@@ -41,6 +41,7 @@ _f32 = ctypes.c_float
 SIGNATURES = {
     "rfdetr_status_string": (ctypes.c_char_p, [_int]),
     "rfdetr_abi_version": (_int, []),
+    "rfdetr_take_device_fault": (_int, [_vp]),
     "rfdetr_msda_forward": (_int, [_vp, _vp, _int, _c_int64_p, _c_int64_p, _vp, _vp, _int, _vp, _int,
                                    _i64, _i64, _i64, _i64, _i64, _i64]),
     "rfdetr_msda_backward_workspace_size": (ctypes.c_size_t, [_int, _i64, _i64, _i64, _i64]),

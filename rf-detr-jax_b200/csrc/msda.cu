@@ -26,6 +26,37 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "tma.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace rfdetr {
+
+bool encode_tensor_map(CUtensorMap *map, CUtensorMapDataType dtype, int rank, const void *base,
+                       const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
+                       CUtensorMapSwizzle swizzle) {
+    static const PFN_cuTensorMapEncodeTiled_v12000 encode = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }();
+    if (!encode || rank < 1 || rank > 5) return false;
+    cuuint64_t d[5], st[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+        es[i] = 1;
+        if (i + 1 < rank) st[i] = strides_bytes[i];
+    }
+    return encode(map, dtype, (cuuint32_t)rank, const_cast<void *>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace rfdetr
 
 namespace rfdetr {
 namespace {
@@ -1395,6 +1426,8 @@ constexpr int kOwnMaxThreads = 576;
 struct OwnPlan {
     int tq, cap, threads, gl, ga, gg;
     unsigned o_loc, loc_sz, o_attn, attn_sz, o_gst, gst_sz, o_G, o_cnt, o_vbad, o_coef, o_idx;
+    int tma, box;       // TMA tile loads (1) or cp.async (0); rows per TMA box
+    unsigned tx_bytes;  // bytes a TMA tile delivers
     size_t smem;
 };
 
@@ -1456,20 +1489,26 @@ __device__ __forceinline__ bool any_nonfinite(const float2 *x) {
     return r != r;
 }
 
-template <typename TW, int LP, int SEG>
+template <typename TW, int LP, int SEG, bool TMA>
 __global__ void __launch_bounds__(kOwnMaxThreads, 1)
 msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restrict__ loc, const TW *__restrict__ attn,
                            const typename OutOf<bf16, TW>::T *__restrict__ grad_out, bf16 *__restrict__ grad_value,
-                           float *__restrict__ grad_loc, TW *__restrict__ grad_attn, const Geom g, const OwnPlan op) {
+                           float *__restrict__ grad_loc, TW *__restrict__ grad_attn, const Geom g, const OwnPlan op,
+                           const __grid_constant__ CUtensorMap tm_loc, const __grid_constant__ CUtensorMap tm_g) {
     using TG = typename OutOf<bf16, TW>::T;
     constexpr int D = 16 * SEG;
     constexpr int LPS = LP == 1 ? 0 : LP == 2 ? 1 : LP == 4 ? 2 : 3;
-    // Staged gradient rows are padded by 16 bytes so rows that differ in their low three bits
-    // start in different bank groups.
-    constexpr unsigned GSTRIDE = (unsigned)(D * sizeof(TG)) + 16u;
-    extern __shared__ __align__(16) unsigned char smem[];
+    // Gradient rows: with TMA, dense rows written with the swizzle mode of their width (16-byte
+    // chunk index XORed with the row's bits 7..); with cp.async, rows padded by 16 bytes.  Both
+    // make rows that differ in their low three bits start in different bank groups.
+    constexpr unsigned ROWB = (unsigned)(D * sizeof(TG));
+    constexpr unsigned GSTRIDE = TMA ? ROWB : ROWB + 16u;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ int lvl_i[LP][3];
     __shared__ float lvl_f[LP][2];
+    __shared__ __align__(8) uint64_t mbar[3];
+    __shared__ int abort_flag;
+    unsigned char *const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int bh = blockIdx.x;
     const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
     const int Lv = g.Lv, cap = op.cap;
@@ -1485,7 +1524,22 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
     auto locb = [&](int i) { return reinterpret_cast<float2 *>(smem + op.o_loc + i * op.loc_sz); };
     auto attnb = [&](int i) { return reinterpret_cast<TW *>(smem + op.o_attn + i * op.attn_sz); };
     auto gstb = [&](int i) { return reinterpret_cast<TG *>(smem + op.o_gst + i * op.gst_sz); };
+    // Byte offset of 16-byte chunk c of staged gradient row r.
+    auto grow = [&](unsigned r, unsigned c) -> unsigned {
+        if constexpr (TMA) return swizzled_chunk(r, c, ROWB);
+        else return r * GSTRIDE + c * 16u;
+    };
 
+    if constexpr (TMA) {
+        if (tid == 0) {
+            for (int i = 0; i < 3; ++i) mbar_init(&mbar[i], 1);
+            abort_flag = 0;
+            mbar_init_fence();
+            tma_prefetch_map(&tm_loc);
+            tma_prefetch_map(&tm_g);
+        }
+        __syncthreads();
+    }
     if (tid < LP) {
         const int l = tid / g.P;
         lvl_i[tid][0] = g.lw[l];
@@ -1498,9 +1552,35 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
     const int nqc = max(qend - qbeg, 0);
     const int ntiles = (nqc + op.tq - 1) / op.tq;
     auto issue = [&](int t) {
-        const int q0 = qbeg + t * op.tq;
-        issue_bwd_tile<TW, TG, LP>(loc, attn, grad_out, reinterpret_cast<float *>(locb(t % 3)), attnb(t % 3),
-                                   gstb(t % 3), g, b, h, q0, min(op.tq, qend - q0), op.gl, op.ga, op.gg, (int)GSTRIDE);
+        const int q0 = qbeg + t * op.tq, slot = t % 3;
+        if constexpr (TMA) {
+            // Weights by cp.async (their per-query rows are narrower than a TMA box allows);
+            // locations and gradient rows as TMA boxes of op.box rows.
+            const int nq = min(op.tq, qend - q0);
+            const int abytes = LP * (int)sizeof(TW), as = 31 - __clz(abytes / op.ga);
+            const size_t row0 = ((size_t)b * g.Lq + q0) * g.H + h;
+            for (int i = tid; i < (nq << as); i += nthr) {
+                const int qi = i >> as, j = i & ((1 << as) - 1);
+                cp_async_bytes(reinterpret_cast<char *>(attnb(slot)) + (size_t)qi * abytes + j * op.ga,
+                               reinterpret_cast<const char *>(attn + (row0 + (size_t)qi * g.H) * LP) + j * op.ga,
+                               op.ga);
+            }
+            if (tid == 0) {
+                mbar_arrive_expect_tx(&mbar[slot], op.tx_bytes);
+                for (int r = 0; r < op.tq; r += op.box) {
+                    tma_load_4d(locb(slot) + r * LP, &tm_loc, &mbar[slot], 0, h, q0 + r, b);
+                    tma_load_4d(reinterpret_cast<unsigned char *>(gstb(slot)) + r * ROWB, &tm_g, &mbar[slot], 0, h,
+                                q0 + r, b);
+                }
+            }
+        } else {
+            issue_bwd_tile<TW, TG, LP>(loc, attn, grad_out, reinterpret_cast<float *>(locb(slot)), attnb(slot),
+                                       gstb(slot), g, b, h, q0, min(op.tq, qend - q0), op.gl, op.ga, op.gg,
+                                       (int)GSTRIDE);
+        }
+    };
+    auto landed = [&](int t) {  // tile t's locations and gradient rows are in shared memory
+        if constexpr (TMA) mbar_wait(&mbar[t % 3], (unsigned)(t / 3) & 1u, &abort_flag);
     };
     if (ntiles > 0) issue(0);
     cp_async_commit();
@@ -1529,6 +1609,7 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
         if (is_owner && seg == 0) vbad[pos] = bad ? 1 : 0;
     }
     cp_async_wait_one();
+    if (ntiles > 0) landed(0);
     __syncthreads();
 
     // Files the corners of sample s selected by `want` (bit c = corner c); returns those whose
@@ -1565,20 +1646,20 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
         if constexpr (SEG > 1) __syncwarp();
         if (is_owner && seg == 0) counts[pos] = 0;
         const unsigned team = SEG > 1 ? (3u << ((tid & 31) & ~1)) : 0u;
-        const unsigned gseg = gs_s + (unsigned)seg * (16u * (unsigned)sizeof(TG));
+        constexpr unsigned SEGCH = 16u * (unsigned)sizeof(TG) / 16u;  // 16-byte chunks per segment
         for (int e = 0; e < n; ++e) {
             const float c = bcoef[e * Lv + pos];
             const unsigned idx = bidx[e * Lv + pos];
-            const unsigned ga = gseg + (idx >> (2 + LPS)) * GSTRIDE;
+            const unsigned r = idx >> (2 + LPS);
             float2 q[8];
             if constexpr (sizeof(TG) == 2) {
-                const uint4 u0 = lds128(ga), u1 = lds128(ga + 16u);
+                const uint4 u0 = lds128(gs_s + grow(r, seg * SEGCH)), u1 = lds128(gs_s + grow(r, seg * SEGCH + 1));
                 q[0] = bf16x2_lo_hi(u0.x); q[1] = bf16x2_lo_hi(u0.y); q[2] = bf16x2_lo_hi(u0.z); q[3] = bf16x2_lo_hi(u0.w);
                 q[4] = bf16x2_lo_hi(u1.x); q[5] = bf16x2_lo_hi(u1.y); q[6] = bf16x2_lo_hi(u1.z); q[7] = bf16x2_lo_hi(u1.w);
             } else {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const float4 f = lds128f(ga + 16u * i);
+                    const float4 f = lds128f(gs_s + grow(r, seg * SEGCH + i));
                     q[2 * i] = make_float2(f.x, f.y);
                     q[2 * i + 1] = make_float2(f.z, f.w);
                 }
@@ -1612,8 +1693,11 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
             float e[4] = {t.m00 * G.x, t.m10 * G.y, t.m01 * G.z, t.m11 * G.w};
             if (!(filed[0] && filed[1] && filed[2] && filed[3])) {
                 bool gbad = false;
-                for (int j = 0; j < D; ++j)
-                    gbad |= !(fabsf(to_f32(reinterpret_cast<const TG *>(gsb + iq * GSTRIDE)[j])) <= 3.4028235e38f);
+                constexpr int PER = 16 / (int)sizeof(TG);
+                for (int j = 0; j < D; ++j) {
+                    const TG x = reinterpret_cast<const TG *>(gsb + grow(iq, j / PER))[j % PER];
+                    gbad |= !(fabsf(to_f32(x)) <= 3.4028235e38f);
+                }
                 const int base = lvl_i[k][2];
                 const int pp[4] = {base + t.p00, base + t.p10, base + t.p01, base + t.p11};
 #pragma unroll
@@ -1662,6 +1746,7 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
             own(gstb(t % 3));
         }
         cp_async_wait_one();
+        if (t + 1 < ntiles) landed(t + 1);
         __syncthreads();
     }
     if (ntiles > 0) {
@@ -1682,7 +1767,7 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
 
 template <typename TW>
 bool plan_backward_owner(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
-                         const void *grad_value, int optin, OwnPlan &op) {
+                         const void *grad_value, int optin, OwnPlan &op, bool allow_tma) {
     using TG = typename OutOf<bf16, TW>::T;
     const int LP = g.L * g.P;
     if (!(LP == 1 || LP == 2 || LP == 4 || LP == 8)) return false;
@@ -1707,14 +1792,22 @@ bool plan_backward_owner(const Geom &g, const void *value, const float *loc, con
     const int per_thread = 8;  // pending-corner masks hold eight samples per thread
     op.tq = std::min(op.tq, per_thread * op.threads / LP);
     if (op.tq < 1 || (size_t)op.tq * LP * 4 > 65536) return false;
+    // TMA tile loads: location rows must be a multiple of 16 bytes, gradient rows one of the
+    // swizzle widths, both bases 16-byte aligned, and a tile a whole number of boxes.
+    const size_t rowb = (size_t)g.D * sizeof(TG);
+    op.box = std::min(op.tq, 256);
+    op.tma = allow_tma && tune.acc != 0 && LP >= 2 && (rowb == 32 || rowb == 64 || rowb == 128) && aligned(loc, 16) &&
+             aligned(gout, 16) && op.tq % op.box == 0;
+    op.tx_bytes = (unsigned)((size_t)op.tq * (LP * 8 + rowb));
     auto r16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
+    auto r1k = [](size_t x) { return (x + 1023) & ~(size_t)1023; };
     size_t o = 0;
-    op.loc_sz = (unsigned)r16((size_t)op.tq * LP * 8);
+    op.gst_sz = op.tma ? (unsigned)r1k((size_t)op.tq * rowb) : (unsigned)r16((size_t)op.tq * (rowb + 16));
+    op.o_gst = (unsigned)o; o += 3 * (size_t)op.gst_sz;  // first: 1024-byte aligned for the swizzle
+    op.loc_sz = (unsigned)((((size_t)op.tq * LP * 8) + 127) & ~(size_t)127);
     op.o_loc = (unsigned)o; o += 3 * (size_t)op.loc_sz;
     op.attn_sz = (unsigned)r16((size_t)op.tq * LP * sizeof(TW));
     op.o_attn = (unsigned)o; o += 3 * (size_t)op.attn_sz;
-    op.gst_sz = (unsigned)r16((size_t)op.tq * (g.D * sizeof(TG) + 16));
-    op.o_gst = (unsigned)o; o += 3 * (size_t)op.gst_sz;
     op.o_G = (unsigned)o; o += r16((size_t)op.tq * LP * 16);
     op.o_cnt = (unsigned)o; o += r16((size_t)g.Lv * 4);
     op.o_vbad = (unsigned)o; o += r16((size_t)g.Lv);
@@ -1723,28 +1816,74 @@ bool plan_backward_owner(const Geom &g, const void *value, const float *loc, con
     op.o_idx = (unsigned)(o + bins);
     bins += r16((size_t)op.cap * g.Lv * 2);
     o += bins;
-    op.smem = o;
+    op.smem = o + (op.tma ? 1024 : 0);  // slack to align the base to 1024 bytes at run time
     return op.smem <= (size_t)optin;
 }
 
-template <typename TW, int LP, int SEG>
-int launch_backward_owner(const Geom &g, const OwnPlan &op, const void *value, const float *loc, const void *attn,
-                          const void *gout, void *gv, float *gl, void *ga, cudaStream_t stream) {
-    auto kernel = msda_backward_owner_kernel<TW, LP, SEG>;
+template <typename TW, int LP, int SEG, bool TMA>
+int launch_backward_owner_k(const Geom &g, const OwnPlan &op, const void *value, const float *loc, const void *attn,
+                            const void *gout, void *gv, float *gl, void *ga, const CUtensorMap &tml,
+                            const CUtensorMap &tmg, cudaStream_t stream) {
+    auto kernel = msda_backward_owner_kernel<TW, LP, SEG, TMA>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)op.smem) != cudaSuccess)
         return RFDETR_ERR_CUDA;
     kernel<<<(unsigned)(g.B * g.H), op.threads, op.smem, stream>>>(
         static_cast<const bf16 *>(value), loc, static_cast<const TW *>(attn),
         static_cast<const typename OutOf<bf16, TW>::T *>(gout), static_cast<bf16 *>(gv), gl, static_cast<TW *>(ga), g,
-        op);
+        op, tml, tmg);
     return launch_status();
+}
+
+template <typename TW, int LP, int SEG>
+int launch_backward_owner(const Geom &g, const OwnPlan &op, const void *value, const float *loc, const void *attn,
+                          const void *gout, void *gv, float *gl, void *ga, cudaStream_t stream) {
+    using TG = typename OutOf<bf16, TW>::T;
+    CUtensorMap tml, tmg;
+    std::memset(&tml, 0, sizeof(tml));
+    std::memset(&tmg, 0, sizeof(tmg));
+    bool tma = op.tma != 0;
+    if (tma) {
+        // Locations [B, Lq, H, LP*2] f32 and gradient rows [B, Lq, H, D]: boxes of one head's rows.
+        const uint64_t lrow = (uint64_t)LP * 8, grow = (uint64_t)g.D * sizeof(TG);
+        const uint64_t ldims[4] = {(uint64_t)LP * 2, (uint64_t)g.H, (uint64_t)g.Lq, (uint64_t)g.B};
+        const uint64_t lstr[3] = {lrow, lrow * g.H, lrow * g.H * g.Lq};
+        const uint32_t lbox[4] = {(uint32_t)LP * 2, 1, (uint32_t)op.box, 1};
+        const uint64_t gdims[4] = {(uint64_t)g.D, (uint64_t)g.H, (uint64_t)g.Lq, (uint64_t)g.B};
+        const uint64_t gstr[3] = {grow, grow * g.H, grow * g.H * g.Lq};
+        const uint32_t gbox[4] = {(uint32_t)g.D, 1, (uint32_t)op.box, 1};
+        const CUtensorMapSwizzle sw = grow == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                      : grow == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                   : CU_TENSOR_MAP_SWIZZLE_128B;
+        tma = encode_tensor_map(&tml, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, loc, ldims, lstr, lbox,
+                                CU_TENSOR_MAP_SWIZZLE_NONE) &&
+              encode_tensor_map(&tmg,
+                                sizeof(TG) == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                                gout, gdims, gstr, gbox, sw);
+    }
+    if (!tma) return -1;  // the caller re-plans without TMA
+    return launch_backward_owner_k<TW, LP, SEG, true>(g, op, value, loc, attn, gout, gv, gl, ga, tml, tmg, stream);
+}
+
+template <typename TW, int LP, int SEG>
+int launch_backward_owner_plain(const Geom &g, const OwnPlan &op, const void *value, const float *loc,
+                                const void *attn, const void *gout, void *gv, float *gl, void *ga,
+                                cudaStream_t stream) {
+    CUtensorMap none;
+    std::memset(&none, 0, sizeof(none));
+    return launch_backward_owner_k<TW, LP, SEG, false>(g, op, value, loc, attn, gout, gv, gl, ga, none, none, stream);
 }
 
 template <typename TW, int LP>
 int dispatch_owner_seg(const Geom &g, const OwnPlan &op, const void *value, const float *loc, const void *attn,
                        const void *gout, void *gv, float *gl, void *ga, cudaStream_t s) {
-    return g.D == 16 ? launch_backward_owner<TW, LP, 1>(g, op, value, loc, attn, gout, gv, gl, ga, s)
-                     : launch_backward_owner<TW, LP, 2>(g, op, value, loc, attn, gout, gv, gl, ga, s);
+    if (op.tma) {
+        if constexpr (LP >= 2)
+            return g.D == 16 ? launch_backward_owner<TW, LP, 1>(g, op, value, loc, attn, gout, gv, gl, ga, s)
+                             : launch_backward_owner<TW, LP, 2>(g, op, value, loc, attn, gout, gv, gl, ga, s);
+        return -1;
+    }
+    return g.D == 16 ? launch_backward_owner_plain<TW, LP, 1>(g, op, value, loc, attn, gout, gv, gl, ga, s)
+                     : launch_backward_owner_plain<TW, LP, 2>(g, op, value, loc, attn, gout, gv, gl, ga, s);
 }
 
 // bf16 values only; returns -1 when the owner path does not apply.
@@ -1752,14 +1891,21 @@ template <typename TW>
 int try_backward_owner(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
                        void *gv, float *gl, void *ga, cudaStream_t s) {
     OwnPlan op;
-    if (!plan_backward_owner<TW>(g, value, loc, attn, gout, gv, max_smem_optin(), op)) return -1;
-    switch (g.L * g.P) {
-        case 1: return dispatch_owner_seg<TW, 1>(g, op, value, loc, attn, gout, gv, gl, ga, s);
-        case 2: return dispatch_owner_seg<TW, 2>(g, op, value, loc, attn, gout, gv, gl, ga, s);
-        case 4: return dispatch_owner_seg<TW, 4>(g, op, value, loc, attn, gout, gv, gl, ga, s);
-        case 8: return dispatch_owner_seg<TW, 8>(g, op, value, loc, attn, gout, gv, gl, ga, s);
-        default: return -1;
+    if (!plan_backward_owner<TW>(g, value, loc, attn, gout, gv, max_smem_optin(), op, true)) return -1;
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        int st = -1;
+        switch (g.L * g.P) {
+            case 1: st = dispatch_owner_seg<TW, 1>(g, op, value, loc, attn, gout, gv, gl, ga, s); break;
+            case 2: st = dispatch_owner_seg<TW, 2>(g, op, value, loc, attn, gout, gv, gl, ga, s); break;
+            case 4: st = dispatch_owner_seg<TW, 4>(g, op, value, loc, attn, gout, gv, gl, ga, s); break;
+            case 8: st = dispatch_owner_seg<TW, 8>(g, op, value, loc, attn, gout, gv, gl, ga, s); break;
+            default: return -1;
+        }
+        if (st >= 0 || !op.tma) return st;
+        // The tensor maps could not be built: fall back to cp.async tile loads.
+        if (!plan_backward_owner<TW>(g, value, loc, attn, gout, gv, max_smem_optin(), op, false)) return -1;
     }
+    return -1;
 }
 
 }  // namespace
@@ -1969,4 +2115,18 @@ extern "C" int rfdetr_msda_backward_noalloc(void *stream, const void *value, int
                                 attention_weights, weight_dtype, grad_output, grad_output_dtype, grad_value,
                                 grad_sampling_locations, grad_attention_weights, scratch, scratch_bytes, batch,
                                 n_heads, head_dim, len_query, n_levels, n_points);
+}
+
+extern "C" int rfdetr_take_device_fault(void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbolAsync(&v, rfdetr::g_device_fault, sizeof(v), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return RFDETR_ERR_CUDA;
+    if (v == 0) return RFDETR_OK;
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbolAsync(rfdetr::g_device_fault, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return RFDETR_ERR_CUDA;
+    return RFDETR_ERR_LIMIT;
 }

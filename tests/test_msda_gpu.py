@@ -210,6 +210,32 @@ def test_unaligned_views_and_entry_points(pkg):
                            torch.tensor(attn, device=DEV))
 
 
+@pytest.mark.parametrize(
+    ("paths", "env"),
+    [
+        ("owner, TMA tile loads", {}),
+        ("owner, cp.async tile loads", {"RFDETR_MSDA_OWN": "24,1,0"}),
+        ("owner, full bins refiled", {"RFDETR_MSDA_OWN": "2,1,1"}),
+        ("bins", {"RFDETR_MSDA_OWN": "0,0"}),
+        ("float32 workspace", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_BINS": "0,0"}),
+    ],
+)
+def test_backward_variants(pkg, monkeypatch, paths, env):
+    """Every backward variant the library can select (tile loads by TMA or cp.async, bins that
+    overflow and are refiled, the capped-bin and workspace kernels) against the oracle, over
+    several tiles; then the device fault word must be clear (no bounded wait gave up)."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    args = dict(seed=5, batch=2, len_query=1300, heads=16, shapes=((24, 24),), points=2, dim=16, lo=-0.05, hi=1.05)
+    value, loc, attn, grad = sampler_inputs(**args)
+    value, attn, grad = O.bf16_round(value), O.bf16_round(attn), O.bf16_round(grad)
+    shapes = args["shapes"]
+    want = (O.ms_deform_attn_forward(value, shapes, loc, attn),) + O.ms_deform_attn_backward(
+        value, shapes, loc, attn, grad)
+    _check(_run(pkg, value, shapes, loc, attn, grad, torch.bfloat16), want, True, paths)
+    assert pkg._native.lib().rfdetr_take_device_fault(torch.cuda.current_stream().cuda_stream) == 0
+
+
 def test_error_behaviour(pkg):
     value, loc, attn, _ = sampler_inputs(0, 1, 4, 2, ((3, 3),), 1, 4)
     v, l, a = (torch.tensor(x, device=DEV) for x in (value, loc, attn))
