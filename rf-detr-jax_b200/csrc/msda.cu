@@ -1422,10 +1422,11 @@ int try_backward_bins(const Geom &g, const void *value, const float *loc, const 
 // owner state stays in registers without spills and the bins hold 512-query tiles.
 // ------------------------------------------------------------------------------------------
 constexpr int kOwnMaxThreads = 576;
+constexpr int kOwnSamplesPerThread = 2;  // samples a thread files (and later finishes) per tile
 
 struct OwnPlan {
     int tq, cap, threads, gl, ga, gg;
-    unsigned o_loc, loc_sz, o_attn, attn_sz, o_gst, gst_sz, o_G, o_cnt, o_vbad, o_coef, o_idx;
+    unsigned o_loc, loc_sz, o_attn, attn_sz, o_gst, gst_sz, o_G, o_cnt, o_vbad, o_pois, o_coef, o_idx;
     int tma, box;       // TMA tile loads (1) or cp.async (0); rows per TMA box
     unsigned tx_bytes;  // bytes a TMA tile delivers
     size_t smem;
@@ -1508,6 +1509,8 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
     __shared__ float lvl_f[LP][2];
     __shared__ __align__(8) uint64_t mbar[3];
     __shared__ int abort_flag;
+    __shared__ int slab_bad;     // some value row of the slab holds inf/NaN
+    __shared__ int tile_bad[3];  // some gradient row of the tile in that slot holds inf/NaN
     unsigned char *const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int bh = blockIdx.x;
     const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
@@ -1519,6 +1522,7 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
     float *const sG = reinterpret_cast<float *>(smem + op.o_G);
     int *const counts = reinterpret_cast<int *>(smem + op.o_cnt);
     unsigned char *const vbad = smem + op.o_vbad;
+    unsigned *const gpois = reinterpret_cast<unsigned *>(smem + op.o_pois);  // per-position channel bits
     float *const bcoef = reinterpret_cast<float *>(smem + op.o_coef);
     unsigned short *const bidx = reinterpret_cast<unsigned short *>(smem + op.o_idx);
     auto locb = [&](int i) { return reinterpret_cast<float2 *>(smem + op.o_loc + i * op.loc_sz); };
@@ -1548,7 +1552,12 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
         lvl_f[tid][0] = (float)g.lw[l];
         lvl_f[tid][1] = (float)g.lh[l];
     }
-    for (int i = tid; i < Lv; i += nthr) counts[i] = 0;
+    for (int i = tid; i < Lv; i += nthr) {
+        counts[i] = 0;
+        gpois[i] = 0;
+    }
+    if (tid < 3) tile_bad[tid] = 0;
+    if (tid == 0) slab_bad = 0;
     const int nqc = max(qend - qbeg, 0);
     const int ntiles = (nqc + op.tq - 1) / op.tq;
     auto issue = [&](int t) {
@@ -1607,6 +1616,8 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
         bool bad = any_nonfinite<8>(vv);
         if constexpr (SEG > 1) bad |= __shfl_xor_sync(0xffffffffu, (int)bad, 1) != 0;
         if (is_owner && seg == 0) vbad[pos] = bad ? 1 : 0;
+        __syncthreads();  // slab_bad was cleared above
+        if (is_owner && bad) slab_bad = 1;
     }
     cp_async_wait_one();
     if (ntiles > 0) landed(0);
@@ -1676,42 +1687,118 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
         }
     };
 
-    // Weight and location gradients of the samples of a drained tile.
-    auto finish = [&](int tb, int qa, int nq) {
-        const float2 *tl = locb(tb % 3);
-        const TW *ta = attnb(tb % 3);
-        const unsigned char *gsb = reinterpret_cast<const unsigned char *>(gstb(tb % 3));
-        for (int s = tid; s < nq * LP; s += nthr) {
-            const int k = s & (LP - 1), iq = s >> LPS;
-            const float Wf = lvl_f[k][0], Hf = lvl_f[k][1];
-            const OwnTaps t = own_taps(tl[s], Wf, Hf, lvl_i[k][0], lvl_i[k][1]);
+    // Per-sample state kept in registers from "file" to "finish" of the same tile: the
+    // fractional weights, the attention weight and bits {ok, in-range corners, filed corners}.
+    constexpr int MAXS = kOwnSamplesPerThread;
+    float st_wx1[MAXS], st_wy1[MAXS], st_a[MAXS];
+    unsigned st_bits[MAXS];
+
+    // First filing of a tile: taps, stash, corners; returns the per-sample bins-full masks.
+    auto file_tile = [&](const float2 *tl, const TW *ta, int nq) -> unsigned {
+        unsigned pending = 0;
+#pragma unroll
+        for (int i = 0; i < MAXS; ++i) {
+            const int s = tid + i * nthr;
+            if (s >= nq * LP) break;
+            const int k = s & (LP - 1);
+            const OwnTaps t = own_taps(tl[s], lvl_f[k][0], lvl_f[k][1], lvl_i[k][0], lvl_i[k][1]);
             const float a = to_f32(ta[s]);
             float cf[4];
             bool filed[4];
             own_coefs(t, a, cf, filed);
+            st_wx1[i] = t.wx1;
+            st_wy1[i] = t.wy1;
+            st_a[i] = a;
+            st_bits[i] = (t.ok ? 1u : 0u) | (t.m00 != 0.f ? 2u : 0u) | (t.m10 != 0.f ? 4u : 0u) |
+                         (t.m01 != 0.f ? 8u : 0u) | (t.m11 != 0.f ? 16u : 0u) | (filed[0] ? 32u : 0u) |
+                         (filed[1] ? 64u : 0u) | (filed[2] ? 128u : 0u) | (filed[3] ? 256u : 0u);
+            if (!t.ok) continue;
+            const int base = lvl_i[k][2];
+            const int pp[4] = {base + t.p00, base + t.p10, base + t.p01, base + t.p11};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (!filed[c]) continue;
+                const int slot = atomicAdd(&counts[pp[c]], 1);
+                if (slot < cap) {
+                    bcoef[slot * Lv + pp[c]] = cf[c];
+                    bidx[slot * Lv + pp[c]] = (unsigned short)(s * 4 + c);
+                } else {
+                    pending |= 1u << (4 * i + c);
+                }
+            }
+        }
+        return pending;
+    };
+
+    // Raises tile_bad[slot] when a gradient row of the tile holds inf/NaN (x * 0 is NaN exactly
+    // for those).
+    auto scan_rows = [&](int t, int nq) {
+        const unsigned gs_s = smem_u32(gstb(t % 3));
+        constexpr unsigned NCH = ROWB / 16u;
+        for (int i = tid; i < nq * (int)NCH; i += nthr) {
+            const uint4 u = lds128(gs_s + grow((unsigned)i / NCH, (unsigned)i % NCH));
+            float2 f[4];
+            if constexpr (sizeof(TG) == 2) {
+                f[0] = bf16x2_lo_hi(u.x); f[1] = bf16x2_lo_hi(u.y); f[2] = bf16x2_lo_hi(u.z); f[3] = bf16x2_lo_hi(u.w);
+            } else {
+                f[0] = make_float2(__uint_as_float(u.x), __uint_as_float(u.y));
+                f[1] = make_float2(__uint_as_float(u.z), __uint_as_float(u.w));
+                f[2] = f[3] = make_float2(0.f, 0.f);
+            }
+            if (any_nonfinite<4>(f)) tile_bad[t % 3] = 1;
+        }
+    };
+
+    // Weight and location gradients of the samples of a drained tile, from the stash.
+    auto finish = [&](int tb, int qa, int nq) {
+        const float2 *tl = locb(tb % 3);
+        const unsigned char *gsb = reinterpret_cast<const unsigned char *>(gstb(tb % 3));
+        const bool maybe_bad = (slab_bad | tile_bad[tb % 3]) != 0;
+#pragma unroll
+        for (int i = 0; i < MAXS; ++i) {
+            const int s = tid + i * nthr;
+            if (s >= nq * LP) break;
+            const int k = s & (LP - 1), iq = s >> LPS;
+            const float Wf = lvl_f[k][0], Hf = lvl_f[k][1];
+            const unsigned bits = st_bits[i];
+            const float wx1 = st_wx1[i], wy1 = st_wy1[i], a = st_a[i];
+            const float wx0 = 1.f - wx1, wy0 = 1.f - wy1;
             const float4 G = *reinterpret_cast<const float4 *>(sG + 4 * s);
-            float e[4] = {t.m00 * G.x, t.m10 * G.y, t.m01 * G.z, t.m11 * G.w};
-            if (!(filed[0] && filed[1] && filed[2] && filed[3])) {
-                bool gbad = false;
+            float e[4] = {(bits & 2u ? 1.f : 0.f) * G.x, (bits & 4u ? 1.f : 0.f) * G.y,
+                          (bits & 8u ? 1.f : 0.f) * G.z, (bits & 16u ? 1.f : 0.f) * G.w};
+            // An unfiled corner is out of range: its m * G term is 0 unless the clipped value
+            // row or the gradient row holds inf/NaN (the reference's 0 * inf = NaN).
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                if (!((bits >> (5 + c)) & 1u)) e[c] = 0.f;
+            if (maybe_bad && (bits & 0x1e1u) != 0x1e1u && (bits & 1u)) {
+                unsigned gmask = 0;  // channels of the gradient row holding inf/NaN
                 constexpr int PER = 16 / (int)sizeof(TG);
                 for (int j = 0; j < D; ++j) {
                     const TG x = reinterpret_cast<const TG *>(gsb + grow(iq, j / PER))[j % PER];
-                    gbad |= !(fabsf(to_f32(x)) <= 3.4028235e38f);
+                    if (!(fabsf(to_f32(x)) <= 3.4028235e38f)) gmask |= 1u << j;
                 }
+                const OwnTaps t = own_taps(tl[s], Wf, Hf, lvl_i[k][0], lvl_i[k][1]);
                 const int base = lvl_i[k][2];
                 const int pp[4] = {base + t.p00, base + t.p10, base + t.p01, base + t.p11};
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if (!filed[c]) e[c] = (gbad || vbad[pp[c]]) ? qnan : 0.f;
+                for (int c = 0; c < 4; ++c) {
+                    if ((bits >> (5 + c)) & 1u) continue;
+                    e[c] = (gmask || vbad[pp[c]]) ? qnan : 0.f;
+                    // The reference also scatters 0 * (a * g) into the clipped row: NaN in the
+                    // channels where g is not finite.
+                    if (gmask) atomicOr(&gpois[pp[c]], gmask);
+                }
             }
-            const float ds = t.wy0 * (t.wx0 * e[0] + t.wx1 * e[1]) + t.wy1 * (t.wx0 * e[2] + t.wx1 * e[3]);
-            const float dx = t.wy0 * (e[1] - e[0]) + t.wy1 * (e[3] - e[2]);
-            const float dy = t.wx0 * (e[2] - e[0]) + t.wx1 * (e[3] - e[1]);
+            const bool ok = (bits & 1u) != 0;
+            const float ds = wy0 * (wx0 * e[0] + wx1 * e[1]) + wy1 * (wx0 * e[2] + wx1 * e[3]);
+            const float dx = wy0 * (e[1] - e[0]) + wy1 * (e[3] - e[2]);
+            const float dy = wx0 * (e[2] - e[0]) + wx1 * (e[3] - e[1]);
             const size_t s_idx = (((size_t)b * g.Lq + qa + iq) * g.H + h) * LP + k;
-            grad_attn[s_idx] = from_f32<TW>(t.ok ? ds : qnan);
+            grad_attn[s_idx] = from_f32<TW>(ok ? ds : qnan);
             float2 gl;
-            gl.x = t.ok ? Wf * (a * dx) : qnan;
-            gl.y = t.ok ? Hf * (a * dy) : qnan;
+            gl.x = ok ? Wf * (a * dx) : qnan;
+            gl.y = ok ? Hf * (a * dy) : qnan;
             reinterpret_cast<float2 *>(grad_loc)[s_idx] = gl;
         }
     };
@@ -1723,11 +1810,9 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
         const TW *ta = attnb(t % 3);
         // Phase A: finish the previous tile, file this tile's corners.
         if (t > 0) finish(t - 1, qa - op.tq, op.tq);
-        unsigned pending = 0;
-        {
-            int i = 0;
-            for (int s = tid; s < nq * LP; s += nthr, ++i) pending |= file(tl, ta, s, 0xFu) << (4 * i);
-        }
+        if (tid == 0) tile_bad[(t + 1) % 3] = 0;  // last read by finish(t - 2)
+        scan_rows(t, nq);
+        unsigned pending = file_tile(tl, ta, nq);
         bool again = __syncthreads_or(pending != 0u);
         // Phase B: prefetch two tiles ahead, drain the bins.
         if (t + 2 < ntiles) issue(t + 2);
@@ -1736,10 +1821,11 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
         for (int round = 0; again && round < 65536; ++round) {  // full bins: refile what did not fit
             __syncthreads();
             unsigned left = 0;
-            int i = 0;
-            for (int s = tid; s < nq * LP; s += nthr, ++i) {
+#pragma unroll
+            for (int i = 0; i < MAXS; ++i) {
+                const int s = tid + i * nthr;
                 const unsigned want = (pending >> (4 * i)) & 0xFu;
-                if (want) left |= file(tl, ta, s, want) << (4 * i);
+                if (want && s < nq * LP) left |= file(tl, ta, s, want) << (4 * i);
             }
             pending = left;
             again = __syncthreads_or(pending != 0u);
@@ -1754,12 +1840,14 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
         finish(t, qbeg + t * op.tq, qend - (qbeg + t * op.tq));
     }
 
+    __syncthreads();  // the last finish may have poisoned rows
     if (is_owner) {
+        const unsigned pois = gpois[pos] >> (16 * seg);
         float f[16];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            f[2 * j] = acc[j].x;
-            f[2 * j + 1] = acc[j].y;
+            f[2 * j] = (pois >> (2 * j)) & 1u ? qnan : acc[j].x;
+            f[2 * j + 1] = (pois >> (2 * j + 1)) & 1u ? qnan : acc[j].y;
         }
         store_vec<bf16, 16>(grad_value + ((size_t)bh * Lv + pos) * D + seg * 16, f);
     }
@@ -1789,8 +1877,7 @@ bool plan_backward_owner(const Geom &g, const void *value, const float *loc, con
     op.threads = std::max(64, (owners + 31) & ~31);
     op.cap = tune.hsub > 0 ? tune.hsub : 24;
     op.tq = tune.threads > 0 ? tune.threads : 512;
-    const int per_thread = 8;  // pending-corner masks hold eight samples per thread
-    op.tq = std::min(op.tq, per_thread * op.threads / LP);
+    op.tq = std::min(op.tq, kOwnSamplesPerThread * op.threads / LP);
     if (op.tq < 1 || (size_t)op.tq * LP * 4 > 65536) return false;
     // TMA tile loads: location rows must be a multiple of 16 bytes, gradient rows one of the
     // swizzle widths, both bases 16-byte aligned, and a tile a whole number of boxes.
@@ -1811,6 +1898,7 @@ bool plan_backward_owner(const Geom &g, const void *value, const float *loc, con
     op.o_G = (unsigned)o; o += r16((size_t)op.tq * LP * 16);
     op.o_cnt = (unsigned)o; o += r16((size_t)g.Lv * 4);
     op.o_vbad = (unsigned)o; o += r16((size_t)g.Lv);
+    op.o_pois = (unsigned)o; o += r16((size_t)g.Lv * 4);
     op.o_coef = (unsigned)o;
     size_t bins = r16((size_t)op.cap * g.Lv * 4);
     op.o_idx = (unsigned)(o + bins);

@@ -236,6 +236,40 @@ def test_backward_variants(pkg, monkeypatch, paths, env):
     assert pkg._native.lib().rfdetr_take_device_fault(torch.cuda.current_stream().cuda_stream) == 0
 
 
+@pytest.mark.parametrize(
+    ("paths", "env"),
+    [
+        ("owner, TMA tile loads", {}),
+        ("owner, cp.async tile loads", {"RFDETR_MSDA_OWN": "24,1,0"}),
+    ],
+)
+def test_backward_non_finite_rows(pkg, monkeypatch, paths, env):
+    """inf/NaN entries in value rows (including border rows that clipped corners read) and in
+    gradient rows: the same outputs are non-finite as in the float64 oracle (the reference's
+    0 * inf = NaN through clipped corners included), and the finite ones agree."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    args = dict(seed=9, batch=2, len_query=1100, heads=4, shapes=((24, 24),), points=2, dim=16, lo=-0.05, hi=1.05)
+    value, loc, attn, grad = sampler_inputs(**args)
+    value, attn, grad = O.bf16_round(value), O.bf16_round(attn), O.bf16_round(grad)
+    value[0, 0, 3] = np.inf      # corner position (0, 0) of slab 0
+    value[1, 23, 5] = np.nan     # corner position (0, 23) of slab 1
+    value[5, 300, 0] = -np.inf   # interior position
+    grad[0, 7, 1 * 16 + 2] = np.inf   # image 0, query 7, head 1, channel 2
+    grad[1, 900, 0 * 16 + 9] = np.nan
+    shapes = args["shapes"]
+    with np.errstate(invalid="ignore"):
+        want = (O.ms_deform_attn_forward(value, shapes, loc, attn),) + O.ms_deform_attn_backward(
+            value, shapes, loc, attn, grad)
+    got = _run(pkg, value, shapes, loc, attn, grad, torch.bfloat16)
+    for g, w, n in zip(got, want, ("out", "grad_value", "grad_loc", "grad_attn"), strict=True):
+        fw, fg = np.isfinite(w), np.isfinite(g)
+        assert (~fw).any(), f"{n}: the case should produce non-finite entries"
+        np.testing.assert_array_equal(fg, fw, err_msg=f"{paths}:{n} finiteness")
+        assert_bf16_close(np.where(fw, g, 0.0), np.where(fw, w, 0.0), f"{paths}:{n}")
+    assert pkg._native.lib().rfdetr_take_device_fault(torch.cuda.current_stream().cuda_stream) == 0
+
+
 def test_error_behaviour(pkg):
     value, loc, attn, _ = sampler_inputs(0, 1, 4, 2, ((3, 3),), 1, 4)
     v, l, a = (torch.tensor(x, device=DEV) for x in (value, loc, attn))
