@@ -15,6 +15,11 @@ CUDA events around K steps.  ``e2e``: the public API (``ms_deform_attn_core_rows
 from pinned host buffers, host->device copies of the step's inputs and device->host copies of
 the output and all three gradients inside the timed region.
 
+``components`` (N=1 only): config 4 at training shape on the device -- the two-stage top-k
+(13 groups x 8 images), the matching cost of three stacked decoder layers and the 312 exact
+assignments -- each with its CPU baseline (the oracle for selection and cost; SciPy, the
+reference's own solver, for the assignments, on one core and on all cores).
+
 ``--impl reference`` times the CPU restatement of the reference's sampler (``oracle/msda.py``,
 float32) on the host cores with a process pool over the images of the same workload: JAX, the
 reference's runtime, is not installable here, so the reference's XLA-CPU path cannot run.
@@ -133,6 +138,139 @@ class ClockSampler:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+# Config 4 geometry (two-stage selection + matching at Nano training shape).
+C4_B, C4_Q, C4_C, C4_T, C4_G, C4_LAYERS, C4_POS, C4_K = 8, 3900, 91, 100, 13, 3, 576, 300
+
+
+def make_c4_inputs(seed):
+    """Config-4 inputs with the baseline's distributions: encoder logits N(0,1) per group,
+    K ~ U{1..100} targets per image (cx, cy ~ U(0.05, 0.95), w, h ~ U(0.02, 0.5), labels
+    U{0..90}, padded to 100), decoder logits/boxes for three stacked layers."""
+    rng = np.random.default_rng(seed)
+    enc = rng.standard_normal((C4_G, C4_B, C4_POS, C4_C)).astype(np.float32)
+    sizes = rng.integers(1, C4_T + 1, C4_B).astype(np.int32)
+    mask = np.arange(C4_T)[None, :] < sizes[:, None]
+    labels = np.where(mask, rng.integers(0, C4_C, (C4_B, C4_T)), 0).astype(np.int32)
+    tboxes = np.concatenate([rng.uniform(0.05, 0.95, (C4_B, C4_T, 2)), rng.uniform(0.02, 0.5, (C4_B, C4_T, 2))], -1)
+    tboxes = np.where(mask[..., None], tboxes, 0.0).astype(np.float32)
+    logits = rng.standard_normal((C4_LAYERS, C4_B, C4_Q, C4_C)).astype(np.float32)
+    boxes = np.concatenate([rng.uniform(0.05, 0.95, (C4_LAYERS, C4_B, C4_Q, 2)),
+                            rng.uniform(0.02, 0.5, (C4_LAYERS, C4_B, C4_Q, 2))], -1).astype(np.float32)
+    return enc, logits, boxes, labels, tboxes, mask, sizes
+
+
+def _scipy_image(args):
+    """One (layer, image): SciPy's solver on each group's block, as the reference's host loop
+    (``matcher.py:162-178``) does."""
+    from scipy.optimize import linear_sum_assignment
+
+    cost, size = args
+    per = cost.shape[0] // C4_G
+    for g in range(C4_G):
+        block = cost[g * per:(g + 1) * per, :size]
+        if size:
+            linear_sum_assignment(block)
+    return size
+
+
+def run_components(torch, device, N, lib, peak):
+    """Config 4 on the device (top-k, cost, assignment) with the CPU baselines beside it."""
+    import multiprocessing as mp
+
+    from oracle import matcher as OM
+    from oracle import topk as OT
+
+    enc, logits, boxes, labels, tboxes, mask, sizes = make_c4_inputs(4)
+    t = lambda x: torch.tensor(x, device=device)  # noqa: E731
+    d_enc, d_logits, d_boxes = t(enc), t(logits), t(boxes)
+    d_labels, d_tboxes, d_mask = t(labels), t(tboxes), t(mask.astype(np.uint8))
+    d_sizes = t(sizes)
+    rows = C4_G * C4_B
+    scores = torch.empty((rows, C4_POS), dtype=torch.float32, device=device)
+    values = torch.empty((rows, C4_K), dtype=torch.float32, device=device)
+    idx = torch.empty((rows, C4_K), dtype=torch.int32, device=device)
+    cost = torch.empty((C4_LAYERS, C4_B, C4_Q, C4_T), dtype=torch.float32, device=device)
+    slots = C4_G * C4_T
+    problems = C4_LAYERS * C4_B
+    a_rows = torch.empty((problems, slots), dtype=torch.int32, device=device)
+    a_cols = torch.empty_like(a_rows)
+    a_valid = torch.empty((problems, slots), dtype=torch.uint8, device=device)
+    status = torch.zeros((1,), dtype=torch.int32, device=device)
+    sizes_folded = d_sizes.repeat(C4_LAYERS).contiguous()
+    st = torch.cuda.current_stream(device).cuda_stream
+
+    def topk():
+        N.check(lib.rfdetr_topk_select(st, d_enc.data_ptr(), rows, C4_POS, C4_C, C4_K, scores.data_ptr(),
+                                       values.data_ptr(), idx.data_ptr()), "topk")
+
+    def costs():
+        for layer in range(C4_LAYERS):
+            N.check(lib.rfdetr_match_cost(st, d_logits[layer].data_ptr(), N.F32, d_boxes[layer].data_ptr(), N.F32,
+                                          d_labels.data_ptr(), d_tboxes.data_ptr(), d_mask.data_ptr(),
+                                          cost[layer].data_ptr(), C4_B, C4_Q, C4_C, C4_T, 2.0, 5.0, 2.0, 0.25),
+                    "cost")
+
+    def lsap():
+        N.check(lib.rfdetr_lsap_batched(st, cost.data_ptr(), sizes_folded.data_ptr(), problems, C4_Q, C4_T, C4_G,
+                                        a_rows.data_ptr(), a_cols.data_ptr(), a_valid.data_ptr(), status.data_ptr()),
+                "lsap")
+
+    def dev_ms(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    ms_topk = dev_ms(topk, 50)
+    ms_cost = dev_ms(costs, 30)
+    ms_lsap = dev_ms(lsap, 10)
+    N.check(int(status.item()), "lsap device status")
+    topk_bytes = rows * C4_POS * C4_C * 4 + rows * C4_POS * 4 + 2 * rows * C4_K * 4
+    cost_bytes = C4_LAYERS * (C4_B * C4_Q * (C4_C + 4) * 4 + C4_B * C4_T * 9 + C4_B * C4_Q * C4_T * 4)
+
+    # CPU baselines: the oracle for selection and cost (float64 NumPy, one core); SciPy -- the
+    # reference's own solver -- for the assignment, one core and a process pool over all cores.
+    t0 = time.perf_counter()
+    OT.two_stage_select(enc, C4_K)
+    cpu_topk = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    OM.build_cost_matrix(logits[0], boxes[0], labels, tboxes, mask)
+    cpu_cost = (time.perf_counter() - t0) * C4_LAYERS
+    cost_host = cost.cpu().numpy()
+    tasks = [(cost_host[layer, b], int(sizes[b])) for layer in range(C4_LAYERS) for b in range(C4_B)]
+    t0 = time.perf_counter()
+    for task in tasks:
+        _scipy_image(task)
+    cpu_lsap_1 = time.perf_counter() - t0
+    cores = os.cpu_count() or 1
+    with mp.get_context("spawn").Pool(cores) as pool:
+        pool.map(_scipy_image, tasks[:cores])
+        t0 = time.perf_counter()
+        pool.map(_scipy_image, tasks)
+        cpu_lsap_n = time.perf_counter() - t0
+    gbs = lambda nbytes, ms: nbytes / (ms * 1e-3) / 1e9  # noqa: E731
+    return {
+        "workload": f"config4 training shape: top-{C4_K} of {C4_G}x{C4_B} rows of {C4_POS}x{C4_C} logits; "
+                    f"cost {C4_LAYERS}x{C4_B}x{C4_Q}x{C4_T}; {C4_LAYERS * C4_B * C4_G} exact assignments",
+        "topk_select": {"ms": ms_topk, "GB/s": gbs(topk_bytes, ms_topk), "frac": gbs(topk_bytes, ms_topk) / peak,
+                        "algorithmic_bytes": topk_bytes,
+                        "cpu_ms": cpu_topk * 1e3, "cpu_kind": "port (oracle/topk.py), 1 core"},
+        "match_cost": {"ms": ms_cost, "GB/s": gbs(cost_bytes, ms_cost), "frac": gbs(cost_bytes, ms_cost) / peak,
+                       "algorithmic_bytes": cost_bytes,
+                       "cpu_ms": cpu_cost * 1e3, "cpu_kind": "port (oracle/matcher.py float64), 1 core"},
+        "lsap_batched": {"ms": ms_lsap, "problems_per_s": C4_LAYERS * C4_B * C4_G / (ms_lsap * 1e-3),
+                         "bound": "latency",
+                         "cpu_ms_1core": cpu_lsap_1 * 1e3, f"cpu_ms_{cores}cores": cpu_lsap_n * 1e3,
+                         "cpu_kind": "reference (scipy.optimize.linear_sum_assignment, the reference's solver)"},
+    }
 
 
 def cpu_baseline_sample(steps_budget_s=20.0):
@@ -367,6 +505,9 @@ def run_ours(args):
         e2e_ms = float(t.item())
 
     cpu = cpu_baseline_sample() if (rank == 0 and world == 1) else None
+    peaks_path_ = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak_ = float(json.load(open(peaks_path_))["hbm_gbs"]) if os.path.exists(peaks_path_) else 6650.0
+    components = run_components(torch, device, N, lib, peak_) if (rank == 0 and world == 1) else None
 
     queries = B * LQ * world
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -403,6 +544,8 @@ def run_ours(args):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if components is not None:
+        line["components"] = components
     if rank == 0:
         print(json.dumps(line), flush=True)
     for kind in graphs:
