@@ -6,10 +6,22 @@
 // jax.lax.top_k returns the k largest in descending order, the lower index first among equal
 // values; floats compare in IEEE totalOrder (NaN above +inf).
 //
-// One CTA per row: each warp reduces the classes of a few positions at once (coalesced along
-// the class axis), the CTA packs (totalOrder(score), ~position) into 64-bit keys in shared
-// memory, and a bitonic network sorts them descending; the first k keys give the answer.
+// Keys: (totalOrder(score) << 32) | ~position, so larger keys come first and equal scores order
+// by ascending position; every key of a row is distinct.
+//
+// Rows of up to kTopkClusterMaxPositions positions (the detector's 576 proposals): one cluster of
+// kTopkCluster CTAs per row.  Each CTA reduces the classes of its share of the positions (flat
+// 16-byte loads, all in flight at once; a per-position max of ordered keys by shared-memory
+// atomicMax), sorts those keys in shared memory, and after a cluster
+// barrier pulls every CTA's sorted keys from its peers through distributed shared memory.  The
+// answer needs no global sort: the output slot of a key is its rank, the number of keys above
+// it, which is the sum over the cluster's sorted lists of one binary search each; a CTA ranks
+// its own keys and writes the ones below k straight to their slots.
+// Longer rows: one CTA per row and a bitonic sort of the keys in shared memory.
 #include <algorithm>
+#include <cstdlib>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
@@ -95,6 +107,153 @@ topk_kernel(const float *__restrict__ logits, int N, int C, int k, int P2, float
     }
 }
 
+// CTAs per row.  Measured at config 4 (104 rows of 576 x 91): 4 runs the whole grid in one
+// wave (12.0 us); 8 leaves a tail of clusters for a second wave (17.3 us); 2 gives each CTA
+// too much to load (16.4 us).
+constexpr int kTopkCluster = 4;
+constexpr int kTopkClusterThreads = 256;
+constexpr int kTopkClusterMaxPositions = 2048;
+
+template <int CL>
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kTopkClusterThreads)
+topk_cluster_kernel(const float *__restrict__ logits, int N, int C, int k, float *__restrict__ scores_out,
+                    float *__restrict__ values_out, int32_t *__restrict__ idx_out) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    __shared__ unsigned long long mine[(kTopkClusterMaxPositions + CL - 1) / CL];
+    __shared__ unsigned long long sorted[(kTopkClusterMaxPositions + CL - 1) / CL];
+    __shared__ unsigned long long all[kTopkClusterMaxPositions];
+    __shared__ int rank_of[(kTopkClusterMaxPositions + CL - 1) / CL];
+    __shared__ unsigned okey[(kTopkClusterMaxPositions + CL - 1) / CL];
+    const int crank = (int)cluster.block_rank();
+    const int r = blockIdx.x / CL;
+    const int per = (((N + CL - 1) / CL) + 3) & ~3;  // a multiple of 4 positions
+    const int p_lo = crank * per, p_hi = min(N, p_lo + per), mine_n = max(p_hi - p_lo, 0);
+    const float *rowp = logits + (size_t)r * N * C;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int nwarps = kTopkClusterThreads / 32;
+    constexpr int U = 4;  // positions per warp step: independent load chains in flight
+
+    for (int i = threadIdx.x; i < mine_n; i += kTopkClusterThreads) {
+        rank_of[i] = 0;
+        okey[i] = 0u;  // below every ordered key
+    }
+    // Rows whose elements start on 16-byte boundaries are read as flat float4 vectors (all of a
+    // CTA's loads in flight at once); a vector spans at most two positions (C >= 4), and each
+    // position's max is an atomicMax of ordered keys (NaN canonicalised, so it wins like jnp.max).
+    const bool flat = C >= 4 && C <= 1024 && ((size_t)N * C) % 4 == 0 && (reinterpret_cast<size_t>(logits) & 15) == 0;
+    if (flat) {
+        __syncthreads();
+        // [e0, e1): this CTA's elements (empty when its positions start past the row's end);
+        // e0 is a multiple of 4 because per is.
+        const unsigned e0 = (unsigned)(p_lo * C), e1 = e0 + (unsigned)(mine_n * C);
+        const unsigned nv = (e1 - e0) / 4;
+        const float4 *v4 = reinterpret_cast<const float4 *>(rowp + e0);
+        const unsigned magic = 0xffffffffu / (unsigned)C + 1u;  // floor(e / C) for e < 2^32 / C
+        constexpr int VU = 8;
+        for (unsigned v0 = threadIdx.x; v0 < nv; v0 += kTopkClusterThreads * VU) {
+            float4 x[VU];
+#pragma unroll
+            for (int u = 0; u < VU; ++u) {
+                const unsigned v = v0 + u * kTopkClusterThreads;
+                x[u] = v < nv ? __ldg(v4 + v) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            }
+#pragma unroll
+            for (int u = 0; u < VU; ++u) {
+                const unsigned v = v0 + u * kTopkClusterThreads;
+                if (v >= nv) break;
+                const unsigned e = e0 + 4 * v;                     // row-relative element index
+                const unsigned pa = __umulhi(e, magic);            // position of the first element
+                const unsigned split = (pa + 1) * (unsigned)C - e; // elements before the next position
+                const float f[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+                unsigned ka = 0u, kb = 0u;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const unsigned kk = order_key(f[i] != f[i] ? __uint_as_float(0x7fc00000u) : f[i]);
+                    if ((unsigned)i < split) ka = max(ka, kk);
+                    else kb = max(kb, kk);
+                }
+                atomicMax(&okey[pa - p_lo], ka);
+                if (split < 4u) atomicMax(&okey[pa + 1 - p_lo], kb);
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < mine_n; i += kTopkClusterThreads) {
+            const int p = p_lo + i;
+            mine[i] = ((unsigned long long)okey[i] << 32) | (unsigned long long)(0xffffffffu - (unsigned)p);
+            if (scores_out) scores_out[(size_t)r * N + p] = key_to_float(okey[i]);
+        }
+    }
+    for (int q0 = warp * U; !flat && q0 < mine_n; q0 += nwarps * U) {
+        float m[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            m[u] = -INFINITY;
+            if (q0 + u < mine_n) {
+                const float *x = rowp + (size_t)(p_lo + q0 + u) * C;
+                for (int c = lane; c < C; c += 32) m[u] = nan_max(m[u], __ldg(x + c));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m[u] = nan_max(m[u], __shfl_xor_sync(0xffffffffu, m[u], o));
+        }
+        if (lane < U && q0 + lane < mine_n) {
+            float sc = m[0];
+#pragma unroll
+            for (int u = 1; u < U; ++u) sc = (lane == u) ? m[u] : sc;
+            if (sc != sc) sc = __uint_as_float(0x7fc00000u);  // canonical (positive) NaN sorts first
+            const int p = p_lo + q0 + lane;
+            mine[q0 + lane] = ((unsigned long long)order_key(sc) << 32) | (unsigned long long)(0xffffffffu - (unsigned)p);
+            if (scores_out) scores_out[(size_t)r * N + p] = sc;
+        }
+    }
+    __syncthreads();
+    // Sort this CTA's keys (descending): a key's local rank is the count of own keys above it.
+    for (int i = threadIdx.x; i < mine_n; i += kTopkClusterThreads) {
+        const unsigned long long key = mine[i];
+        int lr = 0;
+        for (int j = 0; j < mine_n; ++j) lr += mine[j] > key ? 1 : 0;
+        sorted[lr] = key;
+    }
+    cluster.sync();
+    // Every CTA's sorted keys, from the whole cluster (slot c * per + local rank).
+    for (int j = threadIdx.x; j < CL * per; j += kTopkClusterThreads) {
+        const int owner = j / per, o = j - owner * per;
+        const int owner_n = max(min(N, (owner + 1) * per) - owner * per, 0);
+        if (o < owner_n) {
+            const unsigned long long *peer = cluster.map_shared_rank(sorted, owner);
+            all[j] = peer[o];
+        }
+    }
+    __syncthreads();
+    // Rank of an own key = keys above it in each CTA's sorted list (a binary search per list).
+    for (int w = threadIdx.x; w < mine_n * CL; w += kTopkClusterThreads) {
+        const int i = w / CL, c = w - i * CL;
+        const int cn = max(min(N, (c + 1) * per) - c * per, 0);
+        const unsigned long long key = sorted[i];
+        const unsigned long long *list = all + c * per;
+        int lo = 0, hi = cn;  // first index whose key is not above `key`
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (list[mid] > key) lo = mid + 1;
+            else hi = mid;
+        }
+        atomicAdd(&rank_of[i], lo);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < mine_n; i += kTopkClusterThreads) {
+        const int rk = rank_of[i];
+        if (rk < k) {
+            const unsigned long long key = sorted[i];
+            idx_out[(size_t)r * k + rk] = (int)(0xffffffffu - (unsigned)(key & 0xffffffffull));
+            if (values_out) values_out[(size_t)r * k + rk] = key_to_float((unsigned)(key >> 32));
+        }
+    }
+    cluster.sync();  // peers read this CTA's keys until here
+}
+
 template <typename V>
 __global__ void select_rows_kernel(const V *__restrict__ values, long long row_vecs, int N,
                                    const int32_t *__restrict__ idx, int K, V *__restrict__ out,
@@ -146,6 +305,12 @@ extern "C" int rfdetr_topk_select(void *stream, const float *logits, int64_t row
     if (!aligned(logits, 4) || !aligned(indices_out, 4) || (scores_out && !aligned(scores_out, 4)) ||
         (values_out && !aligned(values_out, 4)))
         return RFDETR_ERR_ALIGN;
+    if (positions <= kTopkClusterMaxPositions && rows * kTopkCluster <= 2147483647LL && !std::getenv("RFDETR_TOPK_SORT")) {
+        topk_cluster_kernel<kTopkCluster><<<(unsigned)(rows * kTopkCluster), kTopkClusterThreads, 0,
+                                            static_cast<cudaStream_t>(stream)>>>(
+            logits, (int)positions, (int)classes, (int)k, scores_out, values_out, indices_out);
+        return launch_status();
+    }
     const int P2 = next_pow2((int)positions);
     const size_t smem = (size_t)P2 * sizeof(unsigned long long);
     if (smem > 48 * 1024 &&

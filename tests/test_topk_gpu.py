@@ -30,8 +30,13 @@ def test_golden(pkg):
     np.testing.assert_array_equal(v, d["tie_values"])
 
 
-def test_config4_training_shape(pkg):
-    """Config 4 at training shape: 13 groups x 8 images x 576 proposals x 91 classes."""
+@pytest.mark.parametrize("path", ["cluster ranks", "bitonic sort"])
+def test_config4_training_shape(pkg, monkeypatch, path):
+    """Config 4 at training shape: 13 groups x 8 images x 576 proposals x 91 classes, through
+    both selection kernels (the cluster rank count serves rows of up to 2048 positions, the
+    bitonic sort longer rows; the switch forces the sort here)."""
+    if path == "bitonic sort":
+        monkeypatch.setenv("RFDETR_TOPK_SORT", "1")
     logits = np.random.default_rng(4).standard_normal((13, 8, 576, 91)).astype(np.float32)
     s, v, i = _select(pkg, logits, 300)
     ws, wv, wi = OT.two_stage_select(logits, 300)
@@ -51,8 +56,11 @@ def test_ties_keep_lower_index_first(pkg):
     np.testing.assert_array_equal(i.cpu().numpy(), np.tile(np.arange(300), (3, 1)))
 
 
-def test_special_values(pkg):
+@pytest.mark.parametrize("path", ["cluster ranks", "bitonic sort"])
+def test_special_values(pkg, monkeypatch, path):
     """NaN first, then +inf ... -inf; +0 above -0 (IEEE totalOrder)."""
+    if path == "bitonic sort":
+        monkeypatch.setenv("RFDETR_TOPK_SORT", "1")
     row = np.array([1.0, -np.inf, np.nan, 0.0, -0.0, np.inf, -1.0, 2.0], np.float32)
     v, i = pkg.top_k(torch.tensor(row[None], device=DEV), 8)
     wv, wi = OT.top_k(row[None], 8)
