@@ -340,6 +340,47 @@ def run_reference(args):
     return 0
 
 
+class Ranks:
+    """The job's ranks, one process per GPU: a barrier and max-over-ranks reductions over the
+    process group (NCCL on the GPUs; the tests drive the same code over gloo on CPU).  Every
+    rank takes the same collective steps in the same order."""
+
+    def __init__(self, world, rank, device, dist=None):
+        self.world, self.rank, self.device, self.dist = world, rank, device, dist
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_float(self, x):
+        if self.world == 1:
+            return float(x)
+        import torch
+
+        t = torch.tensor([float(x)], device=self.device, dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def max_int(self, n):
+        if self.world == 1:
+            return int(n)
+        import torch
+
+        t = torch.tensor([int(n)], device=self.device, dtype=torch.int64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return int(t.item())
+
+
+def shard_seed(rank, ring_index):
+    """Seed of one input set of one rank: each rank runs its own batch (weak scaling)."""
+    return 1 + ring_index + 97 * rank
+
+
+def whole_job_value(per_rank_units, world, ms_per_step):
+    """Units all ranks processed per second, from the max-over-ranks step time."""
+    return per_rank_units * world / (ms_per_step * 1e-3)
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -361,9 +402,8 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    ranks = Ranks(world, rank, device, dist)
+    barrier = ranks.barrier
 
     lib = N.lib()
     stream = torch.cuda.Stream(device)
@@ -372,7 +412,7 @@ def run_ours(args):
     ring = max(4, int(np.ceil(3 * L2_BYTES / per_set)))
     sets = []
     for r in range(ring):
-        value, loc, attn, grad = make_inputs(1 + r + 97 * rank, torch, device)
+        value, loc, attn, grad = make_inputs(shard_seed(rank, r), torch, device)
         out = torch.empty((B, LQ, H * D), dtype=torch.bfloat16, device=device)
         gv = torch.empty_like(value)
         gl = torch.empty_like(loc)
@@ -427,12 +467,7 @@ def run_ours(args):
         end.synchronize()
         torch.cuda.synchronize()
         barrier()
-        ms = start.elapsed_time(end)
-        if world > 1:
-            t = torch.tensor([ms], device=device, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms / steps
+        return ranks.max_float(start.elapsed_time(end)) / steps
 
     def timed(kind, steps, warmup, min_seconds):
         """Warm up, then repeat the K-step timed region until `min_seconds` of device time have
@@ -444,11 +479,7 @@ def run_ours(args):
                 gl_[i % ring].replay()
         stream.synchronize()
         first = timed_once(kind, steps)
-        reps = max(1, min(2000, int(min_seconds * 1e3 / max(first * steps, 1e-3))))
-        if world > 1:
-            t = torch.tensor([reps], device=device, dtype=torch.int64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            reps = int(t.item())
+        reps = ranks.max_int(max(1, min(2000, int(min_seconds * 1e3 / max(first * steps, 1e-3)))))
         samples = [timed_once(kind, steps) for _ in range(reps)]
         return statistics.median(samples), reps
 
@@ -498,18 +529,13 @@ def run_ours(args):
         e_end.record(stream)
     e_end.synchronize()
     barrier()
-    e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = ranks.max_float(e_start.elapsed_time(e_end)) / e2e_steps
 
     cpu = cpu_baseline_sample() if (rank == 0 and world == 1) else None
     peaks_path_ = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak_ = float(json.load(open(peaks_path_))["hbm_gbs"]) if os.path.exists(peaks_path_) else 6650.0
     components = run_components(torch, device, N, lib, peak_) if (rank == 0 and world == 1) else None
 
-    queries = B * LQ * world
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak, peak_src = 6650.0, "fallback"
     if os.path.exists(peaks_path):
@@ -522,7 +548,7 @@ def run_ours(args):
             traffic = json.load(f).get("msda_backward_c2")
     achieved = bwd_bytes / (ms_bwd * 1e-3) / 1e9
     line = {
-        "metric": METRIC, "value": queries / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
+        "metric": METRIC, "value": whole_job_value(B * LQ, world, ms_step), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "config2 sampler fwd+bwd (Nano decoder cross-attn, train shape)",
@@ -537,7 +563,7 @@ def run_ours(args):
         "kernels": {"msda_forward": {"ms": ms_fwd, "GB/s": fwd_bytes / (ms_fwd * 1e-3) / 1e9,
                                      "frac": fwd_bytes / (ms_fwd * 1e-3) / 1e9 / peak},
                     "msda_backward": {"ms": ms_bwd, "GB/s": achieved, "frac": achieved / peak}},
-        "e2e": {"value": queries / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+        "e2e": {"value": whole_job_value(B * LQ, world, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "gpu_launches": 2 * args.steps,
         "clocks": clock_summary,
