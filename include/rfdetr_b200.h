@@ -144,7 +144,8 @@ int rfdetr_msda_backward_noalloc(void *stream,
  * Descending IEEE totalOrder (NaN first), equal scores keep the lower index first.
  * C == 1 selects directly over a [R, N] score tensor.
  *   scores_out  [R, N] f32 or NULL;  values_out [R, k] f32 or NULL;  indices_out [R, k] int32.
- * Limits: 1 <= k <= N <= 16384.
+ * Limits: 1 <= k <= N <= 16384; for C == 1 (a flat score row, as the inference post-process's
+ * top-k over Q*C sigmoid scores, postprocess.py:37-41) N may reach 2^24 when k <= 4096.
  * ------------------------------------------------------------------------------------- */
 int rfdetr_topk_select(void *stream, const float *logits, int64_t rows, int64_t positions,
                        int64_t classes, int64_t k, float *scores_out, float *values_out,

@@ -62,3 +62,27 @@ def two_stage_select(logits: np.ndarray, num_queries: int):
     k = min(num_queries, scores.shape[-1])
     values, indices = top_k(scores, k)
     return scores, values, indices
+
+
+def post_process(probabilities: np.ndarray, pred_boxes: np.ndarray, target_sizes: np.ndarray, num_classes: int,
+                 num_select: int = 300):
+    """The reference's ``post_process`` (``postprocess.py:37-51``) from already computed sigmoid
+    probabilities ``[B, Q*C]``: top-k, query/label split, ``xyxy`` boxes (``box_ops.py:27-32``)
+    scaled to ``(width, height)`` and clipped to the image."""
+    batch = probabilities.shape[0]
+    k = min(num_select, probabilities.shape[1])
+    scores, indexes = top_k(probabilities, k)
+    query_index = indexes // num_classes
+    labels = (indexes % num_classes).astype(np.int32)
+    b = np.asarray(pred_boxes, np.float32)
+    cx, cy = b[..., 0], b[..., 1]
+    w, h = np.clip(b[..., 2], 0.0, None), np.clip(b[..., 3], 0.0, None)
+    xyxy = np.stack([cx - np.float32(0.5) * w, cy - np.float32(0.5) * h, cx + np.float32(0.5) * w,
+                     cy + np.float32(0.5) * h], axis=-1).astype(np.float32)
+    xyxy = np.take_along_axis(xyxy, query_index[..., None].astype(np.int64), axis=1)
+    sizes = np.asarray(target_sizes)
+    height, width = sizes[:, 0].astype(np.float32), sizes[:, 1].astype(np.float32)
+    scale = np.stack([width, height, width, height], axis=1)[:, None, :]
+    xyxy = np.clip(xyxy * scale, 0.0, scale).astype(np.float32)
+    assert xyxy.shape == (batch, k, 4)
+    return scores, labels, xyxy

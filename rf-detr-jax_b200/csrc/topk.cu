@@ -17,7 +17,8 @@
 // answer needs no global sort: the output slot of a key is its rank, the number of keys above
 // it, which is the sum over the cluster's sorted lists of one binary search each; a CTA ranks
 // its own keys and writes the ones below k straight to their slots.
-// Longer rows: one CTA per row and a bitonic sort of the keys in shared memory.
+// Longer rows: for flat scores (C == 1, k <= 4096) the radix select below; otherwise one CTA
+// per row and a bitonic sort of the keys in shared memory (up to 16384 positions).
 #include <algorithm>
 #include <cstdlib>
 
@@ -254,6 +255,191 @@ topk_cluster_kernel(const float *__restrict__ logits, int N, int C, int k, float
     cluster.sync();  // peers read this CTA's keys until here
 }
 
+// ------------------------------------------------------------------------------------------
+// Radix select for long flat score rows (C == 1): the inference post-process selects the top
+// 300 of Q*C = 27,300 sigmoid scores per image (postprocess.py:37-41).  One CTA per row.  A
+// min/max reduction of the row's ordered keys gives their common leading bits; 8-bit histogram
+// passes over the bits below that prefix narrow the k-th largest key T (a pass reads the row
+// from L2; starting below the common prefix keeps the first pass from piling every thread's
+// shared-memory atomic onto one bin when the scores share their top bits, as sigmoid scores
+// do).  An ordered pass then takes every key above T and, among keys equal to T, the lowest
+// positions -- exactly lax.top_k's choice -- and a bitonic sort of those k candidates (64-bit
+// keys with ~position) gives the output order.
+// ------------------------------------------------------------------------------------------
+constexpr int kRadixThreads = 1024;
+constexpr int kRadixMaxK = 4096;
+constexpr long long kRadixMaxPositions = 1LL << 24;
+
+__device__ __forceinline__ unsigned canon_key(float x) {
+    return order_key(x != x ? __uint_as_float(0x7fc00000u) : x);
+}
+
+__global__ void __launch_bounds__(kRadixThreads)
+topk_radix_kernel(const float *__restrict__ scores, int N, int k, float *__restrict__ scores_out,
+                  float *__restrict__ values_out, int32_t *__restrict__ idx_out) {
+    __shared__ unsigned hist[256];
+    __shared__ unsigned long long cand[kRadixMaxK];
+    __shared__ unsigned wsum[kRadixThreads / 32];
+    __shared__ unsigned wmin[kRadixThreads / 32], wmax[kRadixThreads / 32];
+    __shared__ unsigned sh_prefix, sh_need, sh_gt, sh_eq, sh_min, sh_max, sh_cnt;
+    const int r = blockIdx.x;
+    const float *row = scores + (size_t)r * N;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned kmin = 0xffffffffu, kmax = 0u;
+    for (int i = tid; i < N; i += kRadixThreads) {
+        const float x = __ldg(row + i);
+        if (scores_out) scores_out[(size_t)r * N + i] = x != x ? __uint_as_float(0x7fc00000u) : x;
+        const unsigned key = canon_key(x);
+        kmin = min(kmin, key);
+        kmax = max(kmax, key);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+        kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    if (lane == 0) {
+        wmin[warp] = kmin;
+        wmax[warp] = kmax;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        kmin = wmin[lane];
+        kmax = wmax[lane];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+            kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+        }
+        if (lane == 0) {
+            sh_min = kmin;
+            sh_max = kmax;
+        }
+    }
+    __syncthreads();
+    // Bits above `hi` are common to every key of the row.
+    const unsigned diff = sh_min ^ sh_max;
+    const int hi = diff ? 32 - __clz(diff) : 0;
+    unsigned pmask = hi >= 32 ? 0u : ~((1u << hi) - 1u);
+    unsigned prefix = sh_max & pmask;
+    unsigned need = (unsigned)k;  // keys still to take from the current bucket
+    if (tid == 0) sh_cnt = (unsigned)N;  // keys in the current bucket
+    for (int top = hi; top > 0; top -= 8) {
+        const int shift = max(top - 8, 0);
+        const unsigned dmask = (1u << (top - shift)) - 1u;
+        for (int i = tid; i < 256; i += kRadixThreads) hist[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < N; i += kRadixThreads) {
+            const unsigned key = canon_key(__ldg(row + i));
+            if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & dmask], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // Lane l holds bins 255-8l .. 248-8l (descending); find the bucket holding the
+            // `need`-th largest key.
+            unsigned c[8], sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = hist[255 - 8 * lane - j];
+                sum += c[j];
+            }
+            unsigned incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const unsigned excl = incl - sum;
+            if (excl < need && incl >= need) {
+                unsigned cum = excl;
+                int bin = 255 - 8 * lane;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (cum + c[j] >= need) {
+                        bin = 255 - 8 * lane - j;
+                        break;
+                    }
+                    cum += c[j];
+                }
+                sh_prefix = prefix | ((unsigned)bin << shift);
+                sh_need = need - cum;
+                sh_cnt = hist[bin];
+            }
+        }
+        __syncthreads();
+        prefix = sh_prefix;
+        need = sh_need;
+        pmask |= dmask << shift;
+    }
+    // prefix is now the k-th largest key T; `need` keys equal to T are taken (lowest positions).
+    if (tid == 0) {
+        sh_gt = 0u;
+        sh_eq = 0u;
+    }
+    __syncthreads();
+    const unsigned gt_total = (unsigned)k - need;
+    if (need == sh_cnt) {
+        // Every key equal to T is taken: no ordered selection, the sort orders the ties.
+        for (int i = tid; i < N; i += kRadixThreads) {
+            const unsigned key = canon_key(__ldg(row + i));
+            if (key >= prefix)
+                cand[atomicAdd(&sh_gt, 1u)] = ((unsigned long long)key << 32) | (unsigned long long)(0xffffffffu - (unsigned)i);
+        }
+    }
+    for (int c0 = 0; need != sh_cnt && c0 < N; c0 += kRadixThreads) {
+        const int i = c0 + tid;
+        const unsigned key = i < N ? canon_key(__ldg(row + i)) : 0u;
+        const unsigned long long full = ((unsigned long long)key << 32) | (unsigned long long)(0xffffffffu - (unsigned)i);
+        if (i < N && key > prefix) cand[atomicAdd(&sh_gt, 1u)] = full;
+        const bool eq = i < N && key == prefix;
+        const unsigned bal = __ballot_sync(0xffffffffu, eq);
+        if (lane == 0) wsum[warp] = __popc(bal);
+        __syncthreads();
+        if (warp == 0) {
+            const unsigned v = wsum[lane];
+            unsigned incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            wsum[lane] = incl - v;  // exclusive warp offsets
+        }
+        __syncthreads();
+        const unsigned base = sh_eq;
+        const unsigned mine = base + wsum[warp] + __popc(bal & ((1u << lane) - 1u));
+        if (eq && mine < need) cand[gt_total + mine] = full;
+        __syncthreads();
+        if (tid == kRadixThreads - 1) sh_eq = mine + (eq ? 1u : 0u);
+        __syncthreads();
+    }
+    // Sort the k candidates descending (padding with keys below every real key).
+    int P2 = 1;
+    while (P2 < k) P2 <<= 1;
+    for (int i = k + tid; i < P2; i += kRadixThreads) cand[i] = 0ull;
+    __syncthreads();
+    for (int size = 2; size <= P2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < (P2 >> 1); i += kRadixThreads) {
+                const int lo = 2 * i - (i & (stride - 1));
+                const int hi2 = lo + stride;
+                const bool desc = (lo & size) == 0;
+                const unsigned long long a = cand[lo], b2 = cand[hi2];
+                if ((a < b2) == desc) {
+                    cand[lo] = b2;
+                    cand[hi2] = a;
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int i = tid; i < k; i += kRadixThreads) {
+        const unsigned long long key = cand[i];
+        idx_out[(size_t)r * k + i] = (int)(0xffffffffu - (unsigned)(key & 0xffffffffull));
+        if (values_out) values_out[(size_t)r * k + i] = key_to_float((unsigned)(key >> 32));
+    }
+}
+
 template <typename V>
 __global__ void select_rows_kernel(const V *__restrict__ values, long long row_vecs, int N,
                                    const int32_t *__restrict__ idx, int K, V *__restrict__ out,
@@ -297,8 +483,10 @@ using namespace rfdetr;
 extern "C" int rfdetr_topk_select(void *stream, const float *logits, int64_t rows, int64_t positions,
                                   int64_t classes, int64_t k, float *scores_out, float *values_out,
                                   int32_t *indices_out) {
+    const bool radix = classes == 1 && positions > kTopkClusterMaxPositions && positions <= kRadixMaxPositions &&
+                       k <= kRadixMaxK;
     if (rows < 0 || positions <= 0 || classes <= 0 || k <= 0 || k > positions ||
-        positions > kTopkMaxPositions || rows > 2147483647LL || positions * classes > (1LL << 31))
+        (positions > kTopkMaxPositions && !radix) || rows > 2147483647LL || positions * classes > (1LL << 31))
         return RFDETR_ERR_SHAPE;
     if (rows == 0) return RFDETR_OK;
     if (!logits || !indices_out) return RFDETR_ERR_SHAPE;
@@ -311,6 +499,12 @@ extern "C" int rfdetr_topk_select(void *stream, const float *logits, int64_t row
             logits, (int)positions, (int)classes, (int)k, scores_out, values_out, indices_out);
         return launch_status();
     }
+    if (radix && !std::getenv("RFDETR_TOPK_SORT")) {
+        topk_radix_kernel<<<(unsigned)rows, kRadixThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+            logits, (int)positions, (int)k, scores_out, values_out, indices_out);
+        return launch_status();
+    }
+    if (positions > kTopkMaxPositions) return RFDETR_ERR_SHAPE;
     const int P2 = next_pow2((int)positions);
     const size_t smem = (size_t)P2 * sizeof(unsigned long long);
     if (smem > 48 * 1024 &&

@@ -60,7 +60,9 @@ def test_argument_validation_without_a_device(pkg):
     assert lib.rfdetr_msda_backward_workspace_size(1, 8, 16, 16, 576) == 8 * 16 * 16 * 576 * 4
     # Top-k: k out of range, too many positions.
     assert lib.rfdetr_topk_select(None, None, 1, 10, 1, 11, None, None, None) == N.ERR_SHAPE
-    assert lib.rfdetr_topk_select(None, None, 1, 20000, 1, 10, None, None, None) == N.ERR_SHAPE
+    assert lib.rfdetr_topk_select(None, None, 1, 20000, 2, 10, None, None, None) == N.ERR_SHAPE
+    assert lib.rfdetr_topk_select(None, None, 1, 20000, 1, 4097, None, None, None) == N.ERR_SHAPE
+    assert lib.rfdetr_topk_select(None, None, 1, (1 << 24) + 1, 1, 10, None, None, None) == N.ERR_SHAPE
     # Matcher: group count must divide the queries; target cap.
     assert lib.rfdetr_lsap_batched(None, None, None, 1, 10, 3, 3, None, None, None, None) == N.ERR_SHAPE
     assert lib.rfdetr_lsap_batched(None, None, None, 1, 10, 2000, 1, None, None, None, None) == N.ERR_SHAPE

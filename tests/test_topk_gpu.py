@@ -76,7 +76,8 @@ def test_special_values(pkg, monkeypatch, path):
 
 
 @pytest.mark.parametrize(("positions", "classes", "k"), [(1, 1, 1), (7, 3, 7), (576, 91, 1), (1000, 1, 999),
-                                                          (5000, 2, 300), (16384, 1, 16384)])
+                                                          (5000, 2, 300), (16384, 1, 16384), (2049, 1, 2049),
+                                                          (4097, 1, 1), (20000, 1, 4096), (27300, 1, 300)])
 def test_sizes(pkg, positions, classes, k):
     logits = np.random.default_rng(positions).integers(-50, 50, (3, positions, classes)).astype(np.float32)
     s, v, i = _select(pkg, logits, k)
@@ -103,3 +104,38 @@ def test_errors(pkg):
         pkg.top_k(x, 11)
     with pytest.raises(ValueError):
         pkg.top_k(x.double(), 3)
+
+
+def test_inference_post_process_shape(pkg):
+    """The post-process selection (postprocess.py:37-41): top-300 of Q*C = 300*91 flattened
+    sigmoid scores per image, 8 images -- the radix-select path -- bit-exact, with saturated
+    scores (many exact 1.0 ties), NaN, +-inf and -0 in the rows."""
+    rng = np.random.default_rng(27)
+    logits = rng.standard_normal((8, 300 * 91)).astype(np.float32) * 4
+    scores = (1.0 / (1.0 + np.exp(-logits.astype(np.float64)))).astype(np.float32)
+    scores[0, :500] = 1.0            # ties at the top: lower index first
+    scores[1, 123] = np.nan
+    scores[2, 7] = np.inf
+    scores[3, 5:9] = [-0.0, 0.0, -np.inf, np.nan]
+    v, i = pkg.top_k(torch.tensor(scores, device=DEV), 300)
+    wv, wi = OT.top_k(scores, 300)
+    np.testing.assert_array_equal(i.cpu().numpy(), wi)
+    np.testing.assert_array_equal(v.cpu().numpy().view(np.uint32), wv.view(np.uint32))
+
+
+def test_post_process(pkg):
+    """``post_process`` (postprocess.py:19-51) at the inference shape: 8 images x 300 queries x 91
+    classes, top 300.  The selection is checked bit-exact against the oracle on the same sigmoid
+    scores (the sigmoid itself is an elementwise device op); labels exactly; boxes to float32."""
+    rng = np.random.default_rng(31)
+    logits = torch.tensor(rng.standard_normal((8, 300, 91)).astype(np.float32) * 3, device=DEV)
+    boxes = np.concatenate([rng.uniform(0.05, 0.95, (8, 300, 2)), rng.uniform(-0.05, 0.5, (8, 300, 2))], -1)
+    boxes = torch.tensor(boxes.astype(np.float32), device=DEV)
+    sizes = torch.tensor(rng.integers(200, 1300, (8, 2)).astype(np.int32), device=DEV)
+    scores, labels, xyxy = pkg.post_process(logits, boxes, sizes, 300)
+    probs = torch.sigmoid(logits).reshape(8, -1).cpu().numpy()
+    ws, wl, wb = OT.post_process(probs, boxes.cpu().numpy(), sizes.cpu().numpy(), 91, 300)
+    np.testing.assert_array_equal(scores.cpu().numpy().view(np.uint32), ws.view(np.uint32))
+    np.testing.assert_array_equal(labels.cpu().numpy(), wl)
+    np.testing.assert_allclose(xyxy.cpu().numpy(), wb, rtol=1e-6, atol=1e-4)
+    assert labels.dtype == torch.int32 and xyxy.shape == (8, 300, 4)
