@@ -293,6 +293,56 @@ def run_components(torch, device, N, lib, peak):
     }
 
 
+def run_config3(torch, device, N, lib, peak):
+    """Config 3 (4 levels, Lv = 8500, 8 heads x 32, 900 queries, 4 points): forward and backward
+    device time per launch, float32 and bf16, against the algorithmic bytes."""
+    b3, lq3, h3, d3, l3, p3 = 4, 900, 8, 32, 4, 4
+    shapes = ((80, 80), (40, 40), (20, 20), (10, 10))
+    lv3 = sum(a * b for a, b in shapes)
+    rng = np.random.default_rng(3)
+    sh = N.int64_array([x for s in shapes for x in s])
+    st = torch.cuda.current_stream(device).cuda_stream
+    out_line = {"workload": "config3: B=4, 4 levels (80,40,20,10)^2, 8 heads x 32, Lq=900, 4 points"}
+    for name, dt, code in (("f32", torch.float32, N.F32), ("bf16", torch.bfloat16, N.BF16)):
+        value = torch.tensor(rng.standard_normal((b3 * h3, lv3, d3)), dtype=dt, device=device)
+        loc = torch.tensor(rng.uniform(0, 1, (b3, lq3, h3, l3, p3, 2)), dtype=torch.float32, device=device)
+        a = rng.normal(0, 2, (b3, lq3, h3, l3 * p3))
+        a = np.exp(a - a.max(-1, keepdims=True))
+        attn = torch.tensor(a / a.sum(-1, keepdims=True), dtype=dt, device=device)
+        grad = torch.tensor(rng.standard_normal((b3, lq3, h3 * d3)), dtype=dt, device=device)
+        out = torch.empty((b3, lq3, h3 * d3), dtype=dt, device=device)
+        gv, gl, ga = torch.empty_like(value), torch.empty_like(loc), torch.empty_like(attn)
+        wsb = lib.rfdetr_msda_backward_workspace_size(code, b3, h3, d3, lv3)
+        ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=device)
+
+        def fwd():
+            N.check(lib.rfdetr_msda_forward(st, value.data_ptr(), code, sh, None, loc.data_ptr(), attn.data_ptr(), code,
+                                            out.data_ptr(), code, b3, h3, d3, lq3, l3, p3), "c3 forward")
+
+        def bwd():
+            N.check(lib.rfdetr_msda_backward(st, value.data_ptr(), code, sh, None, loc.data_ptr(), attn.data_ptr(),
+                                             code, grad.data_ptr(), code, gv.data_ptr(), gl.data_ptr(), ga.data_ptr(),
+                                             ws.data_ptr(), wsb, b3, h3, d3, lq3, l3, p3), "c3 backward")
+
+        es = value.element_size()
+        fb = value.numel() * es + loc.numel() * 4 + attn.numel() * es + out.numel() * es
+        bb = fb + value.numel() * es + loc.numel() * 4 + attn.numel() * es
+        for kind, fn, nb in (("forward", fwd, fb), ("backward", bwd, bb)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                fn()
+            e1.record()
+            e1.synchronize()
+            ms = e0.elapsed_time(e1) / 20
+            gbs = nb / (ms * 1e-3) / 1e9
+            out_line[f"{kind}_{name}"] = {"ms": ms, "GB/s": gbs, "frac": gbs / peak, "algorithmic_bytes": nb}
+    return out_line
+
+
 def cpu_baseline_sample(steps_budget_s=20.0):
     """The oracle (float32) forward + backward on one image of the workload, single thread."""
     from oracle import msda as O
@@ -582,6 +632,8 @@ def run_ours(args):
     peaks_path_ = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak_ = float(json.load(open(peaks_path_))["hbm_gbs"]) if os.path.exists(peaks_path_) else 6650.0
     components = run_components(torch, device, N, lib, peak_) if (rank == 0 and world == 1) else None
+    if components is not None:
+        components["config3_sampler"] = run_config3(torch, device, N, lib, peak_)
 
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak, peak_src = 6650.0, "fallback"
