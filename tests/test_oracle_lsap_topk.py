@@ -106,6 +106,9 @@ def test_cost_matches_a_torch_restatement():
 
 
 def test_topk_contract():
+    """The reference's known-answer selection (tests/test_parity_tools.py:226-236: scores
+    [5, 4, 4, 1, 0.5, 0.1] select [0, 1, 2], the tied 4s in index order), then the documented
+    lax.top_k order over special values (NaN first, then +inf, ..., +0 above -0, -inf last)."""
     scores = np.array([[5.0, 4.0, 4.0, 1.0, 0.5, 0.1]], np.float32)
     values, idx = OT.top_k(scores, 3)
     np.testing.assert_array_equal(idx, [[0, 1, 2]])
