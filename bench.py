@@ -245,6 +245,24 @@ def run_components(torch, device, N, lib, peak):
     ms_cost = dev_ms(costs, 30)
     ms_lsap = dev_ms(lsap, 10)
     N.check(int(status.item()), "lsap device status")
+
+    # Set losses of every layer on the assignment just solved (IA-BCE, L1, GIoU with gradients).
+    l_rows, l_cols, l_valid = (x.view(C4_LAYERS, C4_B, slots) for x in (a_rows, a_cols, a_valid))
+    num_boxes = torch.tensor([float(C4_G * sizes.sum())], dtype=torch.float32, device=device)
+    losses = torch.empty((C4_LAYERS, 3), dtype=torch.float32, device=device)
+    g_logits = torch.empty_like(d_logits)
+    g_l1 = torch.empty_like(d_boxes)
+    g_giou = torch.empty_like(d_boxes)
+
+    def set_losses():
+        N.check(lib.rfdetr_set_losses(st, d_logits.data_ptr(), d_boxes.data_ptr(), d_labels.data_ptr(),
+                                      d_tboxes.data_ptr(), l_rows.data_ptr(), l_cols.data_ptr(), l_valid.data_ptr(),
+                                      num_boxes.data_ptr(), C4_LAYERS, C4_B, C4_Q, C4_C, C4_T, slots, 0.25, 1,
+                                      losses.data_ptr(), g_logits.data_ptr(), g_l1.data_ptr(), g_giou.data_ptr()),
+                "set losses")
+
+    ms_loss = dev_ms(set_losses, 50)
+    loss_bytes = C4_LAYERS * (C4_B * C4_Q * (C4_C * 8 + 4 * 4 * 3) + C4_B * slots * 9 + C4_B * C4_T * 20)
     topk_bytes = rows * C4_POS * C4_C * 4 + rows * C4_POS * 4 + 2 * rows * C4_K * 4
     cost_bytes = C4_LAYERS * (C4_B * C4_Q * (C4_C + 4) * 4 + C4_B * C4_T * 9 + C4_B * C4_Q * C4_T * 4)
 
@@ -273,6 +291,12 @@ def run_components(torch, device, N, lib, peak):
         t0 = time.perf_counter()
         pool.map(_scipy_image, tasks)
         cpu_lsap_n = time.perf_counter() - t0
+    from oracle import losses as OL
+
+    h_rows, h_cols, h_valid = (x.cpu().numpy() for x in (l_rows[0], l_cols[0], l_valid[0]))
+    t0 = time.perf_counter()
+    OL.set_losses(logits[0], boxes[0], labels, tboxes, h_rows, h_cols, h_valid.astype(bool), float(C4_G * sizes.sum()))
+    cpu_loss = (time.perf_counter() - t0) * C4_LAYERS
     gbs = lambda nbytes, ms: nbytes / (ms * 1e-3) / 1e9  # noqa: E731
     return {
         "workload": f"config4 training shape: top-{C4_K} of {C4_G}x{C4_B} rows of {C4_POS}x{C4_C} logits; "
@@ -290,6 +314,10 @@ def run_components(torch, device, N, lib, peak):
                          "bound": "latency",
                          "cpu_ms_1core": cpu_lsap_1 * 1e3, f"cpu_ms_{cores}cores": cpu_lsap_n * 1e3,
                          "cpu_kind": "reference (scipy.optimize.linear_sum_assignment, the reference's solver)"},
+        "set_losses": {"ms": ms_loss, "GB/s": gbs(loss_bytes, ms_loss), "frac": gbs(loss_bytes, ms_loss) / peak,
+                       "algorithmic_bytes": loss_bytes, "workload": f"{C4_LAYERS} layers of {C4_B}x{C4_Q}x{C4_C}",
+                       "cpu_ms": cpu_loss * 1e3,
+                       "cpu_kind": f"port (oracle/losses.py float64 torch autograd), {torch.get_num_threads()} threads"},
     }
 
 

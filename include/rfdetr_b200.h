@@ -192,6 +192,37 @@ int rfdetr_lsap_batched(void *stream, const float *cost, const int32_t *sizes, i
                         int64_t queries, int64_t max_targets, int64_t group_detr, int32_t *rows,
                         int32_t *cols, uint8_t *valid, int32_t *status_out);
 
+/* ---------------------------------------------------------------------------------------
+ * Set-prediction losses of every decoder layer, with gradients, in one launch.
+ *
+ * Replaces loss_labels (criterion.py:157-217) and loss_boxes (criterion.py:247-265), called by
+ * the reference once per output layer; here layer l of `layers` is one slice of each [L, ...]
+ * argument (the targets are shared):
+ *   losses_out[l, 0], ia_bce != 0 (IA-BCE, criterion.py:188-208): sum over [B, Q, C] of
+ *     (neg * x - log_sigmoid(x) * (pos + neg)) / num_boxes, pos/neg = (w, 1 - w) at the matched
+ *     (image, query, class) entries, with the stop-gradient weight
+ *     w = max(sigmoid(x)^alpha * iou^(1 - alpha), 0.01), and (0, sigmoid(x)^2) elsewhere;
+ *   losses_out[l, 0], ia_bce == 0 (criterion.py:210-230): the sigmoid focal loss (gamma 2,
+ *     alpha_t from focal_alpha, none when it is negative) of the one-hot matched targets,
+ *     summed over [B, Q, C] and divided by num_boxes;
+ *   losses_out[l, 1] = sum over valid matches of |box - target box|_1 / num_boxes;
+ *   losses_out[l, 2] = sum over valid matches of (1 - GIoU) / num_boxes.
+ * Also writes the gradients for unit cotangents: grad_logits [L, B, Q, C] = d losses_out[l, 0]
+ * / d logits, grad_boxes_l1 / grad_boxes_giou [L, B, Q, 4] = d losses_out[l, 1] / d boxes and
+ * d losses_out[l, 2] / d boxes (zero for unmatched queries).
+ *   pred_logits [L, B, Q, C] f32, pred_boxes [L, B, Q, 4] f32 cxcywh, target_labels [B, T]
+ *   int32, target_boxes [B, T, 4] f32, rows/cols [L, B, S] int32 and valid [L, B, S] uint8
+ *   from rfdetr_lsap_batched (a query is matched at most once per layer), num_boxes: device f32
+ *   scalar, losses_out: device f32 [L, 3] (cleared on `stream` first).  Box arrays must be
+ *   16-byte aligned (RFDETR_ERR_ALIGN otherwise).
+ * ------------------------------------------------------------------------------------- */
+int rfdetr_set_losses(void *stream, const float *pred_logits, const float *pred_boxes,
+                      const int32_t *target_labels, const float *target_boxes, const int32_t *rows,
+                      const int32_t *cols, const uint8_t *valid, const float *num_boxes, int64_t layers,
+                      int64_t batch, int64_t queries, int64_t classes, int64_t targets, int64_t slots,
+                      float focal_alpha, int32_t ia_bce, float *losses_out, float *grad_logits,
+                      float *grad_boxes_l1, float *grad_boxes_giou);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,12 +8,14 @@ Components (each a thin host wrapper over ``librfdetr_b200.so``, see ``include/r
 * :mod:`.ops`     -- multi-scale deformable attention, sampler ``"cuda"``, forward + backward;
 * :mod:`.topk`    -- two-stage query selection (class max + top-k) and ``select_rows``;
 * :mod:`.matcher` -- matching cost and exact batched assignment (SciPy-identical);
-* :mod:`.postprocess` -- inference post-process (top-k over all query/class pairs).
+* :mod:`.postprocess` -- inference post-process (top-k over all query/class pairs);
+* :mod:`.losses` -- IA-BCE and matched-pair box losses of one layer, with gradients.
 """
 
 from . import _native
 from .matcher import CriterionConfig, build_cost_matrix, hungarian_match
 from .ops import MSDeformAttnFunction, ms_deform_attn, ms_deform_attn_core, ms_deform_attn_core_rows
+from .losses import SetLossFunction, set_losses
 from .postprocess import post_process
 from .topk import select_rows, top_k, two_stage_topk
 
@@ -26,6 +28,8 @@ __all__ = [
     "ms_deform_attn_core",
     "ms_deform_attn_core_rows",
     "post_process",
+    "set_losses",
+    "SetLossFunction",
     "select_rows",
     "top_k",
     "two_stage_topk",
