@@ -195,14 +195,14 @@ int rfdetr_lsap_batched(void *stream, const float *cost, const int32_t *sizes, i
 /* ---------------------------------------------------------------------------------------
  * Set-prediction losses of every decoder layer, with gradients, in one launch.
  *
- * Replaces loss_labels (criterion.py:157-217) and loss_boxes (criterion.py:247-265), called by
+ * Replaces loss_labels (criterion.py:157-224) and loss_boxes (criterion.py:233-250), called by
  * the reference once per output layer; here layer l of `layers` is one slice of each [L, ...]
  * argument (the targets are shared):
  *   losses_out[l, 0], ia_bce != 0 (IA-BCE, criterion.py:188-208): sum over [B, Q, C] of
  *     (neg * x - log_sigmoid(x) * (pos + neg)) / num_boxes, pos/neg = (w, 1 - w) at the matched
  *     (image, query, class) entries, with the stop-gradient weight
  *     w = max(sigmoid(x)^alpha * iou^(1 - alpha), 0.01), and (0, sigmoid(x)^2) elsewhere;
- *   losses_out[l, 0], ia_bce == 0 (criterion.py:210-230): the sigmoid focal loss (gamma 2,
+ *   losses_out[l, 0], ia_bce == 0 (criterion.py:210-224): the sigmoid focal loss (gamma 2,
  *     alpha_t from focal_alpha, none when it is negative) of the one-hot matched targets,
  *     summed over [B, Q, C] and divided by num_boxes;
  *   losses_out[l, 1] = sum over valid matches of |box - target box|_1 / num_boxes;

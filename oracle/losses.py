@@ -8,9 +8,9 @@ Restates, in float64 torch on the host, the reference's matched-pair losses:
   ``box_ops.py:78-91``) and negative weight ``1 - w``; every other entry has positive weight 0
   and negative weight ``p^2`` (differentiated); ``loss = sum(neg * x - log_sigmoid(x) * (pos +
   neg)) / num_boxes``;
-* ``loss_labels`` without IA-BCE (``criterion.py:210-230``): the sigmoid focal loss (gamma 2) of
+* ``loss_labels`` without IA-BCE (``criterion.py:210-224``): the sigmoid focal loss (gamma 2) of
   the one-hot matched targets, ``mean(1).sum() / num_boxes`` times the query count;
-* ``loss_boxes`` (``criterion.py:247-265``): L1 and ``1 - GIoU`` (``box_ops.py:94-103``) over
+* ``loss_boxes`` (``criterion.py:233-250``): L1 and ``1 - GIoU`` (``box_ops.py:94-103``) over
   valid matched pairs, each divided by ``num_boxes``.
 
 Gradients come from torch autograd, so they follow the reference's own differentiation of the
@@ -79,7 +79,7 @@ def set_losses(pred_logits, pred_boxes, target_labels, target_boxes, rows, cols,
     else:
         loss_ce = _focal(x, tcls, bidx, rows, valid, num_boxes, focal_alpha)
 
-    # loss_boxes (criterion.py:247-265).
+    # loss_boxes (criterion.py:233-250).
     srcb = pb[bidx, rclip]
     w = valid.to(torch.float64)
     l1 = ((srcb - tgt).abs().sum(-1) * w).sum() / num_boxes
@@ -109,7 +109,7 @@ def _ia_bce(x, pb, tgt, tcls, bidx, rows, rclip, valid, num_boxes, focal_alpha):
 
 
 def _focal(x, tcls, bidx, rows, valid, num_boxes, alpha, gamma=2.0):
-    """loss_labels without IA-BCE (criterion.py:210-230): sigmoid focal loss of the one-hot matched
+    """loss_labels without IA-BCE (criterion.py:210-224): sigmoid focal loss of the one-hot matched
     targets, ``mean(1).sum() / num_boxes`` times the query count."""
     sel = valid
     onehot = torch.zeros_like(x).index_put((bidx[sel], rows[sel], tcls[sel]), torch.ones(int(sel.sum()),

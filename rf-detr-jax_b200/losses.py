@@ -1,6 +1,6 @@
 """Set-prediction losses on B200 (IA-BCE or focal classification, L1 and GIoU box terms over
 matched pairs), mirroring ``loss_labels`` / ``loss_boxes`` of
-``src/rfdetr_jax/models/criterion.py:157-265``.
+``src/rfdetr_jax/models/criterion.py:157-250``.
 
 One library launch computes the three losses of every stacked layer and their gradients with
 respect to the logits and the boxes; :class:`SetLossFunction` returns the losses and, in
@@ -64,9 +64,9 @@ class SetLossFunction(torch.autograd.Function):
 
 def set_losses(pred_logits, pred_boxes, target_labels, target_boxes, rows, cols, valid, num_boxes, focal_alpha=0.25,
                ia_bce=True):
-    """``(loss_ce, loss_bbox, loss_giou)``: ``loss_labels`` (``criterion.py:157-217``; IA-BCE when
+    """``(loss_ce, loss_bbox, loss_giou)``: ``loss_labels`` (``criterion.py:157-224``; IA-BCE when
     ``ia_bce``, else the sigmoid focal loss with gamma 2) and the matched-pair box losses
-    (``criterion.py:247-265``), differentiable with respect to ``pred_logits`` and ``pred_boxes``.
+    (``criterion.py:233-250``), differentiable with respect to ``pred_logits`` and ``pred_boxes``.
 
     ``pred_logits [..., B, Q, C]`` and ``pred_boxes [..., B, Q, 4]`` may carry leading layer axes
     (all layers in one launch); ``rows/cols/valid [..., B, S]`` are the matcher's outputs for the
