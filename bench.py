@@ -246,6 +246,17 @@ def run_components(torch, device, N, lib, peak):
     ms_lsap = dev_ms(lsap, 10)
     N.check(int(status.item()), "lsap device status")
 
+    # Both in one call over the stacked layers (one cost launch, one solve launch).
+    def stacked():
+        N.check(lib.rfdetr_match_stacked(st, d_logits.data_ptr(), N.F32, d_boxes.data_ptr(), N.F32,
+                                         d_labels.data_ptr(), d_tboxes.data_ptr(), d_mask.data_ptr(),
+                                         d_sizes.data_ptr(), C4_LAYERS, C4_B, C4_Q, C4_C, C4_T, C4_G, 2.0, 5.0, 2.0,
+                                         0.25, cost.data_ptr(), a_rows.data_ptr(), a_cols.data_ptr(),
+                                         a_valid.data_ptr(), status.data_ptr()), "stacked match")
+
+    ms_stacked = dev_ms(stacked, 10)
+    N.check(int(status.item()), "stacked match device status")
+
     # Set losses of every layer on the assignment just solved (IA-BCE, L1, GIoU with gradients).
     l_rows, l_cols, l_valid = (x.view(C4_LAYERS, C4_B, slots) for x in (a_rows, a_cols, a_valid))
     num_boxes = torch.tensor([float(C4_G * sizes.sum())], dtype=torch.float32, device=device)
@@ -314,6 +325,8 @@ def run_components(torch, device, N, lib, peak):
                          "bound": "latency",
                          "cpu_ms_1core": cpu_lsap_1 * 1e3, f"cpu_ms_{cores}cores": cpu_lsap_n * 1e3,
                          "cpu_kind": "reference (scipy.optimize.linear_sum_assignment, the reference's solver)"},
+        "match_stacked": {"ms": ms_stacked, "bound": "latency",
+                          "workload": f"cost + exact assignment of {C4_LAYERS}x{C4_B}x{C4_G} blocks in one call"},
         "set_losses": {"ms": ms_loss, "GB/s": gbs(loss_bytes, ms_loss), "frac": gbs(loss_bytes, ms_loss) / peak,
                        "algorithmic_bytes": loss_bytes, "workload": f"{C4_LAYERS} layers of {C4_B}x{C4_Q}x{C4_C}",
                        "cpu_ms": cpu_loss * 1e3,

@@ -193,6 +193,26 @@ int rfdetr_lsap_batched(void *stream, const float *cost, const int32_t *sizes, i
                         int32_t *cols, uint8_t *valid, int32_t *status_out);
 
 /* ---------------------------------------------------------------------------------------
+ * Matching cost and exact assignment of stacked layers in one call.
+ *
+ * Replaces the stacked layer_cost + single solve of compute_losses (criterion.py:402-413): the
+ * cost of every layer (one rfdetr_match_cost launch over all layers and images) followed by one
+ * rfdetr_lsap_batched over all (layer, image, group) blocks, on `stream`.
+ *   pred_logits [L, B, Q, C] and pred_boxes [L, B, Q, 4] (f32 or bf16); target_labels [B, T]
+ *   int32, target_boxes [B, T, 4] f32, target_mask [B, T] uint8 and sizes [B] int32 are shared
+ *   by the layers.  cost [L, B, Q, T] f32 receives the cost (the solver's input); rows/cols
+ *   [L, B, G*T] int32 and valid [L, B, G*T] uint8 the assignment; *status_out (device int32)
+ *   as for rfdetr_lsap_batched.  Results are bit for bit those of the two separate calls.
+ * Limits: those of both entry points, and L * B <= 65535.
+ * ------------------------------------------------------------------------------------- */
+int rfdetr_match_stacked(void *stream, const void *pred_logits, int logits_dtype, const void *pred_boxes,
+                         int boxes_dtype, const int32_t *target_labels, const float *target_boxes,
+                         const uint8_t *target_mask, const int32_t *sizes, int64_t layers, int64_t batch,
+                         int64_t queries, int64_t classes, int64_t targets, int64_t group_detr,
+                         float cost_class, float cost_bbox, float cost_giou, float focal_alpha, float *cost,
+                         int32_t *rows, int32_t *cols, uint8_t *valid, int32_t *status_out);
+
+/* ---------------------------------------------------------------------------------------
  * Set-prediction losses of every decoder layer, with gradients, in one launch.
  *
  * Replaces loss_labels (criterion.py:157-224) and loss_boxes (criterion.py:233-250), called by

@@ -9,11 +9,11 @@ Components (each a thin host wrapper over ``librfdetr_b200.so``, see ``include/r
 * :mod:`.topk`    -- two-stage query selection (class max + top-k) and ``select_rows``;
 * :mod:`.matcher` -- matching cost and exact batched assignment (SciPy-identical);
 * :mod:`.postprocess` -- inference post-process (top-k over all query/class pairs);
-* :mod:`.losses` -- IA-BCE and matched-pair box losses of one layer, with gradients.
+* :mod:`.losses` -- IA-BCE or focal and matched-pair box losses of stacked layers, with gradients.
 """
 
 from . import _native
-from .matcher import CriterionConfig, build_cost_matrix, hungarian_match
+from .matcher import CriterionConfig, build_cost_matrix, hungarian_match, match_stacked
 from .ops import MSDeformAttnFunction, ms_deform_attn, ms_deform_attn_core, ms_deform_attn_core_rows
 from .losses import SetLossFunction, set_losses
 from .postprocess import post_process
@@ -24,6 +24,7 @@ __all__ = [
     "MSDeformAttnFunction",
     "build_cost_matrix",
     "hungarian_match",
+    "match_stacked",
     "ms_deform_attn",
     "ms_deform_attn_core",
     "ms_deform_attn_core_rows",

@@ -16,8 +16,8 @@
 //     distance, ties going to an unassigned column (the later one in the work list), else to the
 //     earliest one in the work list.
 // One CTA solves one block: the column scan of each augmenting step is spread over the CTA's
-// threads and the arg-min is a CTA reduction under that tie order.  The block's costs are staged
-// in shared memory when they fit the per-CTA budget, otherwise read from L2.
+// threads and the arg-min is a CTA reduction under that tie order.  The block's costs are read
+// through L1 (optionally staged in shared memory up to a per-CTA budget).
 #include <algorithm>
 
 #include "common.cuh"
@@ -37,19 +37,20 @@ template <typename TL, typename TB>
 __global__ void __launch_bounds__(kCostThreads)
 match_cost_kernel(const TL *__restrict__ logits, const TB *__restrict__ boxes, const int32_t *__restrict__ labels,
                   const float *__restrict__ tboxes, const uint8_t *__restrict__ tmask, float *__restrict__ cost,
-                  int Q, int C, int T, int q_tile, float cost_class, float cost_bbox, float cost_giou,
-                  float alpha) {
+                  int Q, int C, int T, int q_tile, int target_batch, float cost_class, float cost_bbox,
+                  float cost_giou, float alpha) {
     extern __shared__ float tsm[];  // [kTargetFields][T]
-    const int b = blockIdx.y;
+    const int b = blockIdx.y;                 // (layer, image) row of the predictions and the cost
+    const int bt = blockIdx.y % target_batch;  // image of the targets (shared by stacked layers)
     const int q0 = blockIdx.x * q_tile;
     for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        const float cx = __ldg(tboxes + ((size_t)b * T + t) * 4 + 0);
-        const float cy = __ldg(tboxes + ((size_t)b * T + t) * 4 + 1);
-        const float w = __ldg(tboxes + ((size_t)b * T + t) * 4 + 2);
-        const float h = __ldg(tboxes + ((size_t)b * T + t) * 4 + 3);
+        const float cx = __ldg(tboxes + ((size_t)bt * T + t) * 4 + 0);
+        const float cy = __ldg(tboxes + ((size_t)bt * T + t) * 4 + 1);
+        const float w = __ldg(tboxes + ((size_t)bt * T + t) * 4 + 2);
+        const float h = __ldg(tboxes + ((size_t)bt * T + t) * 4 + 3);
         const float wc = fmaxf(w, 0.f), hc = fmaxf(h, 0.f);  // box_ops.py:30-31 clip
-        tsm[0 * T + t] = __int_as_float(__ldg(labels + (size_t)b * T + t));
-        tsm[1 * T + t] = __ldg(tmask + (size_t)b * T + t) ? 1.f : 0.f;
+        tsm[0 * T + t] = __int_as_float(__ldg(labels + (size_t)bt * T + t));
+        tsm[1 * T + t] = __ldg(tmask + (size_t)bt * T + t) ? 1.f : 0.f;
         tsm[2 * T + t] = cx;
         tsm[3 * T + t] = cy;
         tsm[4 * T + t] = w;
@@ -154,7 +155,8 @@ __device__ __forceinline__ Cand shfl_cand(const Cand &c, int o) {
 
 struct LsapArgs {
     const float *cost;
-    const int32_t *sizes;
+    const int32_t *sizes;  // problem n (a (layer, image) row of the cost) uses sizes[n % size_mod]
+    int size_mod;
     int Q, T, G, Qg;
     int smem_cost_floats;  // capacity of the shared cost stage (0 = never stage)
     int32_t *rows, *cols;
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(kLsapThreads) lsap_kernel(const LsapArgs a) {
         a.cols[obase + k] = 0;
         a.valid[obase + k] = 0;
     }
-    int size = __ldg(a.sizes + n);
+    int size = __ldg(a.sizes + n % a.size_mod);
     size = max(0, min(size, T));
     if (size == 0) return;
 
@@ -403,11 +405,15 @@ size_t lsap_state_bytes(int M) {
 
 using namespace rfdetr;
 
-extern "C" int rfdetr_match_cost(void *stream, const void *pred_logits, int logits_dtype, const void *pred_boxes,
-                                 int boxes_dtype, const int32_t *target_labels, const float *target_boxes,
-                                 const uint8_t *target_mask, float *cost, int64_t batch, int64_t queries,
-                                 int64_t classes, int64_t targets, float cost_class, float cost_bbox,
-                                 float cost_giou, float focal_alpha) {
+namespace {
+
+// The cost of `batch` prediction rows (a row: Q queries), row y against target image
+// y % target_batch.
+int launch_match_cost(void *stream, const void *pred_logits, int logits_dtype, const void *pred_boxes,
+                      int boxes_dtype, const int32_t *target_labels, const float *target_boxes,
+                      const uint8_t *target_mask, float *cost, int64_t batch, int64_t target_batch, int64_t queries,
+                      int64_t classes, int64_t targets, float cost_class, float cost_bbox, float cost_giou,
+                      float focal_alpha) {
     if ((logits_dtype != RFDETR_F32 && logits_dtype != RFDETR_BF16) ||
         (boxes_dtype != RFDETR_F32 && boxes_dtype != RFDETR_BF16))
         return RFDETR_ERR_DTYPE;
@@ -429,8 +435,8 @@ extern "C" int rfdetr_match_cost(void *stream, const void *pred_logits, int logi
 #define RFDETR_COST_LAUNCH(TL, TB)                                                                        \
     match_cost_kernel<TL, TB><<<grid, kCostThreads, smem, s>>>(                                           \
         static_cast<const TL *>(pred_logits), static_cast<const TB *>(pred_boxes), target_labels,        \
-        target_boxes, target_mask, cost, (int)queries, (int)classes, T, q_tile, cost_class, cost_bbox,  \
-        cost_giou, focal_alpha)
+        target_boxes, target_mask, cost, (int)queries, (int)classes, T, q_tile, (int)target_batch,      \
+        cost_class, cost_bbox, cost_giou, focal_alpha)
     if (logits_dtype == RFDETR_F32 && boxes_dtype == RFDETR_F32) RFDETR_COST_LAUNCH(float, float);
     else if (logits_dtype == RFDETR_F32) RFDETR_COST_LAUNCH(float, bf16);
     else if (boxes_dtype == RFDETR_F32) RFDETR_COST_LAUNCH(bf16, float);
@@ -439,9 +445,10 @@ extern "C" int rfdetr_match_cost(void *stream, const void *pred_logits, int logi
     return launch_status();
 }
 
-extern "C" int rfdetr_lsap_batched(void *stream, const float *cost, const int32_t *sizes, int64_t problems,
-                                   int64_t queries, int64_t max_targets, int64_t group_detr, int32_t *rows,
-                                   int32_t *cols, uint8_t *valid, int32_t *status_out) {
+// The exact assignment of `problems` cost rows (a row: Q x T), row n with sizes[n % size_mod].
+int launch_lsap(void *stream, const float *cost, const int32_t *sizes, int64_t size_mod, int64_t problems,
+                int64_t queries, int64_t max_targets, int64_t group_detr, int32_t *rows, int32_t *cols,
+                uint8_t *valid, int32_t *status_out) {
     if (problems < 0 || queries <= 0 || max_targets <= 0 || group_detr <= 0 || queries % group_detr != 0 ||
         max_targets > kLsapMaxTargets || queries / group_detr > kLsapMaxGroup ||
         problems * group_detr > 2147483647LL || problems * queries * max_targets > (1LL << 40))
@@ -454,6 +461,7 @@ extern "C" int rfdetr_lsap_batched(void *stream, const float *cost, const int32_
     LsapArgs a;
     a.cost = cost;
     a.sizes = sizes;
+    a.size_mod = (int)size_mod;
     a.Q = (int)queries;
     a.T = (int)max_targets;
     a.G = (int)group_detr;
@@ -464,12 +472,13 @@ extern "C" int rfdetr_lsap_batched(void *stream, const float *cost, const int32_
     a.status = status_out;
     const int M = std::max(a.Qg, a.T);
     const size_t state = lsap_state_bytes(M);
-    // Stage costs in shared memory up to a budget that still lets two CTAs share an SM; larger
-    // blocks are read from L2.
+    // Costs are read through L1 by default: staging blocks in shared memory measured slower at
+    // config 4 (277 vs 265 us with a 100 KB stage; fewer CTAs fit an SM).  RFDETR_LSAP_STAGE_KB
+    // sets a stage budget per CTA.
     int dev = 0, optin = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    size_t budget = 100 * 1024;
+    size_t budget = 0;
     if (const char *e = getenv("RFDETR_LSAP_STAGE_KB")) budget = (size_t)atoi(e) * 1024;
     const size_t want = (size_t)a.Qg * a.T * sizeof(float);
     size_t stage = std::min(want, budget > state ? budget - state : 0);
@@ -482,4 +491,44 @@ extern "C" int rfdetr_lsap_batched(void *stream, const float *cost, const int32_
         return RFDETR_ERR_CUDA;
     lsap_kernel<<<(unsigned)(problems * group_detr), kLsapThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
     return launch_status();
+}
+
+}  // namespace
+
+extern "C" int rfdetr_match_cost(void *stream, const void *pred_logits, int logits_dtype, const void *pred_boxes,
+                                 int boxes_dtype, const int32_t *target_labels, const float *target_boxes,
+                                 const uint8_t *target_mask, float *cost, int64_t batch, int64_t queries,
+                                 int64_t classes, int64_t targets, float cost_class, float cost_bbox,
+                                 float cost_giou, float focal_alpha) {
+    return launch_match_cost(stream, pred_logits, logits_dtype, pred_boxes, boxes_dtype, target_labels, target_boxes,
+                             target_mask, cost, batch, batch, queries, classes, targets, cost_class, cost_bbox,
+                             cost_giou, focal_alpha);
+}
+
+extern "C" int rfdetr_lsap_batched(void *stream, const float *cost, const int32_t *sizes, int64_t problems,
+                                   int64_t queries, int64_t max_targets, int64_t group_detr, int32_t *rows,
+                                   int32_t *cols, uint8_t *valid, int32_t *status_out) {
+    return launch_lsap(stream, cost, sizes, problems, problems, queries, max_targets, group_detr, rows, cols, valid,
+                       status_out);
+}
+
+extern "C" int rfdetr_match_stacked(void *stream, const void *pred_logits, int logits_dtype, const void *pred_boxes,
+                                    int boxes_dtype, const int32_t *target_labels, const float *target_boxes,
+                                    const uint8_t *target_mask, const int32_t *sizes, int64_t layers, int64_t batch,
+                                    int64_t queries, int64_t classes, int64_t targets, int64_t group_detr,
+                                    float cost_class, float cost_bbox, float cost_giou, float focal_alpha,
+                                    float *cost, int32_t *rows, int32_t *cols, uint8_t *valid, int32_t *status_out) {
+    if (layers < 0 || batch < 0 || layers > 65535 || batch > 65535 || layers * batch > 65535) return RFDETR_ERR_SHAPE;
+    if (layers == 0 || batch == 0) return RFDETR_OK;
+    // Check the solver's limits before launching the cost.
+    if (queries <= 0 || targets <= 0 || group_detr <= 0 || queries % group_detr != 0 || targets > kLsapMaxTargets ||
+        queries / group_detr > kLsapMaxGroup)
+        return RFDETR_ERR_SHAPE;
+    if (!sizes || !rows || !cols || !valid || !status_out) return RFDETR_ERR_SHAPE;
+    const int st = launch_match_cost(stream, pred_logits, logits_dtype, pred_boxes, boxes_dtype, target_labels,
+                                     target_boxes, target_mask, cost, layers * batch, batch, queries, classes, targets,
+                                     cost_class, cost_bbox, cost_giou, focal_alpha);
+    if (st != RFDETR_OK) return st;
+    return launch_lsap(stream, cost, sizes, batch, layers * batch, queries, targets, group_detr, rows, cols, valid,
+                       status_out);
 }

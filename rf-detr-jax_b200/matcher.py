@@ -8,6 +8,8 @@ Mirrors ``src/rfdetr_jax/models/matcher.py`` and the solver switch of
 * :func:`hungarian_match` -- ``(cost [..., B, Q, T], sizes [B], group_detr) -> (rows, cols,
   valid)`` each ``[..., B, group_detr * T]`` (``matcher.py:182-208``), solved on the device with
   SciPy's algorithm and tie rules, so the assignment equals the reference's host solve;
+* :func:`match_stacked` -- cost and assignment of all stacked layers in one call
+  (``criterion.py:402-413``: the stacked ``layer_cost`` then one ``solve``);
 * :class:`CriterionConfig` -- ``solve`` dispatch with ``matcher="cuda"``.
 """
 
@@ -50,6 +52,58 @@ def build_cost_matrix(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targe
         float(cost_class), float(cost_bbox), float(cost_giou), float(focal_alpha))
     N.check(status, "rfdetr_match_cost")
     return cost
+
+
+def match_stacked(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, target_labels: torch.Tensor,
+                  target_boxes: torch.Tensor, target_mask: torch.Tensor, sizes: torch.Tensor, group_detr: int,
+                  cost_class: float, cost_bbox: float, cost_giou: float, focal_alpha: float, check: bool = True):
+    """Cost and exact assignment of every stacked layer in one call: one cost launch over all
+    layers and images, then one batched solve (bit for bit :func:`build_cost_matrix` per layer
+    followed by :func:`hungarian_match` of the stacked cost).
+
+    Args:
+        pred_logits ``[..., B, Q, C]``, pred_boxes ``[..., B, Q, 4]`` (leading axes: layers);
+        target_labels ``[B, T]``, target_boxes ``[B, T, 4]``, target_mask ``[B, T]`` shared by the
+        layers; sizes ``[B]``; group_detr divides ``Q``.
+
+    Returns:
+        ``(cost [..., B, Q, T] float32, rows int32, cols int32, valid bool)``, the last three
+        ``[..., B, group_detr * T]``.
+    """
+    N.require_cuda(pred_logits, pred_boxes, target_labels, target_boxes, target_mask, sizes)
+    if pred_logits.dim() < 3:
+        raise ValueError("pred_logits must be [..., B, Q, C]")
+    leading = pred_logits.shape[:-3]
+    batch, queries, classes = pred_logits.shape[-3:]
+    targets = target_labels.shape[-1]
+    if pred_boxes.shape != (*leading, batch, queries, 4) or target_labels.shape != (batch, targets) \
+            or target_boxes.shape != (batch, targets, 4) or target_mask.shape != (batch, targets) \
+            or sizes.shape != (batch,):
+        raise ValueError("inconsistent shapes for match_stacked")
+    if group_detr < 1 or queries % group_detr:
+        raise ValueError("group_detr must be positive and divide the query count")
+    layers = 1
+    for d in leading:
+        layers *= d
+    dev = pred_logits.device
+    logits = pred_logits.contiguous()
+    boxes = pred_boxes.contiguous()
+    slots = group_detr * targets
+    cost = torch.empty((*leading, batch, queries, targets), dtype=torch.float32, device=dev)
+    rows = torch.empty((*leading, batch, slots), dtype=torch.int32, device=dev)
+    cols = torch.empty_like(rows)
+    valid = torch.empty((*leading, batch, slots), dtype=torch.uint8, device=dev)
+    status_buf = torch.zeros((1,), dtype=torch.int32, device=dev)
+    status = N.lib().rfdetr_match_stacked(
+        N.stream_of(logits), N.ptr(logits), N.dtype_code(logits.dtype), N.ptr(boxes), N.dtype_code(boxes.dtype),
+        N.ptr(target_labels.to(torch.int32).contiguous()), N.ptr(target_boxes.to(torch.float32).contiguous()),
+        N.ptr(target_mask.to(torch.uint8).contiguous()), N.ptr(sizes.to(torch.int32).contiguous()), layers, batch,
+        queries, classes, targets, group_detr, float(cost_class), float(cost_bbox), float(cost_giou),
+        float(focal_alpha), N.ptr(cost), N.ptr(rows), N.ptr(cols), N.ptr(valid), N.ptr(status_buf))
+    N.check(status, "rfdetr_match_stacked")
+    if check:
+        N.check(int(status_buf.item()), "rfdetr_match_stacked (device status)")
+    return cost, rows, cols, valid.to(torch.bool)
 
 
 def hungarian_match(cost: torch.Tensor, sizes: torch.Tensor, group_detr: int, check: bool = True):
@@ -114,3 +168,13 @@ class CriterionConfig:
     def cost(self, pred_logits, pred_boxes, target_labels, target_boxes, target_mask):
         return build_cost_matrix(pred_logits, pred_boxes, target_labels, target_boxes, target_mask,
                                  self.set_cost_class, self.set_cost_bbox, self.set_cost_giou, self.focal_alpha)
+
+    def match(self, pred_logits, pred_boxes, target_labels, target_boxes, target_mask, sizes, group_detr):
+        """The stacked ``layer_cost`` + ``solve`` of ``compute_losses`` (``criterion.py:402-413``)
+        in one call; returns ``(rows, cols, valid)``."""
+        if self.matcher not in MATCHERS:
+            raise ValueError(f"unknown matcher {self.matcher!r}; expected 'cuda' or 'hungarian'")
+        _, rows, cols, valid = match_stacked(pred_logits, pred_boxes, target_labels, target_boxes, target_mask,
+                                             sizes, group_detr, self.set_cost_class, self.set_cost_bbox,
+                                             self.set_cost_giou, self.focal_alpha)
+        return rows, cols, valid

@@ -147,3 +147,66 @@ def test_cost_dtypes_and_errors(pkg):
     cfg = pkg.CriterionConfig(matcher="auction")
     with pytest.raises(ValueError, match="unknown matcher"):
         cfg.solve(_t(np.zeros((1, 10, 3), np.float32)), _t(np.array([1], np.int32)), 1)
+
+
+def _stacked_inputs(seed, layers, batch, groups, per_group, classes, max_targets, sizes=None):
+    logits, boxes, labels, tboxes, mask, sizes = match_inputs(seed, batch, groups * per_group, classes, max_targets,
+                                                              sizes)
+    rng = np.random.default_rng(seed + 1)
+    lg = np.stack([logits] + [rng.standard_normal(logits.shape).astype(np.float32) for _ in range(layers - 1)])
+    bx = np.stack([boxes] + [np.concatenate([rng.uniform(0.05, 0.95, boxes.shape[:-1] + (2,)),
+                                             rng.uniform(0.02, 0.5, boxes.shape[:-1] + (2,))], -1).astype(np.float32)
+                             for _ in range(layers - 1)])
+    return lg, bx, labels, tboxes, mask, sizes
+
+
+def _stacked_vs_separate(pkg, lg, bx, labels, tboxes, mask, sizes, groups, dtype=None):
+    args = [_t(lg, dtype), _t(bx, dtype), _t(labels), _t(tboxes), _t(mask)]
+    cost, rows, cols, valid = pkg.match_stacked(*args, _t(sizes), groups, 2.0, 5.0, 2.0, 0.25)
+    sep = torch.stack([pkg.build_cost_matrix(args[0][i], args[1][i], *args[2:], 2.0, 5.0, 2.0, 0.25)
+                       for i in range(lg.shape[0])])
+    np.testing.assert_array_equal(cost.cpu().numpy(), sep.cpu().numpy())  # NaN where the separate cost has NaN
+    want = pkg.hungarian_match(sep, _t(sizes), groups)
+    _assert_same([x.cpu().numpy() for x in (rows, cols, valid)], [x.cpu().numpy() for x in want])
+    return cost.cpu().numpy(), [x.cpu().numpy() for x in (rows, cols, valid)]
+
+
+def test_stacked_config4(pkg):
+    """Cost + assignment of 3 stacked layers in one call at config-4 training shape: the separate
+    calls' cost bits and assignment, and SciPy's assignment on that cost."""
+    sizes = np.random.default_rng(21).integers(1, 101, 8)
+    sizes[0], sizes[1] = 100, 1
+    lg, bx, labels, tboxes, mask, sizes = _stacked_inputs(21, 3, 8, 13, 300, 91, 100, sizes=sizes)
+    cost, got = _stacked_vs_separate(pkg, lg, bx, labels, tboxes, mask, sizes, 13)
+    _assert_same(got, OM.hungarian_match(cost, sizes, 13))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_stacked_dtypes_and_edges(pkg, dtype):
+    """bf16 predictions, an image with no targets, and non-finite logits (the solver's sentinel
+    replacement, matcher.py:169-172) -- all as the separate calls."""
+    lg, bx, labels, tboxes, mask, sizes = _stacked_inputs(33, 2, 4, 3, 40, 7, 9, sizes=[0, 9, 4, 1])
+    lg[1, 2, 5, :] = np.nan
+    lg[0, 1, 7, 3] = np.inf
+    _stacked_vs_separate(pkg, lg, bx, labels, tboxes, mask, sizes, 3, dtype)
+
+
+def test_stacked_single_layer_shape(pkg):
+    """No leading layer axis: ``[B, Q, C]`` in, ``[B, G*T]`` out."""
+    lg, bx, labels, tboxes, mask, sizes = _stacked_inputs(44, 1, 3, 2, 25, 5, 6)
+    cost, rows, cols, valid = pkg.match_stacked(_t(lg[0]), _t(bx[0]), _t(labels), _t(tboxes), _t(mask), _t(sizes), 2,
+                                                2.0, 5.0, 2.0, 0.25)
+    assert cost.shape == (3, 50, 6) and rows.shape == (3, 12) and valid.dtype == torch.bool
+    _assert_same([x.cpu().numpy() for x in (rows, cols, valid)], OM.hungarian_match(cost.cpu().numpy(), sizes, 2))
+
+
+def test_staged_costs(pkg, monkeypatch):
+    """The solver with each block's costs staged in shared memory (a per-CTA budget set through
+    RFDETR_LSAP_STAGE_KB; by default costs are read through L1) gives SciPy's assignment too."""
+    monkeypatch.setenv("RFDETR_LSAP_STAGE_KB", "100")
+    rng = np.random.default_rng(5)
+    groups, per_group, max_targets = 4, 60, 30
+    cost = rng.standard_normal((5, groups * per_group, max_targets)).astype(np.float32)
+    cost[1, 3, 2] = np.nan
+    sizes = np.array([30, 1, 17, 0, 29], np.int32)
+    _assert_same(_match(pkg, cost, sizes, groups), OM.hungarian_match(cost, sizes, groups))
