@@ -325,6 +325,7 @@ def run_components(torch, device, N, lib, peak):
                          "bound": "latency",
                          "cpu_ms_1core": cpu_lsap_1 * 1e3, f"cpu_ms_{cores}cores": cpu_lsap_n * 1e3,
                          "cpu_kind": "reference (scipy.optimize.linear_sum_assignment, the reference's solver)"},
+        "msda_prologue": run_prologue(torch, device, N, lib, peak),
         "match_stacked": {"ms": ms_stacked, "bound": "latency",
                           "workload": f"cost + exact assignment of {C4_LAYERS}x{C4_B}x{C4_G} blocks in one call"},
         "set_losses": {"ms": ms_loss, "GB/s": gbs(loss_bytes, ms_loss), "frac": gbs(loss_bytes, ms_loss) / peak,
@@ -332,6 +333,70 @@ def run_components(torch, device, N, lib, peak):
                        "cpu_ms": cpu_loss * 1e3,
                        "cpu_kind": f"port (oracle/losses.py float64 torch autograd), {torch.get_num_threads()} threads"},
     }
+
+
+def run_prologue(torch, device, N, lib, peak):
+    """The fused MSDA prologue at the Nano decoder's training shape (8 x 3900 queries, C = 256,
+    16 heads x 1 level x 2 points, box reference points, bf16), beside the same prologue as
+    separate torch ops (two Linear layers, softmax, location arithmetic); both timed as CUDA-graph
+    replays, so the figures are device time, not Python launch overhead."""
+    import torch.nn.functional as F
+
+    b_, q_, c_, h_, l_, p_ = B, LQ, 256, H, 1, P
+    hlp = h_ * l_ * p_
+    g = torch.Generator(device=device).manual_seed(9)
+    query = torch.randn(b_, q_, c_, generator=g, device=device).to(torch.bfloat16)
+    ref = torch.rand(b_, q_, l_, 4, generator=g, device=device)
+    weight = (torch.randn(3 * hlp, c_, generator=g, device=device) * 0.05).to(torch.bfloat16)
+    bias = torch.randn(3 * hlp, generator=g, device=device)
+    loc = torch.empty((b_, q_, h_, l_, p_, 2), dtype=torch.float32, device=device)
+    attn = torch.empty((b_, q_, h_, l_ * p_), dtype=torch.bfloat16, device=device)
+    shapes = N.int64_array([24, 24])
+    w_off, w_att = weight[:2 * hlp], weight[2 * hlp:]
+    bb = bias.to(torch.bfloat16)
+
+    def composed():
+        off = F.linear(query, w_off, bb[:2 * hlp]).reshape(b_, q_, h_, l_, p_, 2)
+        logits = F.linear(query, w_att, bb[2 * hlp:]).reshape(b_, q_, h_, l_ * p_)
+        lc = ref[:, :, None, :, None, :2] + (off / p_).float() * ref[:, :, None, :, None, 2:] * 0.5
+        at = torch.softmax(logits.float(), -1).to(torch.bfloat16)
+        return lc, at
+
+    def graph_ms(fn, per_graph=20, replays=10):
+        """Device time per call: `per_graph` calls captured in one CUDA graph, replayed."""
+        s = torch.cuda.Stream(device)
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fn()
+        s.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s, capture_error_mode="relaxed"):
+            for _ in range(per_graph):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            for _ in range(replays):
+                graph.replay()
+            e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / (replays * per_graph)
+
+    def fused_on_current():
+        N.check(lib.rfdetr_msda_prologue(torch.cuda.current_stream(device).cuda_stream, query.data_ptr(), N.BF16,
+                                         weight.data_ptr(), bias.data_ptr(), ref.data_ptr(), 4, shapes,
+                                         loc.data_ptr(), attn.data_ptr(), b_, q_, c_, h_, l_, p_), "prologue")
+
+    ms_fused = graph_ms(fused_on_current)
+    ms_composed = graph_ms(composed)
+    nbytes = (query.numel() * 2 + weight.numel() * 2 + bias.numel() * 4 + ref.numel() * 4 + loc.numel() * 4 +
+              attn.numel() * 2)
+    gbs = nbytes / (ms_fused * 1e-3) / 1e9
+    return {"ms": ms_fused, "GB/s": gbs, "frac": gbs / peak, "algorithmic_bytes": nbytes,
+            "composed_torch_ms": ms_composed,
+            "workload": f"{b_}x{q_} queries, C={c_}, {h_} heads x {l_} level x {p_} points, box references, bf16"}
 
 
 def run_config3(torch, device, N, lib, peak):

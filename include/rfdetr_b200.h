@@ -193,6 +193,26 @@ int rfdetr_lsap_batched(void *stream, const float *cost, const int32_t *sizes, i
                         int32_t *cols, uint8_t *valid, int32_t *status_out);
 
 /* ---------------------------------------------------------------------------------------
+ * Prologue of multi-scale deformable attention: query -> (sampling locations, weights).
+ *
+ * Replaces MSDeformAttn.__call__'s sampling_offsets / attention_weights Linear layers, the
+ * location arithmetic and the softmax (ops.py:381-404), writing the sampler's inputs:
+ *   query [B, Lq, C] (f32 or bf16); weight [H*L*P*3, C] in the query dtype (rows 0..H*L*P*2-1:
+ *   sampling_offsets.weight, then attention_weights.weight); bias [H*L*P*3] f32 (likewise);
+ *   reference_points [B, Lq, L, ref_dim] f32 with ref_dim 2 (points) or 4 (boxes);
+ *   spatial_shapes [L][2] = (H_l, W_l), host memory.
+ *   sampling_locations [B, Lq, H, L, P, 2] f32; attention_weights [B, Lq, H, L*P] in the query
+ *   dtype.  The projection and bias are rounded to the query dtype as the reference's Linear
+ *   does (layers.py:276-279); the softmax runs in f32.
+ * Limits: L <= 8, C <= 4096, H*L*P <= 1024; bf16 needs C % 16 == 0 and H*L*P % 8 == 0.
+ * ------------------------------------------------------------------------------------- */
+int rfdetr_msda_prologue(void *stream, const void *query, int query_dtype, const void *weight,
+                         const float *bias, const float *reference_points, int64_t ref_dim,
+                         const int64_t *spatial_shapes, float *sampling_locations,
+                         void *attention_weights, int64_t batch, int64_t len_query, int64_t channels,
+                         int64_t n_heads, int64_t n_levels, int64_t n_points);
+
+/* ---------------------------------------------------------------------------------------
  * Matching cost and exact assignment of stacked layers in one call.
  *
  * Replaces the stacked layer_cost + single solve of compute_losses (criterion.py:402-413): the

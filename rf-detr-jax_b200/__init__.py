@@ -5,7 +5,8 @@ The package directory is ``rf-detr-jax_b200``; it is imported as ``rfdetr_jax_b2
 
 Components (each a thin host wrapper over ``librfdetr_b200.so``, see ``include/rfdetr_b200.h``):
 
-* :mod:`.ops`     -- multi-scale deformable attention, sampler ``"cuda"``, forward + backward;
+* :mod:`.ops`     -- multi-scale deformable attention, sampler ``"cuda"``, forward + backward, and
+  its query -> (locations, weights) prologue;
 * :mod:`.topk`    -- two-stage query selection (class max + top-k) and ``select_rows``;
 * :mod:`.matcher` -- matching cost and exact batched assignment (SciPy-identical);
 * :mod:`.postprocess` -- inference post-process (top-k over all query/class pairs);
@@ -14,7 +15,8 @@ Components (each a thin host wrapper over ``librfdetr_b200.so``, see ``include/r
 
 from . import _native
 from .matcher import CriterionConfig, build_cost_matrix, hungarian_match, match_stacked
-from .ops import MSDeformAttnFunction, ms_deform_attn, ms_deform_attn_core, ms_deform_attn_core_rows
+from .ops import (MSDeformAttnFunction, MSDeformAttnPrologueFunction, ms_deform_attn, ms_deform_attn_core,
+                  ms_deform_attn_core_rows, msda_prologue)
 from .losses import SetLossFunction, set_losses
 from .postprocess import post_process
 from .topk import select_rows, top_k, two_stage_topk
@@ -28,6 +30,8 @@ __all__ = [
     "ms_deform_attn",
     "ms_deform_attn_core",
     "ms_deform_attn_core_rows",
+    "msda_prologue",
+    "MSDeformAttnPrologueFunction",
     "post_process",
     "set_losses",
     "SetLossFunction",

@@ -1,0 +1,262 @@
+// Prologue of multi-scale deformable attention for sm_100a: from the decoder queries to the
+// sampler's inputs, in one launch.
+//
+// Reference (src/rfdetr_jax/models/ops.py:381-404, MSDeformAttn.__call__):
+//   offsets = Linear(query) -> [B, Lq, H, L, P, 2]       (sampling_offsets, layers.py:258-280)
+//   logits  = Linear(query) -> [B, Lq, H, L*P]           (attention_weights)
+//   points form (reference_points [B, Lq, L, 2]):
+//     loc = ref[..., None, :, None, :] + precise_divide(offsets, (W_l, H_l))
+//   box form (reference_points [B, Lq, L, 4]):
+//     loc = ref[..., :2] + precise_divide(offsets, P) * ref[..., 2:] * 0.5
+//   attn = softmax(logits in float32, over L*P).astype(query.dtype)
+// Linear computes in the query's dtype: x @ weight.astype(x.dtype).T, then + bias.astype(y.dtype)
+// (layers.py:276-279).  For bf16 queries the projection is therefore rounded to bf16, the bias
+// added in bf16, and the box form's division by P rounds to bf16 too (a bf16 numerator over a
+// Python int); the point form divides in float32 (the normaliser is a float32 array).  All of
+// that is reproduced here; the float32 accumulation order of the dot products is the only
+// difference from XLA's.
+//
+// One CTA (128 threads) per 64 query rows.  Phase 1 computes the rows' projection
+// y [64, H*L*P*3] into shared memory: for bf16 with mma.sync m16n8k16 (bf16 in, float32
+// accumulate; each warp 16 rows, up to 12 column tiles of 8 per pass, A fragments from the rows
+// staged in shared memory, B fragments from the weight rows through L1), for float32 with
+// CUDA-core FMAs over a shared copy of the rows.  Phase 2, one thread per (row, head), applies the bias, the
+// softmax over the head's L*P logits and the location arithmetic, and writes loc (float32) and
+// attn (query dtype) in the sampler's layouts.  The GEMM is ~1.5 GFLOP at the Nano training shape
+// and its N (H*L*P*3 = 96) is narrow, so the legacy tensor path is ample: the kernel is bound by
+// reading the queries.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace rfdetr {
+namespace {
+
+constexpr int kProThreads = 128;
+constexpr int kProRows = 64;        // query rows per CTA (4 warps x 16)
+constexpr int kProTilesPerPass = 12;  // column tiles of 8 held in registers per pass
+constexpr int kProMaxLevels = 8;
+
+struct ProGeom {
+    int N, Lq, C, H, L, P, R;  // rows, queries per image, channels, heads, levels, points, ref dim
+    int cout;                  // H * L * P * 3
+    float lw[kProMaxLevels], lh[kProMaxLevels];
+};
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void mma_bf16(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Phase 1, bf16: ys[r][o] = bf16(sum_i x[n0 + r][i] * w[o][i]) for the CTA's rows.  The rows are
+// staged in shared memory first (16-byte cp.async, all in flight at once; row stride C + 8 so the
+// fragment reads of a warp hit 32 distinct banks); weight rows come through L1.
+__device__ void project_bf16(const bf16 *__restrict__ x, const bf16 *__restrict__ w, float *ys, int ys_stride,
+                             bf16 *xs, int n0, const ProGeom &g) {
+    const int xs_stride = g.C + 8;
+    const int chunks = g.C / 8;  // 16-byte pieces per row
+    for (int i = threadIdx.x; i < kProRows * chunks; i += blockDim.x) {
+        const int r = i / chunks, c = i - r * chunks;
+        const int n = min(n0 + r, g.N - 1);  // tail rows: clamped reads
+        cp_async16(xs + (size_t)r * xs_stride + c * 8, x + (size_t)n * g.C + c * 8);
+    }
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = lane >> 2, tig = lane & 3;
+    const int r_lo = warp * 16 + grp, r_hi = r_lo + 8;
+    const uint32_t *xlo = reinterpret_cast<const uint32_t *>(xs + (size_t)r_lo * xs_stride);
+    const uint32_t *xhi = reinterpret_cast<const uint32_t *>(xs + (size_t)r_hi * xs_stride);
+    const int ntiles = g.cout / 8;
+    for (int t0 = 0; t0 < ntiles; t0 += kProTilesPerPass) {
+        float acc[kProTilesPerPass][4];
+#pragma unroll
+        for (int j = 0; j < kProTilesPerPass; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        for (int k = 0; k < g.C; k += 16) {
+            const int c2 = (k >> 1) + tig;  // u32 index of columns k + 2*tig
+            uint32_t a[4];
+            a[0] = xlo[c2];
+            a[1] = xhi[c2];
+            a[2] = xlo[c2 + 4];
+            a[3] = xhi[c2 + 4];
+#pragma unroll
+            for (int j = 0; j < kProTilesPerPass; ++j) {
+                if (t0 + j < ntiles) {
+                    const uint32_t *wr = reinterpret_cast<const uint32_t *>(w + (size_t)((t0 + j) * 8 + grp) * g.C);
+                    mma_bf16(acc[j], a, __ldg(wr + c2), __ldg(wr + c2 + 4));
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kProTilesPerPass; ++j) {
+            if (t0 + j < ntiles) {
+                const int o = (t0 + j) * 8 + 2 * tig;
+                ys[r_lo * ys_stride + o] = bf16_round(acc[j][0]);
+                ys[r_lo * ys_stride + o + 1] = bf16_round(acc[j][1]);
+                ys[r_hi * ys_stride + o] = bf16_round(acc[j][2]);
+                ys[r_hi * ys_stride + o + 1] = bf16_round(acc[j][3]);
+            }
+        }
+    }
+}
+
+// Phase 1, float32: the rows are staged in shared memory, each thread forms whole dot products.
+__device__ void project_f32(const float *__restrict__ x, const float *__restrict__ w, float *ys, int ys_stride,
+                            float *xs, int n0, const ProGeom &g) {
+    const int rows = min(kProRows, g.N - n0);
+    for (int i = threadIdx.x; i < rows * g.C; i += blockDim.x) xs[i] = __ldg(x + (size_t)n0 * g.C + i);
+    __syncthreads();
+    for (int e = threadIdx.x; e < rows * g.cout; e += blockDim.x) {
+        const int r = e / g.cout, o = e - r * g.cout;
+        const float *xr = xs + (size_t)r * g.C;
+        const float *wr = w + (size_t)o * g.C;
+        float s = 0.f;
+        for (int i = 0; i < g.C; ++i) s = fmaf(xr[i], __ldg(wr + i), s);
+        ys[r * ys_stride + o] = s;
+    }
+}
+
+template <typename TQ>
+__global__ void __launch_bounds__(kProThreads)
+msda_prologue_kernel(const TQ *__restrict__ query, const TQ *__restrict__ weight, const float *__restrict__ bias,
+                     const float *__restrict__ ref, float *__restrict__ loc, TQ *__restrict__ attn, const ProGeom g) {
+    extern __shared__ __align__(16) float psm[];
+    const int ys_stride = g.cout + 1;
+    float *ys = psm;
+    const int n0 = blockIdx.x * kProRows;
+    if constexpr (sizeof(TQ) == 2) {
+        project_bf16(query, weight, ys, ys_stride, reinterpret_cast<bf16 *>(psm + kProRows * ys_stride), n0, g);
+    } else {
+        project_f32(query, weight, ys, ys_stride, psm + kProRows * ys_stride, n0, g);
+    }
+    __syncthreads();
+
+    // Phase 2: one thread per (row, head).
+    const int LP = g.L * g.P;
+    const int hlp2 = g.H * LP * 2;
+    const bool lowp = sizeof(TQ) == 2;
+    for (int it = threadIdx.x; it < kProRows * g.H; it += blockDim.x) {
+        const int r = it / g.H, h = it - r * g.H;
+        const int n = n0 + r;
+        if (n >= g.N) continue;
+        const float *y = ys + r * ys_stride;
+        // Bias in the projection's dtype (layers.py:278-279).
+        auto yb = [&](int o) {
+            const float b = __ldg(bias + o);
+            return lowp ? bf16_round(y[o] + bf16_round(b)) : y[o] + b;
+        };
+        // Softmax over the head's L*P logits in float32 (ops.py:403-404).
+        float m = -INFINITY;
+        for (int k = 0; k < LP; ++k) m = fmaxf(m, yb(hlp2 + h * LP + k));
+        float s = 0.f;
+        for (int k = 0; k < LP; ++k) s += expf(yb(hlp2 + h * LP + k) - m);
+        TQ *arow = attn + ((size_t)n * g.H + h) * LP;
+        for (int k = 0; k < LP; ++k) arow[k] = from_f32<TQ>(__fdiv_rn(expf(yb(hlp2 + h * LP + k) - m), s));
+        // Locations (ops.py:388-401).
+        const float *rrow = ref + (size_t)n * g.L * g.R;
+        float *lrow = loc + ((size_t)n * g.H + h) * LP * 2;
+        for (int l = 0; l < g.L; ++l) {
+            const float rx = __ldg(rrow + l * g.R), ry = __ldg(rrow + l * g.R + 1);
+            for (int p = 0; p < g.P; ++p) {
+                const int o = ((h * g.L + l) * g.P + p) * 2;
+                const float ox = yb(o), oy = yb(o + 1);
+                float lx, ly;
+                if (g.R == 2) {
+                    lx = __fadd_rn(rx, __fdiv_rn(ox, g.lw[l]));
+                    ly = __fadd_rn(ry, __fdiv_rn(oy, g.lh[l]));
+                } else {
+                    const float rw = __ldg(rrow + l * g.R + 2), rh = __ldg(rrow + l * g.R + 3);
+                    float tx = __fdiv_rn(ox, (float)g.P), ty = __fdiv_rn(oy, (float)g.P);
+                    if (lowp) {
+                        tx = bf16_round(tx);
+                        ty = bf16_round(ty);
+                    }
+                    lx = __fadd_rn(rx, __fmul_rn(__fmul_rn(tx, rw), 0.5f));
+                    ly = __fadd_rn(ry, __fmul_rn(__fmul_rn(ty, rh), 0.5f));
+                }
+                lrow[(l * g.P + p) * 2] = lx;
+                lrow[(l * g.P + p) * 2 + 1] = ly;
+            }
+        }
+    }
+}
+
+}  // namespace
+}  // namespace rfdetr
+
+using namespace rfdetr;
+
+extern "C" int rfdetr_msda_prologue(void *stream, const void *query, int query_dtype, const void *weight,
+                                    const float *bias, const float *reference_points, int64_t ref_dim,
+                                    const int64_t *spatial_shapes, float *sampling_locations,
+                                    void *attention_weights, int64_t batch, int64_t len_query, int64_t channels,
+                                    int64_t n_heads, int64_t n_levels, int64_t n_points) {
+    if (query_dtype != RFDETR_F32 && query_dtype != RFDETR_BF16) return RFDETR_ERR_DTYPE;
+    if (batch < 0 || len_query < 0 || channels <= 0 || n_heads <= 0 || n_levels <= 0 || n_levels > kProMaxLevels ||
+        n_points <= 0 || (ref_dim != 2 && ref_dim != 4) || channels > 4096 || n_heads * n_levels * n_points > 1024 ||
+        batch * len_query > (1LL << 31))
+        return RFDETR_ERR_SHAPE;
+    const long long cout = n_heads * n_levels * n_points * 3;
+    if (query_dtype == RFDETR_BF16 && (channels % 16 != 0 || cout % 8 != 0)) return RFDETR_ERR_SHAPE;
+    if (batch == 0 || len_query == 0) return RFDETR_OK;
+    if (!query || !weight || !bias || !reference_points || !spatial_shapes || !sampling_locations ||
+        !attention_weights)
+        return RFDETR_ERR_SHAPE;
+    const int es = dtype_size(query_dtype);
+    if (!aligned(query, query_dtype == RFDETR_BF16 ? 16 : 4) || !aligned(weight, 4) || !aligned(bias, 4) ||
+        !aligned(reference_points, 4) || !aligned(sampling_locations, 4) || !aligned(attention_weights, es))
+        return RFDETR_ERR_ALIGN;
+    ProGeom g;
+    g.N = (int)(batch * len_query);
+    g.Lq = (int)len_query;
+    g.C = (int)channels;
+    g.H = (int)n_heads;
+    g.L = (int)n_levels;
+    g.P = (int)n_points;
+    g.R = (int)ref_dim;
+    g.cout = (int)cout;
+    for (int l = 0; l < g.L; ++l) {
+        const int64_t hgt = spatial_shapes[2 * l], wid = spatial_shapes[2 * l + 1];
+        if (hgt <= 0 || wid <= 0) return RFDETR_ERR_SHAPE;
+        g.lh[l] = (float)hgt;
+        g.lw[l] = (float)wid;
+    }
+    size_t smem = (size_t)kProRows * (g.cout + 1) * sizeof(float);
+    smem = (smem + 15) & ~(size_t)15;
+    if (query_dtype == RFDETR_F32) smem += (size_t)kProRows * g.C * sizeof(float);
+    else smem += (size_t)kProRows * (g.C + 8) * sizeof(bf16);
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (smem > (size_t)optin) return RFDETR_ERR_SHAPE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned grid = (unsigned)((g.N + kProRows - 1) / kProRows);
+    if (query_dtype == RFDETR_BF16) {
+        auto k = msda_prologue_kernel<bf16>;
+        if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                                    cudaSuccess)
+            return RFDETR_ERR_CUDA;
+        k<<<grid, kProThreads, smem, s>>>(static_cast<const bf16 *>(query), static_cast<const bf16 *>(weight), bias,
+                                          reference_points, sampling_locations, static_cast<bf16 *>(attention_weights),
+                                          g);
+    } else {
+        auto k = msda_prologue_kernel<float>;
+        if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                                    cudaSuccess)
+            return RFDETR_ERR_CUDA;
+        k<<<grid, kProThreads, smem, s>>>(static_cast<const float *>(query), static_cast<const float *>(weight), bias,
+                                          reference_points, sampling_locations,
+                                          static_cast<float *>(attention_weights), g);
+    }
+    return launch_status();
+}

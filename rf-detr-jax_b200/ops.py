@@ -7,7 +7,9 @@ Mirrors the reference's operator interface (``src/rfdetr_jax/models/ops.py``):
   rejected with the reference's ``ValueError("unknown sampler ...")`` (``ops.py:235-238``);
 * :func:`ms_deform_attn_core` -- the ``[B, H, D, sum(HW)]`` entry point (``ops.py:295-314``);
 * :func:`ms_deform_attn` -- the signature of the drop-in contract,
-  ``(value, spatial_shapes, level_start_index, sampling_locations, attention_weights)``.
+  ``(value, spatial_shapes, level_start_index, sampling_locations, attention_weights)``;
+* :func:`msda_prologue` -- the query -> (locations, weights) prologue of ``MSDeformAttn``
+  (``ops.py:381-404``) in one launch.
 
 Autodiff mirrors the reference's ``custom_vjp`` pattern (``deform_pallas.py:132-178``): a
 ``torch.autograd.Function`` whose backward returns ``(grad_value, grad_locations,
@@ -168,3 +170,83 @@ def ms_deform_attn(value: torch.Tensor, spatial_shapes, level_start_index, sampl
         if starts != expected:
             raise ValueError(f"level_start_index {starts} does not match spatial_shapes (expected {expected})")
     return ms_deform_attn_core_rows(value, shapes, sampling_locations, attention_weights, "cuda")
+
+
+def _prologue_launch(query, reference_points, shapes, weight, bias, n_heads, n_levels, n_points):
+    batch, len_query, channels = query.shape
+    dev = query.device
+    loc = torch.empty((batch, len_query, n_heads, n_levels, n_points, 2), dtype=torch.float32, device=dev)
+    attn = torch.empty((batch, len_query, n_heads, n_levels * n_points), dtype=query.dtype, device=dev)
+    status = N.lib().rfdetr_msda_prologue(
+        N.stream_of(query), N.ptr(query), N.dtype_code(query.dtype), N.ptr(weight), N.ptr(bias),
+        N.ptr(reference_points), reference_points.shape[-1], N.int64_array([v for hw in shapes for v in hw]),
+        N.ptr(loc), N.ptr(attn), batch, len_query, channels, n_heads, n_levels, n_points)
+    N.check(status, "rfdetr_msda_prologue")
+    return loc, attn
+
+
+class MSDeformAttnPrologueFunction(torch.autograd.Function):
+    """Forward: one ``rfdetr_msda_prologue`` launch.  Backward (with respect to the query, both
+    projections and the reference points) from the saved attention weights: the softmax and
+    location derivatives are elementwise and the projection's are two GEMMs (cuBLAS)."""
+
+    @staticmethod
+    def forward(ctx, query, reference_points, weight, bias, shapes, n_heads, n_levels, n_points):
+        loc, attn = _prologue_launch(query, reference_points, shapes, weight, bias, n_heads, n_levels, n_points)
+        ctx.save_for_backward(query, reference_points, weight, bias, attn)
+        ctx.geom = (shapes, n_heads, n_levels, n_points)
+        return loc, attn
+
+    @staticmethod
+    def backward(ctx, g_loc, g_attn):
+        query, ref, weight, bias, attn = ctx.saved_tensors
+        shapes, H, L, P = ctx.geom
+        B, Lq, C = query.shape
+        g_loc = attn.new_zeros((B, Lq, H, L, P, 2), dtype=torch.float32) if g_loc is None else g_loc.float()
+        g_attn = torch.zeros_like(attn, dtype=torch.float32) if g_attn is None else g_attn.float()
+        a = attn.float()
+        g_logit = a * (g_attn - (a * g_attn).sum(-1, keepdim=True))           # softmax over L*P
+        if ref.shape[-1] == 2:
+            norm = torch.tensor([[w, h] for h, w in shapes], dtype=torch.float32, device=query.device)
+            g_off = g_loc / norm[None, None, None, :, None, :]
+            g_ref = g_loc.sum(dim=(2, 4))                                         # [B, Lq, L, 2]
+        else:
+            half = ref[:, :, None, :, None, 2:].float() * 0.5
+            g_off = g_loc * half / P
+            g_ref_xy = g_loc.sum(dim=(2, 4))
+            y = (torch.matmul(query.float(), weight.float().t()) + bias)[..., :H * L * P * 2].reshape(B, Lq, H, L, P, 2)
+            g_ref_wh = (g_loc * (y / P) * 0.5).sum(dim=(2, 4))
+            g_ref = torch.cat([g_ref_xy, g_ref_wh], -1)
+        g_y = torch.cat([g_off.reshape(B, Lq, -1), g_logit.reshape(B, Lq, -1)], -1)   # [B, Lq, H*L*P*3]
+        g_query = torch.matmul(g_y, weight.float()).to(query.dtype)
+        g_weight = torch.matmul(g_y.reshape(-1, g_y.shape[-1]).t(), query.float().reshape(-1, C)).to(weight.dtype)
+        g_bias = g_y.reshape(-1, g_y.shape[-1]).sum(0)
+        return g_query, g_ref.to(ref.dtype), g_weight, g_bias, None, None, None, None
+
+
+def msda_prologue(query: torch.Tensor, reference_points: torch.Tensor, spatial_shapes, sampling_offsets_weight,
+                  sampling_offsets_bias, attention_weights_weight, attention_weights_bias, n_heads: int,
+                  n_levels: int, n_points: int):
+    """The prologue of ``MSDeformAttn.__call__`` (``ops.py:381-404``) in one launch: the
+    ``sampling_offsets`` and ``attention_weights`` Linear layers on ``query [B, Lq, C]``, the
+    softmax over ``L*P`` and the location arithmetic for point (``[B, Lq, L, 2]``) or box
+    (``[B, Lq, L, 4]``) reference points.  Weights use torch's Linear layout ``[out, in]`` (the
+    reference's too, ``layers.py:258-280``) and are cast to the query dtype as the reference does.
+
+    Returns ``(sampling_locations [B, Lq, H, L, P, 2] float32, attention_weights [B, Lq, H, L*P]
+    in the query dtype)`` -- the sampler's inputs.
+    """
+    N.require_cuda(query, reference_points, sampling_offsets_weight, attention_weights_weight)
+    shapes = _shapes_tuple(spatial_shapes)
+    if query.dim() != 3 or len(shapes) != n_levels or reference_points.shape[:3] != (*query.shape[:2], n_levels) \
+            or reference_points.shape[-1] not in (2, 4):
+        raise ValueError("inconsistent shapes for msda_prologue")
+    if query.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("query must be float32 or bfloat16")
+    hlp = n_heads * n_levels * n_points
+    weight = torch.cat([sampling_offsets_weight, attention_weights_weight], 0).to(query.dtype).contiguous()
+    bias = torch.cat([sampling_offsets_bias, attention_weights_bias], 0).to(torch.float32).contiguous()
+    if weight.shape != (3 * hlp, query.shape[-1]):
+        raise ValueError("projection weights must be [H*L*P*2, C] and [H*L*P, C]")
+    return MSDeformAttnPrologueFunction.apply(query.contiguous(), reference_points.to(torch.float32).contiguous(),
+                                              weight, bias, shapes, n_heads, n_levels, n_points)
