@@ -16,15 +16,17 @@
 // that is reproduced here; the float32 accumulation order of the dot products is the only
 // difference from XLA's.
 //
-// One CTA (128 threads) per 64 query rows.  Phase 1 computes the rows' projection
-// y [64, H*L*P*3] into shared memory: for bf16 with mma.sync m16n8k16 (bf16 in, float32
-// accumulate; each warp 16 rows, up to 12 column tiles of 8 per pass, A fragments from the rows
-// staged in shared memory, B fragments from the weight rows through L1), for float32 with
-// CUDA-core FMAs over a shared copy of the rows.  Phase 2, one thread per (row, head), applies the bias, the
-// softmax over the head's L*P logits and the location arithmetic, and writes loc (float32) and
-// attn (query dtype) in the sampler's layouts.  The GEMM is ~1.5 GFLOP at the Nano training shape
-// and its N (H*L*P*3 = 96) is narrow, so the legacy tensor path is ample: the kernel is bound by
-// reading the queries.
+// Persistent CTAs of 256 threads loop over tiles of 64 query rows; for bf16 the weight is staged
+// in shared memory once per CTA when it fits.  Phase 1 computes a tile's projection y [64,
+// H*L*P*3] into shared memory, rounded and with its bias as the reference's Linear gives it: for
+// bf16 with mma.sync m16n8k16 (bf16 in, float32 accumulate; two warps per 16-row slice, each
+// half of the column tiles, up to 6 tiles of 8 per pass, A fragments from the rows staged in
+// shared memory), for float32 with
+// CUDA-core FMAs over a shared copy of the rows.  Phase 2, one thread per (row, head), applies
+// the softmax over the head's L*P logits (one exponential each) and the location arithmetic, and
+// writes loc (float32) and attn (query dtype) in the sampler's layouts.  The GEMM is ~1.5 GFLOP
+// at the Nano training shape and its N (H*L*P*3 = 96) is narrow, so the legacy tensor path is
+// ample.
 #include <algorithm>
 
 #include "common.cuh"
@@ -32,14 +34,15 @@
 namespace rfdetr {
 namespace {
 
-constexpr int kProThreads = 128;
-constexpr int kProRows = 64;        // query rows per CTA (4 warps x 16)
-constexpr int kProTilesPerPass = 12;  // column tiles of 8 held in registers per pass
+constexpr int kProThreads = 256;
+constexpr int kProRows = 64;          // query rows per tile: 4 row slices of 16, two warps each
+constexpr int kProTilesPerPass = 6;   // column tiles of 8 held in registers per pass
 constexpr int kProMaxLevels = 8;
 
 struct ProGeom {
     int N, Lq, C, H, L, P, R;  // rows, queries per image, channels, heads, levels, points, ref dim
     int cout;                  // H * L * P * 3
+    int w_staged;              // bf16: the weight is staged in shared memory (else read through L1)
     float lw[kProMaxLevels], lh[kProMaxLevels];
 };
 
@@ -58,11 +61,14 @@ __device__ __forceinline__ void mma_bf16(float *c, const uint32_t *a, uint32_t b
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Phase 1, bf16: ys[r][o] = bf16(sum_i x[n0 + r][i] * w[o][i]) for the CTA's rows.  The rows are
-// staged in shared memory first (16-byte cp.async, all in flight at once; row stride C + 8 so the
-// fragment reads of a warp hit 32 distinct banks); weight rows come through L1.
-__device__ void project_bf16(const bf16 *__restrict__ x, const bf16 *__restrict__ w, float *ys, int ys_stride,
-                             bf16 *xs, int n0, const ProGeom &g) {
+// Phase 1, bf16: ys[r][o] = bf16(sum_i x[n0 + r][i] * w[o][i]) for the CTA's rows.  The rows
+// and, when it fits, the weight are staged in shared memory first (16-byte cp.async, all in
+// flight at once; row stride C + 8 so the fragment reads of a warp hit 32 distinct banks).  A
+// B fragment spans 8 weight rows, so reading it from global memory costs 8 L1 wavefronts per
+// load -- staged, one.
+__device__ __forceinline__ void project_bf16(const bf16 *__restrict__ x, const bf16 *__restrict__ w,
+                                             const float *__restrict__ bias, float *ys, int ys_stride, bf16 *xs,
+                                             const bf16 *wsm, int n0, const ProGeom &g) {
     const int xs_stride = g.C + 8;
     const int chunks = g.C / 8;  // 16-byte pieces per row
     for (int i = threadIdx.x; i < kProRows * chunks; i += blockDim.x) {
@@ -74,11 +80,15 @@ __device__ void project_bf16(const bf16 *__restrict__ x, const bf16 *__restrict_
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = lane >> 2, tig = lane & 3;
-    const int r_lo = warp * 16 + grp, r_hi = r_lo + 8;
+    const int slice = warp & 3, half = warp >> 2;  // 16-row slice; which half of the column tiles
+    const int r_lo = slice * 16 + grp, r_hi = r_lo + 8;
     const uint32_t *xlo = reinterpret_cast<const uint32_t *>(xs + (size_t)r_lo * xs_stride);
     const uint32_t *xhi = reinterpret_cast<const uint32_t *>(xs + (size_t)r_hi * xs_stride);
-    const int ntiles = g.cout / 8;
-    for (int t0 = 0; t0 < ntiles; t0 += kProTilesPerPass) {
+    const int ntiles_all = g.cout / 8;
+    const int tile_mid = (ntiles_all + 1) / 2;
+    const int tile_begin = half ? tile_mid : 0;
+    const int ntiles = half ? ntiles_all : tile_mid;  // this warp's tiles: [tile_begin, ntiles)
+    for (int t0 = tile_begin; t0 < ntiles; t0 += kProTilesPerPass) {
         float acc[kProTilesPerPass][4];
 #pragma unroll
         for (int j = 0; j < kProTilesPerPass; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -89,30 +99,45 @@ __device__ void project_bf16(const bf16 *__restrict__ x, const bf16 *__restrict_
             a[1] = xhi[c2];
             a[2] = xlo[c2 + 4];
             a[3] = xhi[c2 + 4];
+            if (g.w_staged) {
 #pragma unroll
-            for (int j = 0; j < kProTilesPerPass; ++j) {
-                if (t0 + j < ntiles) {
-                    const uint32_t *wr = reinterpret_cast<const uint32_t *>(w + (size_t)((t0 + j) * 8 + grp) * g.C);
-                    mma_bf16(acc[j], a, __ldg(wr + c2), __ldg(wr + c2 + 4));
+                for (int j = 0; j < kProTilesPerPass; ++j) {
+                    if (t0 + j < ntiles) {
+                        const uint32_t *wr =
+                            reinterpret_cast<const uint32_t *>(wsm + (size_t)((t0 + j) * 8 + grp) * xs_stride);
+                        mma_bf16(acc[j], a, wr[c2], wr[c2 + 4]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kProTilesPerPass; ++j) {
+                    if (t0 + j < ntiles) {
+                        const uint32_t *wr =
+                            reinterpret_cast<const uint32_t *>(w + (size_t)((t0 + j) * 8 + grp) * g.C);
+                        mma_bf16(acc[j], a, __ldg(wr + c2), __ldg(wr + c2 + 4));
+                    }
                 }
             }
         }
+        // The projection rounded to bf16, then the bias added in bf16 (layers.py:276-279).
 #pragma unroll
         for (int j = 0; j < kProTilesPerPass; ++j) {
             if (t0 + j < ntiles) {
                 const int o = (t0 + j) * 8 + 2 * tig;
-                ys[r_lo * ys_stride + o] = bf16_round(acc[j][0]);
-                ys[r_lo * ys_stride + o + 1] = bf16_round(acc[j][1]);
-                ys[r_hi * ys_stride + o] = bf16_round(acc[j][2]);
-                ys[r_hi * ys_stride + o + 1] = bf16_round(acc[j][3]);
+                const float b0 = bf16_round(__ldg(bias + o)), b1 = bf16_round(__ldg(bias + o + 1));
+                ys[r_lo * ys_stride + o] = bf16_round(bf16_round(acc[j][0]) + b0);
+                ys[r_lo * ys_stride + o + 1] = bf16_round(bf16_round(acc[j][1]) + b1);
+                ys[r_hi * ys_stride + o] = bf16_round(bf16_round(acc[j][2]) + b0);
+                ys[r_hi * ys_stride + o + 1] = bf16_round(bf16_round(acc[j][3]) + b1);
             }
         }
     }
 }
 
 // Phase 1, float32: the rows are staged in shared memory, each thread forms whole dot products.
-__device__ void project_f32(const float *__restrict__ x, const float *__restrict__ w, float *ys, int ys_stride,
-                            float *xs, int n0, const ProGeom &g) {
+__device__ __forceinline__ void project_f32(const float *__restrict__ x, const float *__restrict__ w,
+                                            const float *__restrict__ bias, float *ys, int ys_stride, float *xs,
+                                            int n0, const ProGeom &g) {
     const int rows = min(kProRows, g.N - n0);
     for (int i = threadIdx.x; i < rows * g.C; i += blockDim.x) xs[i] = __ldg(x + (size_t)n0 * g.C + i);
     __syncthreads();
@@ -122,7 +147,7 @@ __device__ void project_f32(const float *__restrict__ x, const float *__restrict
         const float *wr = w + (size_t)o * g.C;
         float s = 0.f;
         for (int i = 0; i < g.C; ++i) s = fmaf(xr[i], __ldg(wr + i), s);
-        ys[r * ys_stride + o] = s;
+        ys[r * ys_stride + o] = s + __ldg(bias + o);
     }
 }
 
@@ -133,59 +158,84 @@ msda_prologue_kernel(const TQ *__restrict__ query, const TQ *__restrict__ weight
     extern __shared__ __align__(16) float psm[];
     const int ys_stride = g.cout + 1;
     float *ys = psm;
-    const int n0 = blockIdx.x * kProRows;
+    void *xs = psm + kProRows * ys_stride;
+    bf16 *wsm = reinterpret_cast<bf16 *>(xs) + (size_t)kProRows * (g.C + 8);
+    // Persistent CTAs: the weight is staged once (its copies complete with the first tile's).
     if constexpr (sizeof(TQ) == 2) {
-        project_bf16(query, weight, ys, ys_stride, reinterpret_cast<bf16 *>(psm + kProRows * ys_stride), n0, g);
-    } else {
-        project_f32(query, weight, ys, ys_stride, psm + kProRows * ys_stride, n0, g);
+        if (g.w_staged) {
+            const int chunks = g.C / 8;
+            for (int i = threadIdx.x; i < g.cout * chunks; i += blockDim.x) {
+                const int o = i / chunks, c = i - o * chunks;
+                cp_async16(wsm + (size_t)o * (g.C + 8) + c * 8, weight + (size_t)o * g.C + c * 8);
+            }
+        }
     }
-    __syncthreads();
-
-    // Phase 2: one thread per (row, head).
+    __shared__ float s_lw[kProMaxLevels], s_lh[kProMaxLevels];
+#pragma unroll
+    for (int l = 0; l < kProMaxLevels; ++l) {  // constant indices: the parameter struct stays in place
+        if (threadIdx.x == l) {
+            s_lw[l] = g.lw[l];
+            s_lh[l] = g.lh[l];
+        }
+    }
     const int LP = g.L * g.P;
     const int hlp2 = g.H * LP * 2;
     const bool lowp = sizeof(TQ) == 2;
-    for (int it = threadIdx.x; it < kProRows * g.H; it += blockDim.x) {
-        const int r = it / g.H, h = it - r * g.H;
-        const int n = n0 + r;
-        if (n >= g.N) continue;
-        const float *y = ys + r * ys_stride;
-        // Bias in the projection's dtype (layers.py:278-279).
-        auto yb = [&](int o) {
-            const float b = __ldg(bias + o);
-            return lowp ? bf16_round(y[o] + bf16_round(b)) : y[o] + b;
-        };
-        // Softmax over the head's L*P logits in float32 (ops.py:403-404).
-        float m = -INFINITY;
-        for (int k = 0; k < LP; ++k) m = fmaxf(m, yb(hlp2 + h * LP + k));
-        float s = 0.f;
-        for (int k = 0; k < LP; ++k) s += expf(yb(hlp2 + h * LP + k) - m);
-        TQ *arow = attn + ((size_t)n * g.H + h) * LP;
-        for (int k = 0; k < LP; ++k) arow[k] = from_f32<TQ>(__fdiv_rn(expf(yb(hlp2 + h * LP + k) - m), s));
-        // Locations (ops.py:388-401).
-        const float *rrow = ref + (size_t)n * g.L * g.R;
-        float *lrow = loc + ((size_t)n * g.H + h) * LP * 2;
-        for (int l = 0; l < g.L; ++l) {
-            const float rx = __ldg(rrow + l * g.R), ry = __ldg(rrow + l * g.R + 1);
-            for (int p = 0; p < g.P; ++p) {
-                const int o = ((h * g.L + l) * g.P + p) * 2;
-                const float ox = yb(o), oy = yb(o + 1);
-                float lx, ly;
-                if (g.R == 2) {
-                    lx = __fadd_rn(rx, __fdiv_rn(ox, g.lw[l]));
-                    ly = __fadd_rn(ry, __fdiv_rn(oy, g.lh[l]));
-                } else {
-                    const float rw = __ldg(rrow + l * g.R + 2), rh = __ldg(rrow + l * g.R + 3);
-                    float tx = __fdiv_rn(ox, (float)g.P), ty = __fdiv_rn(oy, (float)g.P);
-                    if (lowp) {
-                        tx = bf16_round(tx);
-                        ty = bf16_round(ty);
+    const int ntile = (g.N + kProRows - 1) / kProRows;
+    for (int tile = blockIdx.x; tile < ntile; tile += gridDim.x) {
+        const int n0 = tile * kProRows;
+        __syncthreads();  // the previous tile's rows and projection are consumed
+        if constexpr (sizeof(TQ) == 2) {
+            project_bf16(query, weight, bias, ys, ys_stride, reinterpret_cast<bf16 *>(xs), wsm, n0, g);
+        } else {
+            project_f32(query, weight, bias, ys, ys_stride, reinterpret_cast<float *>(xs), n0, g);
+        }
+        __syncthreads();
+
+        // Phase 2: one thread per (row, head); ys holds the projection with its bias.
+        for (int it = threadIdx.x; it < kProRows * g.H; it += blockDim.x) {
+            const int r = it / g.H, h = it - r * g.H;
+            const int n = n0 + r;
+            if (n >= g.N) continue;
+            float *y = ys + r * ys_stride;
+            // Softmax over the head's L*P logits in float32 (ops.py:403-404); the exponentials
+            // overwrite this item's own logits.
+            float *z = y + hlp2 + h * LP;
+            float m = -INFINITY;
+            for (int k = 0; k < LP; ++k) m = fmaxf(m, z[k]);
+            float s = 0.f;
+            for (int k = 0; k < LP; ++k) {
+                const float e = expf(z[k] - m);
+                z[k] = e;
+                s += e;
+            }
+            TQ *arow = attn + ((size_t)n * g.H + h) * LP;
+            for (int k = 0; k < LP; ++k) arow[k] = from_f32<TQ>(__fdividef(z[k], s));
+            // Locations (ops.py:388-401), divisions rounded once as precise_divide does.
+            const float *rrow = ref + (size_t)n * g.L * g.R;
+            float *lrow = loc + ((size_t)n * g.H + h) * LP * 2;
+            for (int l = 0; l < g.L; ++l) {
+                const float rx = __ldg(rrow + l * g.R), ry = __ldg(rrow + l * g.R + 1);
+                const float rw = g.R == 4 ? __ldg(rrow + l * g.R + 2) : 0.f;
+                const float rh = g.R == 4 ? __ldg(rrow + l * g.R + 3) : 0.f;
+                for (int p = 0; p < g.P; ++p) {
+                    const int o = ((h * g.L + l) * g.P + p) * 2;
+                    const float ox = y[o], oy = y[o + 1];
+                    float lx, ly;
+                    if (g.R == 2) {
+                        lx = __fadd_rn(rx, __fdiv_rn(ox, s_lw[l]));
+                        ly = __fadd_rn(ry, __fdiv_rn(oy, s_lh[l]));
+                    } else {
+                        float tx = __fdiv_rn(ox, (float)g.P), ty = __fdiv_rn(oy, (float)g.P);
+                        if (lowp) {
+                            tx = bf16_round(tx);
+                            ty = bf16_round(ty);
+                        }
+                        lx = __fadd_rn(rx, __fmul_rn(__fmul_rn(tx, rw), 0.5f));
+                        ly = __fadd_rn(ry, __fmul_rn(__fmul_rn(ty, rh), 0.5f));
                     }
-                    lx = __fadd_rn(rx, __fmul_rn(__fmul_rn(tx, rw), 0.5f));
-                    ly = __fadd_rn(ry, __fmul_rn(__fmul_rn(ty, rh), 0.5f));
+                    *reinterpret_cast<float2 *>(lrow + (l * g.P + p) * 2) = make_float2(lx, ly);
                 }
-                lrow[(l * g.P + p) * 2] = lx;
-                lrow[(l * g.P + p) * 2 + 1] = ly;
             }
         }
     }
@@ -238,14 +288,29 @@ extern "C" int rfdetr_msda_prologue(void *stream, const void *query, int query_d
     int dev = 0, optin = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    // Stage the weight when the CTA still fits two to an SM with it (the Nano layout: 50 KB).
+    const size_t wbytes = (size_t)g.cout * (g.C + 8) * sizeof(bf16);
+    g.w_staged = query_dtype == RFDETR_BF16 && smem + wbytes <= 112 * 1024;
+    if (g.w_staged) smem += wbytes;
     if (smem > (size_t)optin) return RFDETR_ERR_SHAPE;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const unsigned grid = (unsigned)((g.N + kProRows - 1) / kProRows);
+    const long long ntile = (g.N + kProRows - 1) / kProRows;
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // Persistent grid: as many CTAs as fit at once, each looping over row tiles.
+    auto grid_for = [&](const void *kernel) -> unsigned {
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kProThreads, smem) != cudaSuccess ||
+            per_sm < 1)
+            per_sm = 1;
+        return (unsigned)std::min<long long>(ntile, (long long)per_sm * std::max(sms, 1));
+    };
     if (query_dtype == RFDETR_BF16) {
         auto k = msda_prologue_kernel<bf16>;
         if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
                                     cudaSuccess)
             return RFDETR_ERR_CUDA;
+        const unsigned grid = grid_for(reinterpret_cast<const void *>(k));
         k<<<grid, kProThreads, smem, s>>>(static_cast<const bf16 *>(query), static_cast<const bf16 *>(weight), bias,
                                           reference_points, sampling_locations, static_cast<bf16 *>(attention_weights),
                                           g);
@@ -254,6 +319,7 @@ extern "C" int rfdetr_msda_prologue(void *stream, const void *query, int query_d
         if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
                                     cudaSuccess)
             return RFDETR_ERR_CUDA;
+        const unsigned grid = grid_for(reinterpret_cast<const void *>(k));
         k<<<grid, kProThreads, smem, s>>>(static_cast<const float *>(query), static_cast<const float *>(weight), bias,
                                           reference_points, sampling_locations,
                                           static_cast<float *>(attention_weights), g);
