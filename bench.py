@@ -723,16 +723,22 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     e2e_steps = max(6, min(args.steps, 30))
+    # Three timed trials (every rank runs all three; each trial's figure is the max over ranks);
+    # the median is reported, so one trial slowed by other work on the shared host does not
+    # decide the number.  All trials are in the JSON line.
     t0 = time.perf_counter()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(s_h2d)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    s_h2d.wait_stream(s_d2h)
-    e_end.record(s_h2d)
-    e_end.synchronize()
-    barrier()
-    e2e_ms = ranks.max_float(e_start.elapsed_time(e_end)) / e2e_steps
+    e2e_trials = []
+    for _trial in range(3):
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(s_h2d)
+        for i in range(e2e_steps):
+            e2e_step(i)
+        s_h2d.wait_stream(s_d2h)
+        e_end.record(s_h2d)
+        e_end.synchronize()
+        barrier()
+        e2e_trials.append(ranks.max_float(e_start.elapsed_time(e_end)) / e2e_steps)
+    e2e_ms = sorted(e2e_trials)[1]
 
     cpu = cpu_baseline_sample() if (rank == 0 and world == 1) else None
     peaks_path_ = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -769,7 +775,8 @@ def run_ours(args):
                                      "frac": fwd_bytes / (ms_fwd * 1e-3) / 1e9 / peak},
                     "msda_backward": {"ms": ms_bwd, "GB/s": achieved, "frac": achieved / peak}},
         "e2e": {"value": whole_job_value(B * LQ, world, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "trials_ms_per_step": e2e_trials,
+                "statistic": f"median of 3 trials of {e2e_steps} steps",
                 "pipeline": "copy-in / compute / copy-out on three streams, consecutive steps overlapped"},
         "gpu_launches": 2 * args.steps,
         "clocks": clock_summary,
