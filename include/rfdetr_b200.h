@@ -212,6 +212,22 @@ int rfdetr_msda_prologue(void *stream, const void *query, int query_dtype, const
                          void *attention_weights, int64_t batch, int64_t len_query, int64_t channels,
                          int64_t n_heads, int64_t n_levels, int64_t n_points);
 
+/* Backward of the prologue's elementwise part (the derivatives of the softmax and of the
+ * location arithmetic, ops.py:388-404), for the autodiff of MSDeformAttn's query side:
+ *   grad_locations [B, Lq, H, L, P, 2] f32, grad_weights and attention_weights [B, Lq, H, L*P]
+ *   (weights_dtype, the forward's attention output), reference_points as in the forward,
+ *   offsets [B*Lq, H*L*P*2] f32 (the forward's biased projection, offsets part; box form only,
+ *   else may be NULL), spatial_shapes as in the forward.
+ *   grad_projection [B*Lq, H*L*P*3] f32 receives the gradient of the projection (offsets part,
+ *   then logits part), grad_reference_points [B, Lq, L, ref_dim] f32 that of the reference
+ *   points.  The query / weight gradients are then two GEMMs with grad_projection. */
+int rfdetr_msda_prologue_backward(void *stream, const float *grad_locations, const void *grad_weights,
+                                  const void *attention_weights, int weights_dtype,
+                                  const float *reference_points, int64_t ref_dim, const float *offsets,
+                                  const int64_t *spatial_shapes, float *grad_projection,
+                                  float *grad_reference_points, int64_t batch, int64_t len_query,
+                                  int64_t n_heads, int64_t n_levels, int64_t n_points);
+
 /* ---------------------------------------------------------------------------------------
  * Matching cost and exact assignment of stacked layers in one call.
  *

@@ -241,6 +241,63 @@ msda_prologue_kernel(const TQ *__restrict__ query, const TQ *__restrict__ weight
     }
 }
 
+// Backward of the prologue's elementwise part, one thread per query row: from the sampler's
+// location and weight gradients to the gradient of the projection y (offsets part, then logits
+// part) and of the reference points.
+//   softmax:  d logit_k = a_k (g_k - sum_j a_j g_j)
+//   points:   d off = g_loc / (W_l, H_l);        d ref_xy = sum over heads and points of g_loc
+//   boxes:    d off = g_loc * (ref_wh * 0.5) / P; d ref_xy likewise; d ref_wh = sum g_loc * off / P * 0.5
+// `offsets` (the forward's biased projection, offsets part) is needed by the box form only.
+template <typename TA>
+__global__ void __launch_bounds__(256)
+msda_prologue_bwd_kernel(const float *__restrict__ g_loc, const TA *__restrict__ g_attn, const TA *__restrict__ attn,
+                         const float *__restrict__ ref, const float *__restrict__ offsets, float *__restrict__ g_y,
+                         float *__restrict__ g_ref, const ProGeom g) {
+    const int LP = g.L * g.P;
+    const int hlp = g.H * LP;
+    for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < g.N; n += gridDim.x * blockDim.x) {
+        float *gy = g_y + (size_t)n * g.cout;
+        const float *gl = g_loc + (size_t)n * hlp * 2;
+        const float *rr = ref + (size_t)n * g.L * g.R;
+        for (int h = 0; h < g.H; ++h) {
+            const TA *ah = attn + ((size_t)n * g.H + h) * LP;
+            const TA *gh = g_attn + ((size_t)n * g.H + h) * LP;
+            float dot = 0.f;
+            for (int k = 0; k < LP; ++k) dot += to_f32(ah[k]) * to_f32(gh[k]);
+            for (int k = 0; k < LP; ++k) gy[2 * hlp + h * LP + k] = to_f32(ah[k]) * (to_f32(gh[k]) - dot);
+        }
+        for (int l = 0; l < g.L; ++l) {
+            float sx = 0.f, sy = 0.f, sw = 0.f, sh = 0.f;
+            const float rw = g.R == 4 ? rr[l * g.R + 2] : 0.f, rh = g.R == 4 ? rr[l * g.R + 3] : 0.f;
+            for (int h = 0; h < g.H; ++h) {
+                for (int p = 0; p < g.P; ++p) {
+                    const int o = ((h * g.L + l) * g.P + p) * 2;
+                    const float gx = gl[o], gyv = gl[o + 1];
+                    sx += gx;
+                    sy += gyv;
+                    if (g.R == 2) {
+                        gy[o] = __fdiv_rn(gx, g.lw[l]);
+                        gy[o + 1] = __fdiv_rn(gyv, g.lh[l]);
+                    } else {
+                        gy[o] = __fdiv_rn(gx * (rw * 0.5f), (float)g.P);
+                        gy[o + 1] = __fdiv_rn(gyv * (rh * 0.5f), (float)g.P);
+                        const float *off = offsets + (size_t)n * hlp * 2;
+                        sw += gx * (off[o] / (float)g.P) * 0.5f;
+                        sh += gyv * (off[o + 1] / (float)g.P) * 0.5f;
+                    }
+                }
+            }
+            float *gr = g_ref + ((size_t)n * g.L + l) * g.R;
+            gr[0] = sx;
+            gr[1] = sy;
+            if (g.R == 4) {
+                gr[2] = sw;
+                gr[3] = sh;
+            }
+        }
+    }
+}
+
 }  // namespace
 }  // namespace rfdetr
 
@@ -324,5 +381,50 @@ extern "C" int rfdetr_msda_prologue(void *stream, const void *query, int query_d
                                           reference_points, sampling_locations,
                                           static_cast<float *>(attention_weights), g);
     }
+    return launch_status();
+}
+
+extern "C" int rfdetr_msda_prologue_backward(void *stream, const float *grad_locations, const void *grad_weights,
+                                             const void *attention_weights, int weights_dtype,
+                                             const float *reference_points, int64_t ref_dim, const float *offsets,
+                                             const int64_t *spatial_shapes, float *grad_projection,
+                                             float *grad_reference_points, int64_t batch, int64_t len_query,
+                                             int64_t n_heads, int64_t n_levels, int64_t n_points) {
+    if (weights_dtype != RFDETR_F32 && weights_dtype != RFDETR_BF16) return RFDETR_ERR_DTYPE;
+    if (batch < 0 || len_query < 0 || n_heads <= 0 || n_levels <= 0 || n_levels > kProMaxLevels || n_points <= 0 ||
+        (ref_dim != 2 && ref_dim != 4) || n_heads * n_levels * n_points > 1024 || batch * len_query > (1LL << 31))
+        return RFDETR_ERR_SHAPE;
+    if (batch == 0 || len_query == 0) return RFDETR_OK;
+    if (!grad_locations || !grad_weights || !attention_weights || !reference_points || !spatial_shapes ||
+        !grad_projection || !grad_reference_points || (ref_dim == 4 && !offsets))
+        return RFDETR_ERR_SHAPE;
+    ProGeom g;
+    g.N = (int)(batch * len_query);
+    g.Lq = (int)len_query;
+    g.C = 0;
+    g.H = (int)n_heads;
+    g.L = (int)n_levels;
+    g.P = (int)n_points;
+    g.R = (int)ref_dim;
+    g.cout = (int)(n_heads * n_levels * n_points * 3);
+    g.w_staged = 0;
+    for (int l = 0; l < g.L; ++l) {
+        const int64_t hgt = spatial_shapes[2 * l], wid = spatial_shapes[2 * l + 1];
+        if (hgt <= 0 || wid <= 0) return RFDETR_ERR_SHAPE;
+        g.lh[l] = (float)hgt;
+        g.lw[l] = (float)wid;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned grid = (unsigned)std::min<long long>((g.N + 255) / 256, 148LL * 8);
+    if (weights_dtype == RFDETR_BF16)
+        msda_prologue_bwd_kernel<bf16><<<grid, 256, 0, s>>>(grad_locations, static_cast<const bf16 *>(grad_weights),
+                                                             static_cast<const bf16 *>(attention_weights),
+                                                             reference_points, offsets, grad_projection,
+                                                             grad_reference_points, g);
+    else
+        msda_prologue_bwd_kernel<float><<<grid, 256, 0, s>>>(grad_locations, static_cast<const float *>(grad_weights),
+                                                              static_cast<const float *>(attention_weights),
+                                                              reference_points, offsets, grad_projection,
+                                                              grad_reference_points, g);
     return launch_status();
 }

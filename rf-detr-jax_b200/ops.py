@@ -187,8 +187,9 @@ def _prologue_launch(query, reference_points, shapes, weight, bias, n_heads, n_l
 
 class MSDeformAttnPrologueFunction(torch.autograd.Function):
     """Forward: one ``rfdetr_msda_prologue`` launch.  Backward (with respect to the query, both
-    projections and the reference points) from the saved attention weights: the softmax and
-    location derivatives are elementwise and the projection's are two GEMMs (cuBLAS)."""
+    projections and the reference points) from the saved attention weights: one
+    ``rfdetr_msda_prologue_backward`` launch for the softmax and location derivatives, then the
+    projection's two GEMMs (cuBLAS)."""
 
     @staticmethod
     def forward(ctx, query, reference_points, weight, bias, shapes, n_heads, n_levels, n_points):
@@ -202,26 +203,27 @@ class MSDeformAttnPrologueFunction(torch.autograd.Function):
         query, ref, weight, bias, attn = ctx.saved_tensors
         shapes, H, L, P = ctx.geom
         B, Lq, C = query.shape
-        g_loc = attn.new_zeros((B, Lq, H, L, P, 2), dtype=torch.float32) if g_loc is None else g_loc.float()
-        g_attn = torch.zeros_like(attn, dtype=torch.float32) if g_attn is None else g_attn.float()
-        a = attn.float()
-        g_logit = a * (g_attn - (a * g_attn).sum(-1, keepdim=True))           # softmax over L*P
-        if ref.shape[-1] == 2:
-            norm = torch.tensor([[w, h] for h, w in shapes], dtype=torch.float32, device=query.device)
-            g_off = g_loc / norm[None, None, None, :, None, :]
-            g_ref = g_loc.sum(dim=(2, 4))                                         # [B, Lq, L, 2]
-        else:
-            half = ref[:, :, None, :, None, 2:].float() * 0.5
-            g_off = g_loc * half / P
-            g_ref_xy = g_loc.sum(dim=(2, 4))
-            y = (torch.matmul(query.float(), weight.float().t()) + bias)[..., :H * L * P * 2].reshape(B, Lq, H, L, P, 2)
-            g_ref_wh = (g_loc * (y / P) * 0.5).sum(dim=(2, 4))
-            g_ref = torch.cat([g_ref_xy, g_ref_wh], -1)
-        g_y = torch.cat([g_off.reshape(B, Lq, -1), g_logit.reshape(B, Lq, -1)], -1)   # [B, Lq, H*L*P*3]
-        g_query = torch.matmul(g_y, weight.float()).to(query.dtype)
-        g_weight = torch.matmul(g_y.reshape(-1, g_y.shape[-1]).t(), query.float().reshape(-1, C)).to(weight.dtype)
-        g_bias = g_y.reshape(-1, g_y.shape[-1]).sum(0)
-        return g_query, g_ref.to(ref.dtype), g_weight, g_bias, None, None, None, None
+        hlp = H * L * P
+        dev = query.device
+        g_loc = (torch.zeros((B, Lq, H, L, P, 2), dtype=torch.float32, device=dev) if g_loc is None
+                 else g_loc.to(torch.float32).contiguous())
+        g_attn = torch.zeros_like(attn) if g_attn is None else g_attn.to(attn.dtype).contiguous()
+        offsets = None
+        if ref.shape[-1] == 4:  # the box form's size gradient needs the offsets
+            offsets = (torch.matmul(query.reshape(-1, C).float(), weight[:2 * hlp].float().t())
+                       + bias[:2 * hlp]).contiguous()
+        g_y = torch.empty((B * Lq, 3 * hlp), dtype=torch.float32, device=dev)
+        g_ref = torch.empty_like(ref)
+        status = N.lib().rfdetr_msda_prologue_backward(
+            N.stream_of(g_loc), N.ptr(g_loc), N.ptr(g_attn), N.ptr(attn), N.dtype_code(attn.dtype), N.ptr(ref),
+            ref.shape[-1], N.ptr(offsets) if offsets is not None else None,
+            N.int64_array([v for hw in shapes for v in hw]), N.ptr(g_y), N.ptr(g_ref), B, Lq, H, L, P)
+        N.check(status, "rfdetr_msda_prologue_backward")
+        # The projection's gradients: two plain GEMMs (cuBLAS) and a column sum.
+        g_query = torch.matmul(g_y, weight.float()).reshape(B, Lq, C).to(query.dtype)
+        g_weight = torch.matmul(g_y.t(), query.reshape(-1, C).float()).to(weight.dtype)
+        g_bias = g_y.sum(0)
+        return g_query, g_ref, g_weight, g_bias, None, None, None, None
 
 
 def msda_prologue(query: torch.Tensor, reference_points: torch.Tensor, spatial_shapes, sampling_offsets_weight,

@@ -140,3 +140,22 @@ def test_rejects_bad_shapes(pkg):
         pkg.msda_prologue(query, ref[..., :1], shapes, w_off, b_off, w_att, b_att, H, L, P)
     with pytest.raises(ValueError):
         pkg.msda_prologue(query, ref, shapes, w_off[:-2], b_off, w_att, b_att, H, L, P)
+
+
+@pytest.mark.parametrize("ref_dim", [2, 4])
+def test_backward_bf16(pkg, ref_dim):
+    """bf16 queries: the same gradients as torch autograd of the restatement, within the bf16
+    tolerance (the saved attention weights and the query gradient are bf16)."""
+    C, H, L, P, shapes, B, Lq = CASES[0]
+    leaves = _params(17 + ref_dim, C, H, L, P, torch.bfloat16, B, 64, ref_dim)
+    mine = [t.clone().requires_grad_(True) for t in leaves]
+    theirs = [t.clone().requires_grad_(True) for t in leaves]
+    g = torch.Generator(device=DEV).manual_seed(4)
+    loc, attn = pkg.msda_prologue(mine[0], mine[1], shapes, *mine[2:], H, L, P)
+    g_loc = torch.randn(loc.shape, generator=g, device=DEV)
+    g_attn = torch.randn(attn.shape, generator=g, device=DEV).to(torch.bfloat16)
+    ((loc * g_loc).sum() + (attn.float() * g_attn.float()).sum()).backward()
+    want_loc, want_attn, _, _, _ = _restated(theirs[0], theirs[1], shapes, *theirs[2:], H, L, P)
+    ((want_loc * g_loc).sum() + (want_attn.float() * g_attn.float()).sum()).backward()
+    for name, a, b in zip(("query", "ref", "w_off", "b_off", "w_att", "b_att"), mine, theirs, strict=True):
+        assert_bf16_close(a.grad.float().cpu().numpy(), b.grad.float().cpu().numpy(), name)
