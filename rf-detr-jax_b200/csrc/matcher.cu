@@ -128,6 +128,7 @@ constexpr int kLsapThreads = 128;
 constexpr int kLsapWarps = kLsapThreads / 32;
 constexpr int kLsapMaxTargets = 1024;
 constexpr int kLsapMaxGroup = 4096;
+constexpr int kScanUnroll = 3;  // columns per thread per pass of a scan step (300 columns / 128 threads)
 
 struct Cand {
     double d;
@@ -285,20 +286,45 @@ __global__ void __launch_bounds__(kLsapThreads) lsap_kernel(const LsapArgs a) {
             best.d = INFINITY;
             best.k = -1;
             best.free = 0;
-            for (int k = tid; k < left; k += kLsapThreads) {
-                const int j = todo[k];
-                const double r = __dsub_rn(__dsub_rn(__dadd_rn(minv, cost_at(i, j)), ui), v[j]);
-                double d = dist[j];
-                if (r < d) {
-                    path[j] = i;
-                    dist[j] = r;
-                    d = r;
+            // kScanUnroll of the thread's columns at a time, all their loads issued before the
+            // arithmetic (the work-list entry, then the column's cost, v, dist and owner).
+            for (int k0 = tid; k0 < left; k0 += kScanUnroll * kLsapThreads) {
+                int jj[kScanUnroll];
+#pragma unroll
+                for (int u = 0; u < kScanUnroll; ++u) {
+                    const int k = k0 + u * kLsapThreads;
+                    jj[u] = k < left ? todo[k] : -1;
                 }
-                Cand c;
-                c.d = d;
-                c.k = k;
-                c.free = row4col[j] == -1;
-                if (beats(c, best)) best = c;
+                float cc[kScanUnroll];
+                double vv[kScanUnroll], dd[kScanUnroll];
+                int owner[kScanUnroll];
+#pragma unroll
+                for (int u = 0; u < kScanUnroll; ++u) {
+                    const int j = jj[u];
+                    if (j >= 0) {
+                        cc[u] = (float)cost_at(i, j);
+                        vv[u] = v[j];
+                        dd[u] = dist[j];
+                        owner[u] = row4col[j];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < kScanUnroll; ++u) {
+                    const int j = jj[u];
+                    if (j < 0) continue;
+                    const double r = __dsub_rn(__dsub_rn(__dadd_rn(minv, (double)cc[u]), ui), vv[u]);
+                    double d = dd[u];
+                    if (r < d) {
+                        path[j] = i;
+                        dist[j] = r;
+                        d = r;
+                    }
+                    Cand c;
+                    c.d = d;
+                    c.k = k0 + u * kLsapThreads;
+                    c.free = owner[u] == -1;
+                    if (beats(c, best)) best = c;
+                }
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
