@@ -274,9 +274,13 @@ __device__ __forceinline__ unsigned canon_key(float x) {
     return order_key(x != x ? __uint_as_float(0x7fc00000u) : x);
 }
 
+// Staged: the row's canonical keys are kept in dynamic shared memory from the first pass on, so
+// the histogram passes and the selection read shared memory instead of the row in L1/L2.
+template <bool Staged>
 __global__ void __launch_bounds__(kRadixThreads)
 topk_radix_kernel(const float *__restrict__ scores, int N, int k, float *__restrict__ scores_out,
                   float *__restrict__ values_out, int32_t *__restrict__ idx_out) {
+    extern __shared__ unsigned skeys[];
     __shared__ unsigned hist[256];
     __shared__ unsigned long long cand[kRadixMaxK];
     __shared__ unsigned wsum[kRadixThreads / 32];
@@ -290,9 +294,11 @@ topk_radix_kernel(const float *__restrict__ scores, int N, int k, float *__restr
         const float x = __ldg(row + i);
         if (scores_out) scores_out[(size_t)r * N + i] = x != x ? __uint_as_float(0x7fc00000u) : x;
         const unsigned key = canon_key(x);
+        if (Staged) skeys[i] = key;
         kmin = min(kmin, key);
         kmax = max(kmax, key);
     }
+    auto key_at = [&](int i) -> unsigned { return Staged ? skeys[i] : canon_key(__ldg(row + i)); };
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
@@ -330,7 +336,7 @@ topk_radix_kernel(const float *__restrict__ scores, int N, int k, float *__restr
         for (int i = tid; i < 256; i += kRadixThreads) hist[i] = 0u;
         __syncthreads();
         for (int i = tid; i < N; i += kRadixThreads) {
-            const unsigned key = canon_key(__ldg(row + i));
+            const unsigned key = key_at(i);
             if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & dmask], 1u);
         }
         __syncthreads();
@@ -381,14 +387,14 @@ topk_radix_kernel(const float *__restrict__ scores, int N, int k, float *__restr
     if (need == sh_cnt) {
         // Every key equal to T is taken: no ordered selection, the sort orders the ties.
         for (int i = tid; i < N; i += kRadixThreads) {
-            const unsigned key = canon_key(__ldg(row + i));
+            const unsigned key = key_at(i);
             if (key >= prefix)
                 cand[atomicAdd(&sh_gt, 1u)] = ((unsigned long long)key << 32) | (unsigned long long)(0xffffffffu - (unsigned)i);
         }
     }
     for (int c0 = 0; need != sh_cnt && c0 < N; c0 += kRadixThreads) {
         const int i = c0 + tid;
-        const unsigned key = i < N ? canon_key(__ldg(row + i)) : 0u;
+        const unsigned key = i < N ? key_at(i) : 0u;
         const unsigned long long full = ((unsigned long long)key << 32) | (unsigned long long)(0xffffffffu - (unsigned)i);
         if (i < N && key > prefix) cand[atomicAdd(&sh_gt, 1u)] = full;
         const bool eq = i < N && key == prefix;
@@ -500,8 +506,25 @@ extern "C" int rfdetr_topk_select(void *stream, const float *logits, int64_t row
         return launch_status();
     }
     if (radix && !std::getenv("RFDETR_TOPK_SORT")) {
-        topk_radix_kernel<<<(unsigned)rows, kRadixThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-            logits, (int)positions, (int)k, scores_out, values_out, indices_out);
+        // Keys staged in shared memory when the row fits beside the kernel's static arrays.
+        const size_t kbytes = (size_t)positions * sizeof(unsigned);
+        cudaFuncAttributes fa{};
+        int optin = 0, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        const bool staged = cudaFuncGetAttributes(&fa, topk_radix_kernel<true>) == cudaSuccess &&
+                            fa.sharedSizeBytes + kbytes <= (size_t)optin && !std::getenv("RFDETR_TOPK_UNSTAGED");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (staged) {
+            if (cudaFuncSetAttribute(topk_radix_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kbytes) != cudaSuccess)
+                return RFDETR_ERR_CUDA;
+            topk_radix_kernel<true><<<(unsigned)rows, kRadixThreads, kbytes, s>>>(
+                logits, (int)positions, (int)k, scores_out, values_out, indices_out);
+        } else {
+            topk_radix_kernel<false><<<(unsigned)rows, kRadixThreads, 0, s>>>(
+                logits, (int)positions, (int)k, scores_out, values_out, indices_out);
+        }
         return launch_status();
     }
     if (positions > kTopkMaxPositions) return RFDETR_ERR_SHAPE;

@@ -77,11 +77,25 @@ def test_special_values(pkg, monkeypatch, path):
 
 @pytest.mark.parametrize(("positions", "classes", "k"), [(1, 1, 1), (7, 3, 7), (576, 91, 1), (1000, 1, 999),
                                                           (5000, 2, 300), (16384, 1, 16384), (2049, 1, 2049),
-                                                          (4097, 1, 1), (20000, 1, 4096), (27300, 1, 300)])
+                                                          (4097, 1, 1), (20000, 1, 4096), (27300, 1, 300),
+                                                          (60000, 1, 100)])
 def test_sizes(pkg, positions, classes, k):
     logits = np.random.default_rng(positions).integers(-50, 50, (3, positions, classes)).astype(np.float32)
     s, v, i = _select(pkg, logits, k)
     ws, wv, wi = OT.two_stage_select(logits, k)
+    np.testing.assert_array_equal(i, wi)
+    np.testing.assert_array_equal(v, wv)
+
+
+@pytest.mark.parametrize("unstaged", [False, True])
+def test_radix_staging(pkg, monkeypatch, unstaged):
+    """The radix select with the row's keys staged in shared memory (rows up to ~48k) and without
+    (RFDETR_TOPK_UNSTAGED, the path of longer rows) on the same tie-heavy rows."""
+    if unstaged:
+        monkeypatch.setenv("RFDETR_TOPK_UNSTAGED", "1")
+    logits = np.random.default_rng(11).integers(-20, 20, (4, 27300, 1)).astype(np.float32)
+    s, v, i = _select(pkg, logits, 300)
+    ws, wv, wi = OT.two_stage_select(logits, 300)
     np.testing.assert_array_equal(i, wi)
     np.testing.assert_array_equal(v, wv)
 
