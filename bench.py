@@ -694,11 +694,12 @@ def run_ours(args):
     e2e_ring = 3
     dev_slots = [packed(host, device, False) for _ in range(e2e_ring)]
     dev_in = [views for _, views in dev_slots]
-    h_res = [[torch.empty((B, LQ, H * D), dtype=torch.bfloat16).pin_memory(), torch.empty_like(host[0]).pin_memory(),
-              torch.empty_like(host[1]).pin_memory(), torch.empty_like(host[2]).pin_memory()]
-             for _ in range(e2e_ring)]
+    # Results likewise: gathered on the device into one slot buffer, read back in one transfer.
+    res_like = [torch.empty((B, LQ, H * D), dtype=torch.bfloat16), host[0], host[1], host[2]]
+    h_res = [packed(res_like, "cpu", True) for _ in range(e2e_ring)]
+    d_res = [packed(res_like, device, False) for _ in range(e2e_ring)]
     h2d = host_buf.numel()  # the one transfer per step (inputs plus alignment padding)
-    d2h = sum(x.numel() * x.element_size() for x in h_res[0])
+    d2h = h_res[0][0].numel()
     s_h2d, s_cmp, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device), torch.cuda.Stream(device)
     in_ready = [torch.cuda.Event() for _ in range(e2e_ring)]
     in_free = [torch.cuda.Event() for _ in range(e2e_ring)]
@@ -723,18 +724,16 @@ def run_ours(args):
             out.backward(dev_in[r][3])
             in_free[r].record(s_cmp)
             s_cmp.wait_event(res_done[r])  # the slot's pinned results were read back
-            res = (out.detach(), v.grad, loc.grad, a.grad)
+            for dst, t in zip(d_res[r][1], (out.detach(), v.grad, loc.grad, a.grad)):
+                dst.copy_(t)
             res_ready[r].record(s_cmp)
         with torch.cuda.stream(s_d2h):
             s_d2h.wait_event(res_ready[r])
-            for hbuf, t in zip(h_res[r], res):
-                t.record_stream(s_d2h)
-                hbuf.copy_(t, non_blocking=True)
+            h_res[r][0].copy_(d_res[r][0], non_blocking=True)
             res_done[r].record(s_d2h)
 
-    # At least 12 untimed steps: the results of a step are handed to the copy-out stream
-    # (record_stream), so the caching allocator only reaches its steady set of blocks after a few
-    # ring turns; earlier steps still allocate.
+    # At least 12 untimed steps, so the caching allocator has reached its steady set of blocks
+    # for the autograd outputs before the timed trials.
     for i in range(max(args.warmup, 12)):
         e2e_step(i)
     torch.cuda.synchronize()
