@@ -16,8 +16,9 @@
 //     distance, ties going to an unassigned column (the later one in the work list), else to the
 //     earliest one in the work list.
 // One CTA solves one block: the column scan of each augmenting step is spread over the CTA's
-// threads and the arg-min is a CTA reduction under that tie order.  The block's costs are read
-// through L1 (optionally staged in shared memory up to a per-CTA budget).
+// threads and the arg-min is a CTA reduction under that tie order.  The block's costs are staged
+// in shared memory when they fit the largest per-CTA budget that keeps two CTAs on an SM,
+// otherwise read through L1.
 #include <algorithm>
 
 #include "common.cuh"
@@ -498,13 +499,20 @@ int launch_lsap(void *stream, const float *cost, const int32_t *sizes, int64_t s
     a.status = status_out;
     const int M = std::max(a.Qg, a.T);
     const size_t state = lsap_state_bytes(M);
-    // Costs are read through L1 by default: staging blocks in shared memory measured slower at
-    // config 4 (277 vs 265 us with a 100 KB stage; fewer CTAs fit an SM).  RFDETR_LSAP_STAGE_KB
-    // sets a stage budget per CTA.
-    int dev = 0, optin = 0;
+    // Stage budget: the most shared memory a CTA can take while two still fit an SM.  A
+    // transposed solve reads one target's cost for every query per scan step (a column of the
+    // [Q, T] block: one cache line per query from L2), so staging the block cuts the step; the
+    // largest blocks, which set the launch's duration, need ~90 KB at config 4 (235 us with this
+    // budget, 261 us unstaged, 274 us at 100 KB, 398 us once only one CTA fits an SM).
+    // RFDETR_LSAP_STAGE_KB overrides it.
+    int dev = 0, optin = 0, per_sm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    size_t budget = 0;
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaFuncAttributes fa{};
+    const size_t static_bytes = cudaFuncGetAttributes(&fa, lsap_kernel) == cudaSuccess ? fa.sharedSizeBytes : 0;
+    const size_t half = (size_t)per_sm / 2;
+    size_t budget = half > 1024 + static_bytes ? ((half - 1024 - static_bytes) & ~(size_t)15) : 0;
     if (const char *e = getenv("RFDETR_LSAP_STAGE_KB")) budget = (size_t)atoi(e) * 1024;
     const size_t want = (size_t)a.Qg * a.T * sizeof(float);
     size_t stage = std::min(want, budget > state ? budget - state : 0);

@@ -200,10 +200,12 @@ def test_stacked_single_layer_shape(pkg):
     _assert_same([x.cpu().numpy() for x in (rows, cols, valid)], OM.hungarian_match(cost.cpu().numpy(), sizes, 2))
 
 
-def test_staged_costs(pkg, monkeypatch):
-    """The solver with each block's costs staged in shared memory (a per-CTA budget set through
-    RFDETR_LSAP_STAGE_KB; by default costs are read through L1) gives SciPy's assignment too."""
-    monkeypatch.setenv("RFDETR_LSAP_STAGE_KB", "100")
+@pytest.mark.parametrize("budget_kb", ["0", "100"])
+def test_stage_budgets(pkg, monkeypatch, budget_kb):
+    """The solver with no shared-memory stage (costs read through L1, the path of blocks too big
+    to stage) and with a smaller stage than the default, set through RFDETR_LSAP_STAGE_KB: SciPy's
+    assignment either way."""
+    monkeypatch.setenv("RFDETR_LSAP_STAGE_KB", budget_kb)
     rng = np.random.default_rng(5)
     groups, per_group, max_targets = 4, 60, 30
     cost = rng.standard_normal((5, groups * per_group, max_targets)).astype(np.float32)
