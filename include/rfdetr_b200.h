@@ -43,6 +43,23 @@ const char *rfdetr_status_string(int status);
 /* ABI version of this library; bumped on any signature change. */
 int rfdetr_abi_version(void);
 
+/* Sets a process-wide tuning knob.  Knobs exist for experiments and tests; every default is the
+ * tuned production choice.  `name` is one of
+ *   "RFDETR_MSDA_FWD", "RFDETR_MSDA_BWD", "RFDETR_MSDA_SLAB_FWD", "RFDETR_MSDA_BINS",
+ *   "RFDETR_MSDA_OWN" (sampler kernel selection and launch shapes, "a,b,c,d,e"),
+ *   "RFDETR_LSAP_STAGE_KB" (the assignment's shared-memory cost stage, KiB),
+ *   "RFDETR_LSAP_STEP_CAP" (scan steps an augmenting path may take before the solve gives up with
+ *   RFDETR_ERR_LIMIT; default: the block's column count, which finite costs never exceed),
+ *   "RFDETR_TOPK_SORT", "RFDETR_TOPK_UNSTAGED" (any value: the one-CTA sort kernels; the radix
+ *   select without its shared-memory key stage);
+ * `value` is up to five comma-separated integers, or NULL / "" for the default.  Environment
+ * variables of the same names are read once, before the first knob is read or set; after that
+ * only this call changes a knob (launches read them from atomics, never from the environment).
+ * A knob changed while another thread launches may be seen half-updated by that launch.
+ * Returns RFDETR_ERR_SHAPE for an unknown name or a malformed value.  No reference counterpart:
+ * the reference tunes through XLA flags (src/rfdetr_jax/utilities/gpu_flags.py:15). */
+int rfdetr_set_tuning(const char *name, const char *value);
+
 /* Reads and clears the device fault word.  Kernels that wait on hardware barriers (the TMA
  * tile loads of the sampler backward) bound every wait; a wait that gives up sets this word and
  * the kernel finishes with undefined outputs instead of hanging.  Synchronises `stream`.
@@ -169,7 +186,9 @@ int rfdetr_select_rows(void *stream, const void *values, int64_t element_bytes, 
  *                 + cost_giou * (-GIoU(pb, tb)),   or 1e4 where target_mask[b,t] == 0.
  *   pred_logits [B, Q, C] (f32 | bf16), pred_boxes [B, Q, 4] (f32 | bf16, cxcywh),
  *   target_labels [B, T] int32, target_boxes [B, T, 4] f32, target_mask [B, T] uint8,
- *   cost [B, Q, T] f32.  Labels outside [0, C) produce NaN costs.
+ *   cost [B, Q, T] f32.  The target's logit is read as the reference's one-hot contraction
+ *   gives it: a label outside [0, C) reads 0, and a non-finite logit at any other class of the
+ *   row makes the row's class costs NaN (x * 0 = NaN).
  * ------------------------------------------------------------------------------------- */
 int rfdetr_match_cost(void *stream, const void *pred_logits, int logits_dtype,
                       const void *pred_boxes, int boxes_dtype, const int32_t *target_labels,

@@ -4,7 +4,9 @@ Restates:
 
 * ``focal_classification_cost`` (``src/rfdetr_jax/models/matcher.py:36-41``);
 * ``build_cost_matrix`` for boxes and classes (``matcher.py:44-103,141``): the target class is
-  read out of the logits, ``cost = cost_bbox * L1 + cost_class * focal + cost_giou * (-GIoU)``,
+  read out of the logits with the one-hot contraction's semantics (:func:`onehot_gather_f32`),
+  in float64 (:func:`build_cost_matrix`) or in float32 in the reference's operation order
+  (:func:`build_cost_matrix_f32`), ``cost = cost_bbox * L1 + cost_class * focal + cost_giou * (-GIoU)``,
   and padded target slots get ``1e4``;
 * ``box_cxcywh_to_xyxy`` / ``box_iou`` / ``generalized_box_iou``
   (``src/rfdetr_jax/utilities/box_ops.py:27-75``), keeping the ``1e-7`` clamps;
@@ -81,14 +83,111 @@ def build_cost_matrix(pred_logits, pred_boxes, target_labels, target_boxes, targ
     batch, queries, _ = logits.shape
     targets = labels.shape[1]
     cost = np.empty((batch, queries, targets), np.float64)
+    gathered_all = onehot_gather_f32(logits.astype(np.float32), labels).astype(np.float64)
     for b in range(batch):
-        gathered = logits[b][:, labels[b]]  # [Q, T] -- the one-hot einsum of :92-93
+        gathered = gathered_all[b]  # [Q, T] -- the one-hot einsum of :92-93 (exact for finite rows)
         class_cost = focal_classification_cost(gathered, focal_alpha)
         bbox_cost = np.abs(boxes[b][:, None, :] - tboxes[b][None, :, :]).sum(-1)
         giou = generalized_box_iou(box_cxcywh_to_xyxy(boxes[b]), box_cxcywh_to_xyxy(tboxes[b]))
         cost[b] = cost_bbox * bbox_cost + cost_class * class_cost + cost_giou * (-giou)
     cost = np.where(mask[:, None, :], cost, 1e4)
     return cost.astype(np.float32)
+
+
+def onehot_gather_f32(logits: np.ndarray, labels: np.ndarray) -> np.ndarray:
+    """``einsum("bqc,btc->bqt", logits, one_hot(labels))`` in float32 (``matcher.py:92-93``).
+
+    For a finite logit row the contraction is exactly ``logits[b, q, label]`` (one product by 1,
+    the rest by 0), and 0 for a label outside ``[0, C)`` (``one_hot`` gives an all-zero row).  A
+    non-finite logit anywhere else in the row makes its ``x * 0`` term NaN, so the whole row of
+    gathered values is NaN -- except an infinite logit at the target's own class with every other
+    logit finite, which sums to that infinity.
+    """
+    logits = np.asarray(logits, np.float32)
+    labels = np.asarray(labels).astype(np.int64)
+    in_range = (labels >= 0) & (labels < logits.shape[-1])  # an out-of-range label: all-zero one-hot
+    safe = np.where(in_range, labels, 0)
+    gathered = np.take_along_axis(logits[:, :, None, :], safe[:, None, :, None], -1)[..., 0]
+    gathered = np.where(in_range[:, None, :], gathered, np.float32(0))
+    bad = ~np.isfinite(logits)  # [B, Q, C]
+    n_bad = bad.sum(-1)  # [B, Q]
+    own_bad = np.take_along_axis(bad[:, :, None, :], safe[:, None, :, None], -1)[..., 0] & in_range[:, None, :]
+    other_bad = (n_bad[:, :, None] - own_bad) > 0
+    gathered = np.where(other_bad | np.isnan(gathered), np.float32(np.nan), gathered)
+    return gathered.astype(np.float32)
+
+
+def build_cost_matrix_f32(pred_logits, pred_boxes, target_labels, target_boxes, target_mask,
+                          cost_class=2.0, cost_bbox=5.0, cost_giou=2.0, focal_alpha=0.25) -> np.ndarray:
+    """``build_cost_matrix`` evaluated in float32 in the reference's operation order.
+
+    Every step rounds to float32 as the reference's ``jnp`` expression does:
+
+    * the one-hot gather of :func:`onehot_gather_f32` (``matcher.py:92-93``);
+    * ``focal_classification_cost`` (``matcher.py:36-41``): ``p = sigmoid(x)``,
+      ``negative = ((1 - alpha) * p**2) * softplus(x)``, ``positive = (alpha * (1 - p)**2) *
+      softplus(-x)`` (``-log_sigmoid(-x)`` is ``softplus(x)``, ``jax.nn.log_sigmoid(x) =
+      -softplus(-x)``; ``p**2`` is ``p * p``, the form XLA simplifies ``pow(p, 2)`` to),
+      ``positive - negative``;
+    * the L1 term ``|pb - tb|`` summed over the four coordinates left to right (``:95``);
+    * ``box_cxcywh_to_xyxy`` and ``generalized_box_iou`` (``box_ops.py:27-75``) in float32 with
+      the ``1e-7`` clamps;
+    * ``cost_bbox * l1 + cost_class * class + cost_giou * (-giou)`` summed left to right
+      (``matcher.py:103``), ``1e4`` in padded slots (``:141``).
+
+    ``sigmoid``, ``exp`` and ``log1p`` are NumPy's float32 functions; XLA's may differ in the last
+    bit, which is the sensitivity the assignment-flip count measures.
+    """
+    f = np.float32
+    logits = np.asarray(pred_logits, f)
+    boxes = np.asarray(pred_boxes, f)
+    tboxes = np.asarray(target_boxes, f)
+    mask = np.asarray(target_mask).astype(bool)
+    with np.errstate(over="ignore", invalid="ignore"):
+        x = onehot_gather_f32(logits, target_labels)
+        p = (f(1) / (f(1) + np.exp(-x))).astype(f)
+        sp_pos = np.logaddexp(x, f(0)).astype(f)
+        sp_neg = np.logaddexp(-x, f(0)).astype(f)
+        negative = ((f(1 - focal_alpha) * (p * p)) * sp_pos).astype(f)
+        q = (f(1) - p).astype(f)
+        positive = ((f(focal_alpha) * (q * q)) * sp_neg).astype(f)
+        class_cost = (positive - negative).astype(f)
+        d = np.abs(boxes[:, :, None, :] - tboxes[:, None, :, :]).astype(f)
+        l1 = (((d[..., 0] + d[..., 1]) + d[..., 2]) + d[..., 3]).astype(f)
+
+        def xyxy(bx):
+            cx, cy, w, h = bx[..., 0], bx[..., 1], np.clip(bx[..., 2], f(0), None), np.clip(bx[..., 3], f(0), None)
+            hw, hh = f(0.5) * w, f(0.5) * h
+            return np.stack([cx - hw, cy - hh, cx + hw, cy + hh], -1).astype(f)
+
+        b1 = xyxy(boxes)[:, :, None, :]
+        b2 = xyxy(tboxes)[:, None, :, :]
+        area1 = ((b1[..., 2] - b1[..., 0]) * (b1[..., 3] - b1[..., 1])).astype(f)
+        area2 = ((b2[..., 2] - b2[..., 0]) * (b2[..., 3] - b2[..., 1])).astype(f)
+        lt = np.maximum(b1[..., :2], b2[..., :2])
+        rb = np.minimum(b1[..., 2:], b2[..., 2:])
+        wh = np.clip(rb - lt, f(0), None).astype(f)
+        inter = (wh[..., 0] * wh[..., 1]).astype(f)
+        union = ((area1 + area2) - inter).astype(f)
+        iou = (inter / np.clip(union, f(1e-7), None)).astype(f)
+        lt = np.minimum(b1[..., :2], b2[..., :2])
+        rb = np.maximum(b1[..., 2:], b2[..., 2:])
+        wh = np.clip(rb - lt, f(0), None).astype(f)
+        area = (wh[..., 0] * wh[..., 1]).astype(f)
+        giou = (iou - ((area - union) / np.clip(area, f(1e-7), None)).astype(f)).astype(f)
+        cost = ((f(cost_bbox) * l1 + f(cost_class) * class_cost).astype(f) + f(cost_giou) * (-giou)).astype(f)
+    return np.where(mask[:, None, :], cost, f(1e4)).astype(f)
+
+
+def assignment_objective(cost64: np.ndarray, rows: np.ndarray, cols: np.ndarray, valid: np.ndarray) -> np.ndarray:
+    """Total float64 cost of each problem's assignment (``[N, G*T]`` slots of
+    :func:`solve_batch`) on ``cost64 [N, Q, T]``."""
+    n = cost64.shape[0]
+    out = np.zeros(n, np.float64)
+    for i in range(n):
+        v = valid[i].astype(bool)
+        out[i] = cost64[i, rows[i][v], cols[i][v]].sum()
+    return out
 
 
 def _load_lib():

@@ -14,6 +14,7 @@ Components (each a thin host wrapper over ``librfdetr_b200.so``, see ``include/r
 """
 
 from . import _native
+from ._native import check_device_status, set_tuning
 from .matcher import CriterionConfig, build_cost_matrix, hungarian_match, match_stacked
 from .ops import (MSDeformAttnFunction, MSDeformAttnPrologueFunction, ms_deform_attn, ms_deform_attn_core,
                   ms_deform_attn_core_rows, msda_prologue)
@@ -25,6 +26,7 @@ __all__ = [
     "CriterionConfig",
     "MSDeformAttnFunction",
     "build_cost_matrix",
+    "check_device_status",
     "hungarian_match",
     "match_stacked",
     "ms_deform_attn",
@@ -34,6 +36,7 @@ __all__ = [
     "MSDeformAttnPrologueFunction",
     "post_process",
     "set_losses",
+    "set_tuning",
     "SetLossFunction",
     "select_rows",
     "top_k",

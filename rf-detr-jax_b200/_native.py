@@ -41,6 +41,7 @@ _f32 = ctypes.c_float
 SIGNATURES = {
     "rfdetr_status_string": (ctypes.c_char_p, [_int]),
     "rfdetr_abi_version": (_int, []),
+    "rfdetr_set_tuning": (_int, [ctypes.c_char_p, ctypes.c_char_p]),
     "rfdetr_take_device_fault": (_int, [_vp]),
     "rfdetr_msda_forward": (_int, [_vp, _vp, _int, _c_int64_p, _c_int64_p, _vp, _vp, _int, _vp, _int,
                                    _i64, _i64, _i64, _i64, _i64, _i64]),
@@ -86,6 +87,22 @@ def lib() -> ctypes.CDLL:
                 fn.argtypes = argtypes
             _lib = handle
     return _lib
+
+
+def set_tuning(name: str, value: str | None) -> None:
+    """Sets a process-wide tuning knob of the library (``rfdetr_set_tuning``): ``value`` is
+    ``"a,b,..."`` (up to five integers) or ``None`` for the library's default.  Knob names are
+    those of the environment variables the library reads once at its first launch, e.g.
+    ``"RFDETR_LSAP_STAGE_KB"``."""
+    status = lib().rfdetr_set_tuning(name.encode(), None if value is None else str(value).encode())
+    if status != OK:
+        raise ValueError(f"unknown tuning knob {name!r} or malformed value {value!r}")
+
+
+def check_device_status(status: torch.Tensor, what: str = "device status") -> None:
+    """Reads a device status word written by an entry point (synchronises its stream) and raises
+    for a non-zero status."""
+    check(int(status.reshape(-1)[0].item()), what)
 
 
 def status_text(status: int) -> str:

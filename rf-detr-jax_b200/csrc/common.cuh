@@ -98,4 +98,27 @@ inline int launch_status() {
 
 int num_sms();  // SM count of the current device (cached per device)
 
+// Process-wide tuning knobs, for experiments and tests.  A knob holds up to five integers, set
+// from the environment variable of the knob's name ("a,b,c,d,e"; read once, the first time any
+// knob is read) or by rfdetr_set_tuning(); `count` is how many were given (0: not set, the
+// launchers use their own defaults).  Launchers read a knob per call from atomics: no getenv,
+// no lock.
+enum Knob {
+    kKnobMsdaFwd,       // "RFDETR_MSDA_FWD": generic sampler forward "hsub,stage,acc,threads,waves"
+    kKnobMsdaBwd,       // "RFDETR_MSDA_BWD": generic sampler backward, same fields
+    kKnobMsdaSlabFwd,   // "RFDETR_MSDA_SLAB_FWD": slab forward (hsub, stage = 0 disables, ..., waves)
+    kKnobMsdaBins,      // "RFDETR_MSDA_BINS": capped-bin backward (stage = 0 disables)
+    kKnobMsdaOwn,       // "RFDETR_MSDA_OWN": owner backward (hsub = bin cap, stage = 0 disables, acc = 0 no TMA, threads = tile)
+    kKnobLsapStageKb,   // "RFDETR_LSAP_STAGE_KB": shared-memory cost stage budget of the solver, KiB
+    kKnobLsapStepCap,   // "RFDETR_LSAP_STEP_CAP": scan steps an augmenting path may take (default: the column count)
+    kKnobTopkSort,      // "RFDETR_TOPK_SORT": any value selects the one-CTA sort kernels
+    kKnobTopkUnstaged,  // "RFDETR_TOPK_UNSTAGED": any value keeps the radix select's keys out of shared memory
+    kKnobCount
+};
+struct KnobValue {
+    int count;
+    int v[5];
+};
+KnobValue knob(Knob k);
+
 }  // namespace rfdetr

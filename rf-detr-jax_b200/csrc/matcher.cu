@@ -78,6 +78,12 @@ match_cost_kernel(const TL *__restrict__ logits, const TB *__restrict__ boxes, c
         const float ax1 = pcx + 0.5f * pwc, ay1 = pcy + 0.5f * phc;
         const float area1 = (ax1 - ax0) * (ay1 - ay0);
         const TL *lrow = logits + qrow * C;
+        // The reference reads a target's logit through a one-hot contraction (matcher.py:92-93):
+        // a non-finite logit at any other class contributes x * 0 = NaN to every target of the
+        // row.  Count the row's non-finite logits once.
+        int nbad = 0;
+        for (int c = lane; c < C; c += 32) nbad += isfinite(ldf(lrow + c)) ? 0 : 1;
+        nbad = __reduce_add_sync(0xffffffffu, nbad);
         for (int t = lane; t < T; t += 32) {
             float out;
             if (tsm[1 * T + t] == 0.f) {
@@ -85,9 +91,12 @@ match_cost_kernel(const TL *__restrict__ logits, const TB *__restrict__ boxes, c
             } else {
                 const int label = __float_as_int(tsm[0 * T + t]);
                 // Focal classification cost (matcher.py:36-41) on the target's own logit.
-                float cls = qnan;
-                if (label >= 0 && label < C) {
-                    const float x = ldf(lrow + label);
+                // A label outside [0, C) has an all-zero one-hot row: its logit reads as 0.
+                float x = 0.f;
+                if (label >= 0 && label < C) x = ldf(lrow + label);
+                if (nbad - (isfinite(x) ? 0 : 1) > 0 || x != x) x = qnan;
+                float cls;
+                {
                     const float e_ = __expf(-fabsf(x));
                     const float u = 1.f + e_;
                     const float l1p = __logf(u);                // log1p(e): u - 1 >= 0.0067 unless e_ is tiny
@@ -98,7 +107,7 @@ match_cost_kernel(const TL *__restrict__ logits, const TB *__restrict__ boxes, c
                     const float pm = x >= 0.f ? e_ * inv : inv;  // 1 - sigmoid(x)
                     const float negative = (1.f - alpha) * (p * p) * sp_pos;
                     const float positive = alpha * (pm * pm) * sp_neg;
-                    cls = positive - negative;
+                    cls = x != x ? qnan : positive - negative;
                 }
                 const float l1 = ((fabsf(pcx - tsm[2 * T + t]) + fabsf(pcy - tsm[3 * T + t])) +
                                   fabsf(pw - tsm[4 * T + t])) + fabsf(ph - tsm[5 * T + t]);
@@ -161,6 +170,7 @@ struct LsapArgs {
     int size_mod;
     int Q, T, G, Qg;
     int smem_cost_floats;  // capacity of the shared cost stage (0 = never stage)
+    int step_cap;          // scan steps an augmenting path may take before the solve gives up
     int32_t *rows, *cols;
     uint8_t *valid;
     int32_t *status;
@@ -277,7 +287,8 @@ __global__ void __launch_bounds__(kLsapThreads) lsap_kernel(const LsapArgs a) {
         }
         __syncthreads();
 
-        for (int step = 0; step <= nc; ++step) {  // each step retires one column
+        const int steps = min(nc, a.step_cap - 1);
+        for (int step = 0; step <= steps; ++step) {  // each step retires one column
             const int i = s_i;
             const int left = s_left;
             const double minv = s_minv;
@@ -504,7 +515,7 @@ int launch_lsap(void *stream, const float *cost, const int32_t *sizes, int64_t s
     // [Q, T] block: one cache line per query from L2), so staging the block cuts the step; the
     // largest blocks, which set the launch's duration, need ~90 KB at config 4 (235 us with this
     // budget, 261 us unstaged, 274 us at 100 KB, 398 us once only one CTA fits an SM).
-    // RFDETR_LSAP_STAGE_KB overrides it.
+    // The RFDETR_LSAP_STAGE_KB knob overrides it.
     int dev = 0, optin = 0, per_sm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
@@ -513,7 +524,10 @@ int launch_lsap(void *stream, const float *cost, const int32_t *sizes, int64_t s
     const size_t static_bytes = cudaFuncGetAttributes(&fa, lsap_kernel) == cudaSuccess ? fa.sharedSizeBytes : 0;
     const size_t half = (size_t)per_sm / 2;
     size_t budget = half > 1024 + static_bytes ? ((half - 1024 - static_bytes) & ~(size_t)15) : 0;
-    if (const char *e = getenv("RFDETR_LSAP_STAGE_KB")) budget = (size_t)atoi(e) * 1024;
+    const KnobValue stage_kb = knob(kKnobLsapStageKb);
+    if (stage_kb.count > 0) budget = (size_t)std::max(stage_kb.v[0], 0) * 1024;
+    const KnobValue step_cap = knob(kKnobLsapStepCap);
+    a.step_cap = step_cap.count > 0 ? std::max(step_cap.v[0], 1) : 0x7fffffff;
     const size_t want = (size_t)a.Qg * a.T * sizeof(float);
     size_t stage = std::min(want, budget > state ? budget - state : 0);
     if (state + stage > (size_t)optin) stage = (size_t)optin > state ? (size_t)optin - state : 0;

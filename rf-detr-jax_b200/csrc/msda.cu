@@ -473,15 +473,16 @@ int next_pow2(int x) {
     return p;
 }
 
-// Tuning overrides for experiments: RFDETR_MSDA_FWD / RFDETR_MSDA_BWD = "hsub,stage,acc,threads,waves".
+// Tuning overrides for experiments ("hsub,stage,acc,threads,waves"; the knobs of common.cuh).
 struct Tune {
     int hsub = 0, stage = -1, acc = -1, threads = 0, waves = 0;
 };
 
-Tune read_tune(const char *name) {
+Tune read_tune(Knob k) {
     Tune t;
-    const char *s = getenv(name);
-    if (s && *s) sscanf(s, "%d,%d,%d,%d,%d", &t.hsub, &t.stage, &t.acc, &t.threads, &t.waves);
+    const KnobValue kv = knob(k);
+    int *fields[5] = {&t.hsub, &t.stage, &t.acc, &t.threads, &t.waves};
+    for (int i = 0; i < kv.count; ++i) *fields[i] = kv.v[i];
     return t;
 }
 
@@ -959,7 +960,7 @@ bool plan_forward_slab(const Geom &g, const void *value, const float *loc, const
     if (!aligned(value, 16) || !aligned(out, 16)) return false;
     const size_t slab = (size_t)g.Lv * g.D * es;
     if (slab % 16 != 0) return false;
-    const Tune tune = read_tune("RFDETR_MSDA_SLAB_FWD");
+    const Tune tune = read_tune(kKnobMsdaSlabFwd);
     if (tune.stage == 0) return false;
     const size_t budget = 100 * 1024;
     int best = 0;
@@ -1035,7 +1036,7 @@ int try_forward_slab(const Geom &g, const void *value, const float *loc, const v
                      cudaStream_t stream) {
     SlabPlan sp;
     if (!plan_forward_slab<TV, TW>(g, value, loc, attn, out, max_smem_optin(), sp)) return -1;
-    const int waves = std::max(1, read_tune("RFDETR_MSDA_SLAB_FWD").waves);
+    const int waves = std::max(1, read_tune(kKnobMsdaSlabFwd).waves);
     switch (g.L * g.P) {
         case 1: return launch_forward_slab<TV, TW, 1>(g, sp, value, loc, attn, out, stream, waves);
         case 2: return launch_forward_slab<TV, TW, 2>(g, sp, value, loc, attn, out, stream, waves);
@@ -1342,7 +1343,7 @@ bool plan_backward_bins(const Geom &g, const void *value, const float *loc, cons
     if (!(LP == 1 || LP == 2 || LP == 4 || LP == 8)) return false;
     if (g.D % 8 != 0 || g.D / 8 > 32 || ((g.D / 8) & (g.D / 8 - 1))) return false;
     if (!aligned(value, 16) || !aligned(grad_value, 16)) return false;
-    const Tune tune = read_tune("RFDETR_MSDA_BINS");
+    const Tune tune = read_tune(kKnobMsdaBins);
     if (tune.stage == 0) return false;
     bp.slab_bytes = (size_t)g.Lv * g.D * 2;
     const int chunks = g.D / 8;
@@ -1874,7 +1875,7 @@ bool plan_backward_owner(const Geom &g, const void *value, const float *loc, con
     const int owners = g.Lv * (g.D / 16);
     if (owners > kOwnMaxThreads) return false;
     if (!aligned(value, 16) || !aligned(grad_value, 16)) return false;
-    const Tune tune = read_tune("RFDETR_MSDA_OWN");
+    const Tune tune = read_tune(kKnobMsdaOwn);
     if (tune.stage == 0) return false;
     auto granule = [](long long seg, long long stride, const void *base) -> int {
         for (int gsz = 16; gsz >= 4; gsz >>= 1)
@@ -2049,7 +2050,7 @@ extern "C" int rfdetr_msda_forward(void *stream, const void *value, int value_dt
     if (!p.vec) return aligned(value, vs) && aligned(output, os) ? RFDETR_ERR_SHAPE : RFDETR_ERR_ALIGN;
     p.team = next_pow2(g.D / p.vec);
     choose_layout(p, g, vs, false, value);
-    const Tune tune = read_tune("RFDETR_MSDA_FWD");
+    const Tune tune = read_tune(kKnobMsdaFwd);
     apply_tune(p, tune, g, vs, false, value);
     p.smem = plan_smem(p, g, vs);
     if (p.smem > (size_t)max_smem_optin()) return RFDETR_ERR_SHAPE;
@@ -2135,7 +2136,7 @@ extern "C" int rfdetr_msda_backward(void *stream, const void *value, int value_d
         if (!p.vec) return RFDETR_ERR_ALIGN;
         p.team = next_pow2(g.D / p.vec);
         choose_layout(p, g, vs, true, value);
-        const Tune tune = read_tune("RFDETR_MSDA_BWD");
+        const Tune tune = read_tune(kKnobMsdaBwd);
         apply_tune(p, tune, g, vs, true, value);
         p.smem = plan_smem(p, g, vs);
         if (p.smem > (size_t)max_smem_optin()) return RFDETR_ERR_SHAPE;

@@ -499,13 +499,13 @@ extern "C" int rfdetr_topk_select(void *stream, const float *logits, int64_t row
     if (!aligned(logits, 4) || !aligned(indices_out, 4) || (scores_out && !aligned(scores_out, 4)) ||
         (values_out && !aligned(values_out, 4)))
         return RFDETR_ERR_ALIGN;
-    if (positions <= kTopkClusterMaxPositions && rows * kTopkCluster <= 2147483647LL && !std::getenv("RFDETR_TOPK_SORT")) {
+    if (positions <= kTopkClusterMaxPositions && rows * kTopkCluster <= 2147483647LL && knob(kKnobTopkSort).count == 0) {
         topk_cluster_kernel<kTopkCluster><<<(unsigned)(rows * kTopkCluster), kTopkClusterThreads, 0,
                                             static_cast<cudaStream_t>(stream)>>>(
             logits, (int)positions, (int)classes, (int)k, scores_out, values_out, indices_out);
         return launch_status();
     }
-    if (radix && !std::getenv("RFDETR_TOPK_SORT")) {
+    if (radix && knob(kKnobTopkSort).count == 0) {
         // Keys staged in shared memory when the row fits beside the kernel's static arrays.
         const size_t kbytes = (size_t)positions * sizeof(unsigned);
         cudaFuncAttributes fa{};
@@ -513,7 +513,7 @@ extern "C" int rfdetr_topk_select(void *stream, const float *logits, int64_t row
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         const bool staged = cudaFuncGetAttributes(&fa, topk_radix_kernel<true>) == cudaSuccess &&
-                            fa.sharedSizeBytes + kbytes <= (size_t)optin && !std::getenv("RFDETR_TOPK_UNSTAGED");
+                            fa.sharedSizeBytes + kbytes <= (size_t)optin && knob(kKnobTopkUnstaged).count == 0;
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         if (staged) {
             if (cudaFuncSetAttribute(topk_radix_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,

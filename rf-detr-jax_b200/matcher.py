@@ -20,6 +20,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _native as N
+from ._native import check_device_status  # noqa: F401  (re-exported)
 
 
 def build_cost_matrix(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, target_labels: torch.Tensor,
@@ -56,7 +57,8 @@ def build_cost_matrix(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targe
 
 def match_stacked(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, target_labels: torch.Tensor,
                   target_boxes: torch.Tensor, target_mask: torch.Tensor, sizes: torch.Tensor, group_detr: int,
-                  cost_class: float, cost_bbox: float, cost_giou: float, focal_alpha: float, check: bool = True):
+                  cost_class: float, cost_bbox: float, cost_giou: float, focal_alpha: float, check: bool = False,
+                  status: torch.Tensor | None = None):
     """Cost and exact assignment of every stacked layer in one call: one cost launch over all
     layers and images, then one batched solve (bit for bit :func:`build_cost_matrix` per layer
     followed by :func:`hungarian_match` of the stacked cost).
@@ -65,6 +67,13 @@ def match_stacked(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, target_la
         pred_logits ``[..., B, Q, C]``, pred_boxes ``[..., B, Q, 4]`` (leading axes: layers);
         target_labels ``[B, T]``, target_boxes ``[B, T, 4]``, target_mask ``[B, T]`` shared by the
         layers; sizes ``[B]``; group_detr divides ``Q``.
+
+        check: read the device status word right away (synchronises the stream).  Off by
+            default: the status only reports a solve that reached its iteration cap, which finite
+            costs never do, and reading it every step would stall the stream.
+        status: optional device ``int32`` tensor (one element, zero before the first call) that
+            receives the status; it is only ever raised, so one tensor can collect many calls and
+            be read once with :func:`check_device_status`.
 
     Returns:
         ``(cost [..., B, Q, T] float32, rows int32, cols int32, valid bool)``, the last three
@@ -93,27 +102,42 @@ def match_stacked(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, target_la
     rows = torch.empty((*leading, batch, slots), dtype=torch.int32, device=dev)
     cols = torch.empty_like(rows)
     valid = torch.empty((*leading, batch, slots), dtype=torch.uint8, device=dev)
-    status_buf = torch.zeros((1,), dtype=torch.int32, device=dev)
-    status = N.lib().rfdetr_match_stacked(
+    status_buf = _status_buffer(status, dev)
+    st = N.lib().rfdetr_match_stacked(
         N.stream_of(logits), N.ptr(logits), N.dtype_code(logits.dtype), N.ptr(boxes), N.dtype_code(boxes.dtype),
         N.ptr(target_labels.to(torch.int32).contiguous()), N.ptr(target_boxes.to(torch.float32).contiguous()),
         N.ptr(target_mask.to(torch.uint8).contiguous()), N.ptr(sizes.to(torch.int32).contiguous()), layers, batch,
         queries, classes, targets, group_detr, float(cost_class), float(cost_bbox), float(cost_giou),
         float(focal_alpha), N.ptr(cost), N.ptr(rows), N.ptr(cols), N.ptr(valid), N.ptr(status_buf))
-    N.check(status, "rfdetr_match_stacked")
+    N.check(st, "rfdetr_match_stacked")
     if check:
-        N.check(int(status_buf.item()), "rfdetr_match_stacked (device status)")
+        N.check_device_status(status_buf, "rfdetr_match_stacked (device status)")
     return cost, rows, cols, valid.to(torch.bool)
 
 
-def hungarian_match(cost: torch.Tensor, sizes: torch.Tensor, group_detr: int, check: bool = True):
+def _status_buffer(status, device):
+    if status is None:
+        return torch.zeros((1,), dtype=torch.int32, device=device)
+    if status.dtype != torch.int32 or status.numel() < 1 or status.device != device or not status.is_contiguous():
+        raise ValueError("status must be a contiguous int32 tensor on the cost's device")
+    return status
+
+
+def hungarian_match(cost: torch.Tensor, sizes: torch.Tensor, group_detr: int, check: bool = False,
+                    status: torch.Tensor | None = None):
     """Exact assignment of every (layer, image, group) block in one launch.
 
     Args:
         cost: ``[..., B, Q, T]``; cast to float32 as the reference does (``matcher.py:203``).
         sizes: real target count per image ``[B]``.
         group_detr: number of query groups; must divide ``Q``.
-        check: read the device status flag after the launch (synchronises the stream).
+        check: read the device status word right away (synchronises the stream).  Off by
+            default: a solve only reports a status when it reaches its iteration cap, which
+            finite costs never do, and reading it every step would stall the stream.
+        status: optional device ``int32`` tensor (one element, zero before the first call) that
+            receives ``RFDETR_ERR_LIMIT`` if a solve gives up; the word is only ever raised, so one
+            tensor can collect many calls and be read once with :func:`check_device_status`.
+            A block whose solve gives up keeps its cleared slots ``(0, 0, False)``.
 
     Returns:
         ``(rows int32, cols int32, valid bool)``, each ``[..., B, group_detr * T]``.
@@ -130,13 +154,13 @@ def hungarian_match(cost: torch.Tensor, sizes: torch.Tensor, group_detr: int, ch
     rows = torch.empty((problems, slots), dtype=torch.int32, device=cost.device)
     cols = torch.empty((problems, slots), dtype=torch.int32, device=cost.device)
     valid = torch.empty((problems, slots), dtype=torch.uint8, device=cost.device)
-    status_buf = torch.zeros((1,), dtype=torch.int32, device=cost.device)
-    status = N.lib().rfdetr_lsap_batched(N.stream_of(folded), N.ptr(folded), N.ptr(folded_sizes), problems, queries,
-                                         max_targets, group_detr, N.ptr(rows), N.ptr(cols), N.ptr(valid),
-                                         N.ptr(status_buf))
-    N.check(status, "rfdetr_lsap_batched")
+    status_buf = _status_buffer(status, cost.device)
+    st = N.lib().rfdetr_lsap_batched(N.stream_of(folded), N.ptr(folded), N.ptr(folded_sizes), problems, queries,
+                                     max_targets, group_detr, N.ptr(rows), N.ptr(cols), N.ptr(valid),
+                                     N.ptr(status_buf))
+    N.check(st, "rfdetr_lsap_batched")
     if check:
-        N.check(int(status_buf.item()), "rfdetr_lsap_batched (device status)")
+        N.check_device_status(status_buf, "rfdetr_lsap_batched (device status)")
     shape = (*leading, batch, slots)
     return rows.reshape(shape), cols.reshape(shape), valid.to(torch.bool).reshape(shape)
 

@@ -40,3 +40,18 @@ def pkg():
     import __graft_entry__
 
     return __graft_entry__.load_package()
+
+
+@pytest.fixture
+def tuning(pkg):
+    """``tuning(name, value)`` sets one of the library's process-wide tuning knobs
+    (``rfdetr_set_tuning``) for the test; every knob it touched returns to its default after."""
+    touched = []
+
+    def set_knob(name, value):
+        touched.append(name)
+        pkg._native.set_tuning(name, value)
+
+    yield set_knob
+    for name in touched:
+        pkg._native.set_tuning(name, None)

@@ -201,14 +201,95 @@ def test_stacked_single_layer_shape(pkg):
 
 
 @pytest.mark.parametrize("budget_kb", ["0", "100"])
-def test_stage_budgets(pkg, monkeypatch, budget_kb):
+def test_stage_budgets(pkg, tuning, budget_kb):
     """The solver with no shared-memory stage (costs read through L1, the path of blocks too big
     to stage) and with a smaller stage than the default, set through RFDETR_LSAP_STAGE_KB: SciPy's
     assignment either way."""
-    monkeypatch.setenv("RFDETR_LSAP_STAGE_KB", budget_kb)
+    tuning("RFDETR_LSAP_STAGE_KB", budget_kb)
     rng = np.random.default_rng(5)
     groups, per_group, max_targets = 4, 60, 30
     cost = rng.standard_normal((5, groups * per_group, max_targets)).astype(np.float32)
     cost[1, 3, 2] = np.nan
     sizes = np.array([30, 1, 17, 0, 29], np.int32)
     _assert_same(_match(pkg, cost, sizes, groups), OM.hungarian_match(cost, sizes, groups))
+
+
+def test_config4_reference_order_flips(pkg):
+    """The kernel pipeline (one ``match_stacked`` call: device cost, device solve) against SciPy
+    -- the reference's solver -- on the cost evaluated in float32 in the reference's operation
+    order (``oracle.matcher.build_cost_matrix_f32``), at config 4's training shape: 312
+    assignments.  The two costs differ in the last bits (at most ~4e-6; asserted < 2e-5, the tie
+    margin an assignment must fall inside to flip) and 0 of the 312 assignments differ."""
+    groups, per_group, classes, max_targets, batch = 13, 300, 91, 100, 8
+    lg, bx, labels, tboxes, mask, sizes = _stacked_inputs(10, 3, batch, groups, per_group, classes, max_targets)
+    cost, rows, cols, valid = pkg.match_stacked(_t(lg), _t(bx), _t(labels), _t(tboxes), _t(mask), _t(sizes), groups,
+                                                2.0, 5.0, 2.0, 0.25)
+    ref_cost = np.stack([OM.build_cost_matrix_f32(lg[i], bx[i], labels, tboxes, mask) for i in range(3)])
+    assert np.abs(cost.cpu().numpy().astype(np.float64) - ref_cost).max() < 2e-5
+    want = OM.hungarian_match(ref_cost, sizes, groups)
+    got = [x.cpu().numpy().reshape(3 * batch, groups, max_targets) for x in (rows, cols, valid)]
+    want = [x.reshape(3 * batch, groups, max_targets) for x in want]
+    flips = ((got[0] != want[0]) | (got[1] != want[1]) | (got[2] != want[2])).any(-1)
+    assert int(flips.sum()) == 0, f"{int(flips.sum())} of {flips.size} assignments differ"
+
+
+def test_nonfinite_logits_follow_the_onehot(pkg):
+    """A non-finite logit poisons its row's class costs as the reference's one-hot contraction
+    does (x * 0 = NaN at every other target), an infinite logit at the target's own class gives an
+    infinite cost, and a label outside [0, C) reads logit 0; the assignment after the solver's
+    sentinel replacement is SciPy's on the oracle's cost."""
+    logits, boxes, labels, tboxes, mask, sizes = match_inputs(77, 3, 60, 11, 8, sizes=[8, 5, 3])
+    logits[0, 4, 6] = np.nan
+    logits[1, 10, :] = 0.5
+    logits[1, 10, labels[1, 0]] = np.inf
+    logits[2, 7, 3] = -np.inf
+    labels[2, 1] = 11          # outside [0, C): an all-zero one-hot row
+    labels[2, 2] = -1
+    cost = pkg.build_cost_matrix(_t(logits), _t(boxes), _t(labels), _t(tboxes), _t(mask), 2.0, 5.0, 2.0, 0.25)
+    got = cost.cpu().numpy()
+    want = OM.build_cost_matrix_f32(logits, boxes, labels, tboxes, mask)
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(want))
+    np.testing.assert_array_equal(np.isinf(got), np.isinf(want))
+    fin = np.isfinite(want)
+    np.testing.assert_allclose(got[fin], want[fin], rtol=COST_RTOL, atol=COST_ATOL)
+    assert np.isnan(got[0, 4, :sizes[0]]).all() and np.isinf(got[1, 10, 0])
+    _assert_same(_match(pkg, got, sizes, 2), OM.hungarian_match(want, sizes, 2))
+
+
+def test_step_cap_reports_and_leaves_no_stale_slots(pkg, tuning):
+    """A solve that reaches its iteration cap (forced here by capping every augmenting path at one
+    scan step: every target wants the same query -- the blocks are tall, so they are solved
+    transposed with targets as rows -- and the second target's insertion needs two) reports
+    RFDETR_ERR_LIMIT through the device status word, which the host raises, and leaves its slots
+    cleared -- nothing stale from before the call survives.  The cap is a pure-compute loop
+    bound: nothing waits."""
+    tuning("RFDETR_LSAP_STEP_CAP", "1")
+    n, groups, per_group, max_targets = 3, 2, 20, 6
+    cost = np.ones((n, groups * per_group, max_targets), np.float32)
+    cost[:, 3::per_group, :] = 0.0  # in each group, every target prefers the group's query 3
+    sizes = np.array([6, 4, 2], np.int32)
+    N = pkg._native
+    dev_cost, dev_sizes = _t(cost), _t(sizes)
+    rows = torch.full((n, groups * max_targets), -7, dtype=torch.int32, device=DEV)
+    cols = torch.full_like(rows, -7)
+    valid = torch.full((n, groups * max_targets), 0xAB, dtype=torch.uint8, device=DEV)
+    status = torch.zeros((1,), dtype=torch.int32, device=DEV)
+    st = N.lib().rfdetr_lsap_batched(torch.cuda.current_stream().cuda_stream, N.ptr(dev_cost), N.ptr(dev_sizes), n,
+                                     groups * per_group, max_targets, groups, N.ptr(rows), N.ptr(cols), N.ptr(valid),
+                                     N.ptr(status))
+    assert st == N.OK
+    assert int(status.item()) == N.ERR_LIMIT
+    assert not rows.any() and not cols.any() and not valid.any()
+    with pytest.raises(RuntimeError, match="iteration cap"):
+        pkg.hungarian_match(dev_cost, dev_sizes, groups, check=True)
+    # The python API collects the status in a caller's tensor without synchronising.
+    word = torch.zeros((1,), dtype=torch.int32, device=DEV)
+    pkg.hungarian_match(dev_cost, dev_sizes, groups, status=word)
+    with pytest.raises(RuntimeError):
+        pkg.check_device_status(word)
+    # With the default cap the same problems solve, as SciPy does.
+    tuning("RFDETR_LSAP_STEP_CAP", None)
+    word.zero_()
+    got = pkg.hungarian_match(dev_cost, dev_sizes, groups, status=word)
+    pkg.check_device_status(word)
+    _assert_same([x.cpu().numpy() for x in got], OM.hungarian_match(cost, sizes, groups))

@@ -220,12 +220,12 @@ def test_unaligned_views_and_entry_points(pkg):
         ("float32 workspace", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_BINS": "0,0"}),
     ],
 )
-def test_backward_variants(pkg, monkeypatch, paths, env):
+def test_backward_variants(pkg, tuning, paths, env):
     """Every backward variant the library can select (tile loads by TMA or cp.async, bins that
     overflow and are refiled, the capped-bin and workspace kernels) against the oracle, over
     several tiles; then the device fault word must be clear (no bounded wait gave up)."""
     for k, v in env.items():
-        monkeypatch.setenv(k, v)
+        tuning(k, v)
     args = dict(seed=5, batch=2, len_query=1300, heads=16, shapes=((24, 24),), points=2, dim=16, lo=-0.05, hi=1.05)
     value, loc, attn, grad = sampler_inputs(**args)
     value, attn, grad = O.bf16_round(value), O.bf16_round(attn), O.bf16_round(grad)
@@ -243,12 +243,12 @@ def test_backward_variants(pkg, monkeypatch, paths, env):
         ("owner, cp.async tile loads", {"RFDETR_MSDA_OWN": "24,1,0"}),
     ],
 )
-def test_backward_non_finite_rows(pkg, monkeypatch, paths, env):
+def test_backward_non_finite_rows(pkg, tuning, paths, env):
     """inf/NaN entries in value rows (including border rows that clipped corners read) and in
     gradient rows: the same outputs are non-finite as in the float64 oracle (the reference's
     0 * inf = NaN through clipped corners included), and the finite ones agree."""
     for k, v in env.items():
-        monkeypatch.setenv(k, v)
+        tuning(k, v)
     args = dict(seed=9, batch=2, len_query=1100, heads=4, shapes=((24, 24),), points=2, dim=16, lo=-0.05, hi=1.05)
     value, loc, attn, grad = sampler_inputs(**args)
     value, attn, grad = O.bf16_round(value), O.bf16_round(attn), O.bf16_round(grad)

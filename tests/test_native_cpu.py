@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol(pkg):
     for name in _declared():
         assert hasattr(raw, name), f"{name} declared in include/rfdetr_b200.h but not exported"
         assert name in pkg._native.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.rfdetr_abi_version() == 1
+    assert lib.rfdetr_abi_version() == 2
     assert pkg._native.status_text(0) == "ok"
     assert "element type" in pkg._native.status_text(2)
 
@@ -84,3 +84,19 @@ def test_python_api_rejects_cpu_tensors_and_unknown_names(pkg):
         pkg.hungarian_match(torch.zeros((1, 4, 2)), torch.ones(1, dtype=torch.int32), 1)
     with pytest.raises(ValueError, match="CUDA tensors"):
         pkg.two_stage_topk(torch.zeros((2, 5, 3)), 2)
+
+
+def test_tuning_knobs(pkg):
+    """Knobs are set by name (no device needed); unknown names and malformed values are refused,
+    and None restores the default."""
+    N = pkg._native
+    N.set_tuning("RFDETR_LSAP_STEP_CAP", "3")
+    N.set_tuning("RFDETR_LSAP_STEP_CAP", None)
+    N.set_tuning("RFDETR_MSDA_OWN", "24,1,0")
+    N.set_tuning("RFDETR_MSDA_OWN", "")
+    with pytest.raises(ValueError):
+        N.set_tuning("RFDETR_NO_SUCH_KNOB", "1")
+    with pytest.raises(ValueError):
+        N.set_tuning("RFDETR_MSDA_OWN", "1,x")
+    with pytest.raises(ValueError):
+        N.set_tuning("RFDETR_MSDA_OWN", "1,2,3,4,5,6")

@@ -130,3 +130,47 @@ def test_goldens_reproduce():
     rows, cols, valid = OM.hungarian_match(m["cost"], m["sizes"], int(m["groups"]), solver=OM.lsap_c)
     np.testing.assert_array_equal(rows, m["rows"])
     np.testing.assert_array_equal(cols, m["cols"])
+
+
+def test_onehot_gather_semantics():
+    """``einsum("bqc,btc->bqt", logits, one_hot(labels))`` (``matcher.py:92-93``): the target's
+    logit for a finite row, 0 for a label outside [0, C), NaN for every target of a row holding a
+    non-finite logit at another class, the infinity itself when only the target's logit is."""
+    logits = np.array([[[0.5, 1.0, -2.0], [np.nan, 1.0, 2.0], [np.inf, 0.0, 1.0], [-np.inf, 3.0, 4.0]]], np.float32)
+    labels = np.array([[0, 2, 5, -1]], np.int32)
+    got = OM.onehot_gather_f32(logits, labels)
+    want = np.array([[[0.5, -2.0, 0.0, 0.0], [np.nan] * 4, [np.inf, np.nan, np.nan, np.nan],
+                      [-np.inf, np.nan, np.nan, np.nan]]], np.float32)
+    np.testing.assert_array_equal(got, want)
+    # Against the contraction itself, evaluated by NumPy in float32.
+    rng = np.random.default_rng(0)
+    lg = rng.standard_normal((2, 30, 7)).astype(np.float32)
+    lg[0, 3, 4] = np.nan
+    lg[1, 9, 2] = np.inf
+    lb = rng.integers(-1, 9, (2, 5)).astype(np.int32)
+    onehot = (lb[..., None] == np.arange(7)).astype(np.float32)
+    with np.errstate(invalid="ignore"):
+        direct = np.einsum("bqc,btc->bqt", lg, onehot)
+    np.testing.assert_array_equal(OM.onehot_gather_f32(lg, lb), direct)
+
+
+def test_reference_order_cost_flip_count():
+    """Config 4 at training shape (3 layers x 8 images x 13 groups = 312 assignments): the cost
+    evaluated in float32 in the reference's operation order (``build_cost_matrix_f32``) and the
+    float64 evaluation rounded once differ in the last bits of ~30% of the entries, by at most
+    3.5e-6 (asserted < 1e-5: the tie margin an assignment would have to fall inside to flip), and
+    SciPy assigns all 312 blocks identically on both: 0 flips."""
+    groups, per_group, classes, max_targets, batch = 13, 300, 91, 100, 8
+    logits, boxes, labels, tboxes, mask, sizes = match_inputs(10, batch, groups * per_group, classes, max_targets)
+    c64, c32 = [], []
+    for layer in range(3):
+        lg = np.random.default_rng(100 + layer).standard_normal(logits.shape).astype(np.float32)
+        c64.append(OM.build_cost_matrix(lg, boxes, labels, tboxes, mask))
+        c32.append(OM.build_cost_matrix_f32(lg, boxes, labels, tboxes, mask))
+    c64, c32 = np.stack(c64), np.stack(c32)
+    diff = np.abs(c64.astype(np.float64) - c32.astype(np.float64))
+    assert diff.max() < 1e-5 and (c64 != c32).mean() > 0.05
+    a = [x.reshape(3 * batch, groups, max_targets) for x in OM.hungarian_match(c64, sizes, groups)]
+    b = [x.reshape(3 * batch, groups, max_targets) for x in OM.hungarian_match(c32, sizes, groups)]
+    flips = ((a[0] != b[0]) | (a[1] != b[1]) | (a[2] != b[2])).any(-1)
+    assert int(flips.sum()) == 0

@@ -31,12 +31,12 @@ def test_golden(pkg):
 
 
 @pytest.mark.parametrize("path", ["cluster ranks", "bitonic sort"])
-def test_config4_training_shape(pkg, monkeypatch, path):
+def test_config4_training_shape(pkg, tuning, path):
     """Config 4 at training shape: 13 groups x 8 images x 576 proposals x 91 classes, through
     both selection kernels (the cluster rank count serves rows of up to 2048 positions, the
     bitonic sort longer rows; the switch forces the sort here)."""
     if path == "bitonic sort":
-        monkeypatch.setenv("RFDETR_TOPK_SORT", "1")
+        tuning("RFDETR_TOPK_SORT", "1")
     logits = np.random.default_rng(4).standard_normal((13, 8, 576, 91)).astype(np.float32)
     s, v, i = _select(pkg, logits, 300)
     ws, wv, wi = OT.two_stage_select(logits, 300)
@@ -57,10 +57,10 @@ def test_ties_keep_lower_index_first(pkg):
 
 
 @pytest.mark.parametrize("path", ["cluster ranks", "bitonic sort"])
-def test_special_values(pkg, monkeypatch, path):
+def test_special_values(pkg, tuning, path):
     """NaN first, then +inf ... -inf; +0 above -0 (IEEE totalOrder)."""
     if path == "bitonic sort":
-        monkeypatch.setenv("RFDETR_TOPK_SORT", "1")
+        tuning("RFDETR_TOPK_SORT", "1")
     row = np.array([1.0, -np.inf, np.nan, 0.0, -0.0, np.inf, -1.0, 2.0], np.float32)
     v, i = pkg.top_k(torch.tensor(row[None], device=DEV), 8)
     wv, wi = OT.top_k(row[None], 8)
@@ -88,11 +88,11 @@ def test_sizes(pkg, positions, classes, k):
 
 
 @pytest.mark.parametrize("unstaged", [False, True])
-def test_radix_staging(pkg, monkeypatch, unstaged):
+def test_radix_staging(pkg, tuning, unstaged):
     """The radix select with the row's keys staged in shared memory (rows up to ~48k) and without
     (RFDETR_TOPK_UNSTAGED, the path of longer rows) on the same tie-heavy rows."""
     if unstaged:
-        monkeypatch.setenv("RFDETR_TOPK_UNSTAGED", "1")
+        tuning("RFDETR_TOPK_UNSTAGED", "1")
     logits = np.random.default_rng(11).integers(-20, 20, (4, 27300, 1)).astype(np.float32)
     s, v, i = _select(pkg, logits, 300)
     ws, wv, wi = OT.two_stage_select(logits, 300)
