@@ -34,6 +34,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -81,10 +82,11 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, directory=None):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        directory = directory or os.environ.get("RFDETR_BENCH_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(directory, f"rfdetr_bench_clocks_gpu{gpu_index}_{os.getpid()}.csv")
 
     def __enter__(self):
         try:

@@ -68,6 +68,13 @@ int rfdetr_set_tuning(const char *name, const char *value);
  * under XLA, which has no device-side waits. */
 int rfdetr_take_device_fault(void *stream);
 
+/* Self-test of the bounded device waits: one CTA arms a shared-memory barrier for 16 bytes that
+ * no copy delivers and waits at most `polls` polls (1 .. 2^22).  The wait gives up, *result
+ * (device int32) receives 0 (1 would mean the barrier completed), and the fault word is raised,
+ * so the next rfdetr_take_device_fault() returns RFDETR_ERR_LIMIT.  Nothing is left in flight and
+ * the context stays usable.  Asynchronous on `stream`.  No reference counterpart. */
+int rfdetr_selftest_bounded_wait(void *stream, int polls, int32_t *result);
+
 /* ---------------------------------------------------------------------------------------
  * Multi-scale deformable attention sampler.
  *
@@ -130,15 +137,20 @@ int rfdetr_msda_backward(void *stream,
  *
  * The bf16 path's float32 accumulator lives in a static device array of the library
  * (RFDETR_MSDA_NOALLOC_SCRATCH_BYTES, 8 MiB; every GPU that loads the library holds it until the
- * process exits), so batch * n_heads * Lv * head_dim must not exceed 2,097,152 elements for bf16
- * values; larger problems return RFDETR_ERR_CAPACITY without launching anything.  Float32 values
- * need no scratch and have no extra limit.  The entry point itself allocates nothing.
+ * process exits), so a call that needs it must have batch * n_heads * Lv * head_dim <= 2,097,152
+ * elements; a larger call that needs it returns RFDETR_ERR_CAPACITY without launching anything.
+ * Shapes that the scratch-free bf16 kernels serve (D in {16, 32}, L*P in {1, 2, 4, 8}, small
+ * enough slabs -- the Nano decoder's among them) never touch the array and have no extra limit;
+ * nor do float32 values.  The entry point itself allocates nothing.
  *
  * The first call on each device looks up the array's device address (cudaGetSymbolAddress, with
- * that device current); make that first call before any stream capture.  Every call on a device
- * shares the one array: the call clears it before use, but calls whose work overlaps on the GPU
- * (different streams, or different host threads, on the same device) race on it and must be
- * serialised by the caller.  Arguments and results are those of rfdetr_msda_backward.
+ * that device current) and caches it per device index; make that first call before any stream
+ * capture.  The address belongs to the device's primary context, the one the CUDA runtime uses:
+ * call from threads whose current context is that primary context, and not across a
+ * cudaDeviceReset (which destroys it and would leave the cached address dangling).  Every call on
+ * a device shares the one array: the call clears it before use, but calls whose work overlaps on
+ * the GPU (different streams, or different host threads, on the same device) race on it and must
+ * be serialised by the caller.  Arguments and results are those of rfdetr_msda_backward.
  */
 #define RFDETR_MSDA_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
 int rfdetr_msda_backward_noalloc(void *stream,

@@ -19,7 +19,7 @@
  *   - duals: u[cur] += minVal; u[i] += minVal - d[col4row[i]] for the other scanned rows;
  *     v[j] -= minVal - d[j] for scanned columns; then the path is flipped back to cur.
  *
- * It exists to be checked bit-exactly against SciPy (tests/test_oracle_lsap.py), which pins
+ * It exists to be checked bit-exactly against SciPy (tests/test_oracle_lsap_topk.py), which pins
  * the tie rules that the CUDA solver reproduces.
  */
 #include <math.h>

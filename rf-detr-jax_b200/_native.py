@@ -43,6 +43,7 @@ SIGNATURES = {
     "rfdetr_abi_version": (_int, []),
     "rfdetr_set_tuning": (_int, [ctypes.c_char_p, ctypes.c_char_p]),
     "rfdetr_take_device_fault": (_int, [_vp]),
+    "rfdetr_selftest_bounded_wait": (_int, [_vp, _int, _vp]),
     "rfdetr_msda_forward": (_int, [_vp, _vp, _int, _c_int64_p, _c_int64_p, _vp, _vp, _int, _vp, _int,
                                    _i64, _i64, _i64, _i64, _i64, _i64]),
     "rfdetr_msda_backward_workspace_size": (ctypes.c_size_t, [_int, _i64, _i64, _i64, _i64]),

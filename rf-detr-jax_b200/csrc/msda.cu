@@ -20,6 +20,7 @@
 // directly with vector global reductions -- and rounded once.  grad_loc and grad_weights are
 // produced in the same pass from team-reduced dot products.
 #include <algorithm>
+#include <initializer_list>
 #include <cstdio>
 #include <mutex>
 #include <cstdlib>
@@ -500,8 +501,19 @@ int validate(const int64_t *shapes, const int64_t *starts, int64_t B, int64_t H,
         g.ls[l] = (int)total;
         total += h * w;
     }
+    // Every tensor must hold fewer than 2^31 elements.  The products are formed factor by factor
+    // with a bound check before each multiply, so no intermediate can overflow.
     const long long lim = (1LL << 31) - 1;
-    if (B * H * total * D > lim || B * Lq * H * L * P * 2 > lim || B * Lq * H * D > lim) return RFDETR_ERR_SHAPE;
+    auto within = [lim](std::initializer_list<long long> factors) {
+        long long p = 1;
+        for (long long f : factors) {
+            if (f < 0 || (f > 0 && p > lim / f)) return false;
+            p *= f;
+        }
+        return true;
+    };
+    if (B > lim || H > lim || D > lim || Lq > lim || total > lim) return RFDETR_ERR_SHAPE;
+    if (!within({B, H, total, D}) || !within({B, Lq, H, L, P, 2}) || !within({B, Lq, H, D})) return RFDETR_ERR_SHAPE;
     g.B = (int)B; g.H = (int)H; g.D = (int)D; g.Lq = (int)Lq; g.L = (int)L; g.P = (int)P; g.Lv = (int)total;
     return RFDETR_OK;
 }
@@ -1521,6 +1533,7 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
     __shared__ float lvl_f[LP][2];
     __shared__ __align__(8) uint64_t mbar[3];
     __shared__ int abort_flag;
+    __shared__ int armed[3];     // last tile whose loads were armed on each barrier (-1: none)
     __shared__ int slab_bad;     // some value row of the slab holds inf/NaN
     __shared__ int tile_bad[3];  // some gradient row of the tile in that slot holds inf/NaN
     unsigned char *const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1548,7 +1561,10 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
 
     if constexpr (TMA) {
         if (tid == 0) {
-            for (int i = 0; i < 3; ++i) mbar_init(&mbar[i], 1);
+            for (int i = 0; i < 3; ++i) {
+                mbar_init(&mbar[i], 1);
+                armed[i] = -1;
+            }
             abort_flag = 0;
             mbar_init_fence();
             tma_prefetch_map(&tm_loc);
@@ -1586,7 +1602,8 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
                                reinterpret_cast<const char *>(attn + (row0 + (size_t)qi * g.H) * LP) + j * op.ga,
                                op.ga);
             }
-            if (tid == 0) {
+            if (tid == 0 && !abort_flag) {  // a CTA that gave up arms nothing more
+                armed[slot] = t;
                 mbar_arrive_expect_tx(&mbar[slot], op.tx_bytes);
                 for (int r = 0; r < op.tq; r += op.box) {
                     tma_load_4d(locb(slot) + r * LP, &tm_loc, &mbar[slot], 0, h, q0 + r, b);
@@ -1852,6 +1869,14 @@ msda_backward_owner_kernel(const bf16 *__restrict__ value, const float *__restri
         finish(t, qbeg + t * op.tq, qend - (qbeg + t * op.tq));
     }
 
+    if constexpr (TMA) {
+        // Gave up waiting: let the copies this CTA armed land before it exits (each barrier has at
+        // most one armed phase outstanding, since a tile is armed only after the previous tile of
+        // its slot landed or the CTA aborted, and an aborted CTA arms nothing).
+        if (abort_flag && tid == 0)
+            for (int i = 0; i < 3; ++i)
+                if (armed[i] >= 0) mbar_drain(&mbar[i], (unsigned)(armed[i] / 3) & 1u);
+    }
     __syncthreads();  // the last finish may have poisoned rows
     if (is_owner) {
         const unsigned pois = gpois[pos] >> (16 * seg);
@@ -2196,7 +2221,16 @@ extern "C" int rfdetr_msda_backward_noalloc(void *stream, const void *value, int
                                 n_points, g);
         if (st) return st;
         const size_t need = rfdetr_msda_backward_workspace_size(value_dtype, batch, n_heads, head_dim, g.Lv);
-        if (need > kNoAllocScratchBytes) return RFDETR_ERR_CAPACITY;
+        if (need > kNoAllocScratchBytes) {
+            // Too large for the array: still served when a scratch-free kernel takes the shape (the
+            // workspace path is then never reached); refused when the call would need scratch.
+            const int st2 = rfdetr_msda_backward(stream, value, value_dtype, spatial_shapes, level_start_index,
+                                                 sampling_locations, attention_weights, weight_dtype, grad_output,
+                                                 grad_output_dtype, grad_value, grad_sampling_locations,
+                                                 grad_attention_weights, nullptr, 0, batch, n_heads, head_dim,
+                                                 len_query, n_levels, n_points);
+            return st2 == RFDETR_ERR_WORKSPACE ? RFDETR_ERR_CAPACITY : st2;
+        }
         int dev = 0;
         if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return RFDETR_ERR_CUDA;
         {
@@ -2215,6 +2249,33 @@ extern "C" int rfdetr_msda_backward_noalloc(void *stream, const void *value, int
                                 attention_weights, weight_dtype, grad_output, grad_output_dtype, grad_value,
                                 grad_sampling_locations, grad_attention_weights, scratch, scratch_bytes, batch,
                                 n_heads, head_dim, len_query, n_levels, n_points);
+}
+
+namespace rfdetr {
+namespace {
+// One CTA arms an mbarrier for 16 bytes that no copy delivers and waits for it at most `polls`
+// polls: the wait must give up and raise the fault word.  Nothing is in flight, so nothing needs
+// draining.
+__global__ void bounded_wait_selftest_kernel(int polls, int32_t *result) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        mbar_init_fence();
+        mbar_arrive_expect_tx(&bar, 16u);
+    }
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0u, &abort_flag, polls);
+    if (threadIdx.x == 0) *result = ok ? 1 : 0;
+}
+}  // namespace
+}  // namespace rfdetr
+
+extern "C" int rfdetr_selftest_bounded_wait(void *stream, int polls, int32_t *result) {
+    if (polls < 1 || polls > rfdetr::kWaitLimit || !result) return RFDETR_ERR_SHAPE;
+    rfdetr::bounded_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(polls, result);
+    return launch_status();
 }
 
 extern "C" int rfdetr_take_device_fault(void *stream) {

@@ -10,7 +10,9 @@
 // Waits are bounded: a wait that has not completed after kWaitLimit polls (each poll of
 // mbarrier.try_wait suspends for a hardware-defined interval) raises the device fault word and
 // returns false; a shared abort flag makes the CTA's other waiters give up at once, so the
-// kernel runs to completion with undefined outputs instead of hanging.  The host reads and
+// kernel runs to completion with undefined outputs instead of hanging.  A CTA that gave up arms no
+// further barriers and, before it exits, drains (again bounded) the phases it armed, so no copy
+// is still writing its shared memory when it leaves.  The host reads and
 // clears the fault word with rfdetr_take_device_fault().
 #pragma once
 
@@ -58,14 +60,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
 }
 
 // Bounded wait for the barrier phase with the given parity; see the file comment.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, volatile int *abort_flag) {
-    for (int i = 0; i < kWaitLimit; ++i) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, volatile int *abort_flag,
+                                          int limit = kWaitLimit) {
+    for (int i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
     }
     *abort_flag = 1;
     atomicOr(&g_device_fault, 1u);
     return false;
+}
+
+// After a CTA gave up waiting: waits (bounded, ignoring the abort flag) for a phase this CTA armed
+// and whose copies may still be in flight, so that no bulk copy lands in shared memory after the
+// CTA has exited.  A drain that gives up too raises bit 1 of the fault word.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, unsigned parity, int limit = kWaitLimit) {
+    for (int i = 0; i < limit; ++i)
+        if (mbar_try_wait(bar, parity)) return;
+    atomicOr(&g_device_fault, 2u);
 }
 
 // 4-D tiled load of one box into shared memory, completing on `bar`.

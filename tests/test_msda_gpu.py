@@ -283,3 +283,23 @@ def test_error_behaviour(pkg):
         pkg.ms_deform_attn_core_rows(v.half(), ((3, 3),), l, a.half())
     empty = pkg.ms_deform_attn_core_rows(v, ((3, 3),), l[:, :0], a[:, :0])
     assert empty.shape == (1, 0, 8)
+
+
+def test_bounded_wait_gives_up_and_reports(pkg):
+    """A device wait on a barrier that nothing completes (armed for 16 bytes no copy delivers) gives
+    up after its poll limit, raises the fault word, and the host reads and clears it; the context
+    stays usable (a sampler call afterwards is exact)."""
+    N = pkg._native
+    lib = N.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.rfdetr_take_device_fault(stream) == N.OK
+    result = torch.full((1,), -1, dtype=torch.int32, device=DEV)
+    N.check(lib.rfdetr_selftest_bounded_wait(stream, 2000, result.data_ptr()), "selftest")
+    assert int(result.item()) == 0
+    assert lib.rfdetr_take_device_fault(stream) == N.ERR_LIMIT
+    assert lib.rfdetr_take_device_fault(stream) == N.OK
+    assert lib.rfdetr_selftest_bounded_wait(stream, 0, result.data_ptr()) == N.ERR_SHAPE
+    value, loc, attn, grad = sampler_inputs(3, 1, 50, 2, ((6, 5),), 2, 8)
+    out = pkg.ms_deform_attn_core_rows(torch.tensor(value, device=DEV), ((6, 5),), torch.tensor(loc, device=DEV),
+                                       torch.tensor(attn, device=DEV))
+    assert_fp32_close(out.cpu().numpy(), O.ms_deform_attn_forward(value, ((6, 5),), loc, attn), "after the self-test")

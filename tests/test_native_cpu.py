@@ -54,6 +54,12 @@ def test_argument_validation_without_a_device(pkg):
     bad_start = N.int64_array([1])
     assert lib.rfdetr_msda_forward(None, None, 0, shapes, bad_start, None, None, 0, None, 0, 1, 1, 4, 1, 1,
                                    1) == N.ERR_SHAPE
+    # Sizes whose element counts overflow int64 when multiplied are refused, not wrapped.
+    huge = 1 << 40
+    assert lib.rfdetr_msda_forward(None, None, 0, shapes, None, None, None, 0, None, 0, huge, huge, huge, huge, 1,
+                                   1) == N.ERR_SHAPE
+    assert lib.rfdetr_msda_forward(None, None, 0, shapes, None, None, None, 0, None, 0, 1 << 20, 1 << 20, 1 << 20,
+                                   1, 1, 1) == N.ERR_SHAPE
     # Empty batch is a no-op.
     assert lib.rfdetr_msda_forward(None, None, 0, shapes, None, None, None, 0, None, 0, 0, 1, 4, 1, 1, 1) == N.OK
     assert lib.rfdetr_msda_backward_workspace_size(0, 8, 16, 16, 576) == 0

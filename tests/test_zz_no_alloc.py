@@ -7,8 +7,10 @@ start-up.  For them the bf16 backward keeps its float32 accumulator in a static 
 the library instead of a caller-provided workspace.  This test calls both entry points through
 the C ABI on config-2 inputs and checks that two consecutive no-alloc calls each reproduce the
 workspace call within the bf16 tolerance the other tests use (the array keeps the previous
-call's contents, so the second call also checks that it is cleared), and that a problem larger
-than the array is refused without a launch.  It lives in its own file, collected last.
+call's contents, so the second call also checks that it is cleared) and the oracle, that a
+problem needing more scratch than the array holds is refused without a launch, and that a large
+problem the scratch-free kernels serve is not refused.  It lives in its own file, collected
+last.
 """
 
 from __future__ import annotations
@@ -65,11 +67,14 @@ def test_noalloc_backward_matches_workspace_backward(pkg):
         assert_fp32_close(got[1], want[1], f"call {call}: grad_loc")
         assert_bf16_close(got[2], want[2], f"call {call}: grad_attn")
 
-    # Both agree with the oracle too (the bf16 contract).
+    # The no-alloc result agrees with the oracle too (the bf16 contract), on two of the images:
+    # all three gradients.
     v = value.float().cpu().numpy()
     ref = O.ms_deform_attn_backward(v[: 2 * H], SHAPES, loc[:2].cpu().numpy(), attn[:2].float().cpu().numpy(),
                                     grad[:2].float().cpu().numpy())
     assert_bf16_close(got[0][: 2 * H], ref[0], "oracle: grad_value")
+    assert_bf16_close(got[1][:2], ref[1], "oracle: grad_loc")
+    assert_bf16_close(got[2][:2], ref[2], "oracle: grad_attn")
 
 
 @pytest.mark.parametrize("weights_dtype", [torch.bfloat16, torch.float32])
@@ -111,13 +116,67 @@ def test_noalloc_uses_its_static_scratch(pkg, weights_dtype):
         assert_bf16_close(got[0], want[0], f"call {call}: grad_value")
         assert_bf16_close(got[1], want[1], f"call {call}: grad_loc")
         assert_bf16_close(got[2], want[2], f"call {call}: grad_attn")
+    # And the oracle, on the same bf16-rounded inputs: all three gradients.
+    f64 = lambda t: t.double().cpu().numpy()  # noqa: E731
+    ref = O.ms_deform_attn_backward(f64(v), shapes, f64(l), f64(a), f64(g))
+    for name, x, r in zip(("grad_value", "grad_loc", "grad_attn"), got, ref, strict=True):
+        assert_bf16_close(x, r, f"oracle: {name}")
+
+
+def _oversize(dev, b, h, shapes, p, d, lq):
+    value, loc, attn, grad = sampler_inputs(29, b, lq, h, shapes, p, d, lo=-0.1, hi=1.1)
+    t = lambda x, dt: torch.tensor(x, device=dev).to(dt)  # noqa: E731
+    return t(value, torch.bfloat16), t(loc, torch.float32), t(attn, torch.bfloat16), t(grad, torch.bfloat16)
 
 
 def test_noalloc_refuses_problems_beyond_its_scratch(pkg):
+    """A shape that only the accumulate-in-scratch kernel serves, with more than 2,097,152 value
+    elements (256 images x 8 heads x 160 positions x 8 channels): refused with
+    RFDETR_ERR_CAPACITY, before any launch; the outputs stay untouched."""
     N = pkg._native
     lib = N.lib()
-    # 64 images x 16 heads x 576 positions x 16 channels = 9.4M floats > 2,097,152.
-    status = lib.rfdetr_msda_backward_noalloc(None, None, N.BF16, N.int64_array([24, 24]), None, None, None,
-                                              N.BF16, None, N.BF16, None, None, None, 64, 16, 16, 3900, 1, 2)
+    dev = torch.device("cuda:0")
+    b, h, d, p, lq = 256, 8, 8, 3, 2
+    shapes = ((8, 16), (4, 8))
+    v, l, a, g = _oversize(dev, b, h, shapes, p, d, lq)
+    gv = torch.full_like(v, 7.0)
+    gl, ga = torch.empty_like(l), torch.empty_like(a)
+    status = lib.rfdetr_msda_backward_noalloc(torch.cuda.current_stream(dev).cuda_stream, v.data_ptr(), N.BF16,
+                                              N.int64_array([8, 16, 4, 8]), None, l.data_ptr(), a.data_ptr(), N.BF16,
+                                              g.data_ptr(), N.BF16, gv.data_ptr(), gl.data_ptr(), ga.data_ptr(), b, h,
+                                              d, lq, 2, p)
     assert status == N.ERR_CAPACITY
     assert "static scratch" in N.status_text(status)
+    torch.cuda.synchronize()
+    assert bool((gv == 7.0).all())
+
+
+def test_noalloc_serves_large_scratch_free_shapes(pkg):
+    """The Nano decoder layout at 64 images (9.4M value elements, beyond the array) is served by
+    the scratch-free owner kernel, so the no-alloc entry point takes it and matches the regular
+    entry point."""
+    N = pkg._native
+    lib = N.lib()
+    dev = torch.device("cuda:0")
+    b, lq = 64, 300
+    v, l, a, g = _oversize(dev, b, H, SHAPES, P, D, lq)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    shapes = N.int64_array([24, 24])
+    out = []
+    for noalloc in (False, True):
+        gv, gl, ga = torch.empty_like(v), torch.empty_like(l), torch.empty_like(a)
+        if noalloc:
+            st = lib.rfdetr_msda_backward_noalloc(stream, v.data_ptr(), N.BF16, shapes, None, l.data_ptr(),
+                                                  a.data_ptr(), N.BF16, g.data_ptr(), N.BF16, gv.data_ptr(),
+                                                  gl.data_ptr(), ga.data_ptr(), b, H, D, lq, 1, P)
+        else:
+            ws_bytes = lib.rfdetr_msda_backward_workspace_size(N.BF16, b, H, D, 576)
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+            st = lib.rfdetr_msda_backward(stream, v.data_ptr(), N.BF16, shapes, None, l.data_ptr(), a.data_ptr(),
+                                          N.BF16, g.data_ptr(), N.BF16, gv.data_ptr(), gl.data_ptr(), ga.data_ptr(),
+                                          ws.data_ptr(), ws_bytes, b, H, D, lq, 1, P)
+        N.check(st, "noalloc" if noalloc else "backward")
+        torch.cuda.synchronize()
+        out.append([x.float().cpu().numpy() for x in (gv, gl, ga)])
+    for name, x, y in zip(("grad_value", "grad_loc", "grad_attn"), out[1], out[0], strict=True):
+        np.testing.assert_array_equal(x, y, err_msg=name)
