@@ -106,3 +106,28 @@ def test_tuning_knobs(pkg):
         N.set_tuning("RFDETR_MSDA_OWN", "1,x")
     with pytest.raises(ValueError):
         N.set_tuning("RFDETR_MSDA_OWN", "1,2,3,4,5,6")
+
+
+def test_ffi_sources_cover_every_entry_point():
+    """The XLA FFI handlers (``rf-detr-jax_b200/ffi/rfdetr_ffi.cc``, not compiled here: JAX is
+    absent) call every compute entry point the header declares, and the JAX module registers
+    exactly the handlers the C++ file defines."""
+    import ast
+
+    ffi_dir = os.path.join(ROOT, "rf-detr-jax_b200", "ffi")
+    cc = open(os.path.join(ffi_dir, "rfdetr_ffi.cc")).read()
+    helpers = {"rfdetr_status_string", "rfdetr_abi_version", "rfdetr_set_tuning", "rfdetr_take_device_fault",
+               "rfdetr_selftest_bounded_wait", "rfdetr_msda_backward_workspace_size"}
+    for name in _declared():
+        if name not in helpers:
+            assert re.search(rf"\b{name}\(", cc), f"{name} has no FFI handler"
+    defined = set(re.findall(r"XLA_FFI_DEFINE_HANDLER_SYMBOL\((\w+),", cc))
+    py = open(os.path.join(ffi_dir, "cuda_backend.py")).read()
+    tree = ast.parse(py)
+    handlers = None
+    for node in ast.walk(tree):
+        if isinstance(node, ast.Assign) and any(getattr(t, "id", None) == "HANDLERS" for t in node.targets):
+            handlers = set(ast.literal_eval(node.value))
+    assert handlers == defined
+    called = set(re.findall(r'ffi_call\("(\w+)"', py))
+    assert called <= defined and called >= defined - {"RfdetrMsdaBwdNoAlloc"}
