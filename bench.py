@@ -52,6 +52,23 @@ UNIT = "queries/s"
 L2_BYTES = 126 * 1024 * 1024
 
 
+def ring_size():
+    """Input/output sets the device-timed steps cycle through: together more than L2 (3x)."""
+    fwd_bytes, bwd_bytes = algorithmic_bytes()
+    return max(4, int(np.ceil(3 * L2_BYTES / (2 * (fwd_bytes + bwd_bytes)))))
+
+
+def workload_config(world):
+    """The ``config`` object of the JSON line -- identical for both arms."""
+    fwd_bytes, bwd_bytes = algorithmic_bytes()
+    ring = ring_size()
+    return {"workload": "config2 sampler fwd+bwd (Nano decoder cross-attn, train shape)",
+            "batch_per_gpu": B, "len_query": LQ, "heads": H, "head_dim": D,
+            "levels": [list(sh) for sh in SHAPES], "points": P, "parallelism": f"dp{world} (independent shards)",
+            "l2": f"device arm: ring of {ring} input/output sets ({ring * 2 * (fwd_bytes + bwd_bytes) / 2**20:.0f} "
+                  "MiB) > L2, no flush"}
+
+
 def algorithmic_bytes():
     """Unique bytes read once + written once per launch (value/w/out/grads bf16, loc fp32)."""
     value = B * H * LV * D * 2
@@ -451,15 +468,222 @@ def run_config3(torch, device, N, lib, peak):
     return out_line
 
 
+# Nano's parameter count (fp32 gradients all-reduced per step): an analytic count over the Nano
+# geometry of the reference (variants.py:47-61) -- DINOv2-small windowed backbone at patch 16 with
+# a 24x24 position table ~21.8M, P4 projector ~1.5M, two decoder layers (self-attention, MSDA
+# cross-attention with 16 heads x 2 points, FFN 2048) ~2.9M, 3900 query features ~1.0M, thirteen
+# two-stage encoder heads ~2.9M, box/class heads and the reference-point MLP ~0.4M -- ~30.5M, the
+# figure published for RF-DETR Nano.
+NANO_PARAMS = 30_500_000
+AR_BUCKETS = 4
+
+
+def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
+    """Config 5 stand-in: the decoder side of the Nano training step on this GPU's batch of 8
+    images, built from this repository's kernels, with the data-parallel gradient all-reduce.
+
+    Per rank and step: the two-stage selection (top-300 of 13 groups x 8 images x 576 proposals x
+    91 classes, transformer.py:694-702) and its row gather (layers.py:225-244); for each of the
+    two decoder layers the MSDA prologue (ops.py:381-404) and sampler (ops.py:208-292); the
+    stacked cost and exact assignment of three output layers (criterion.py:402-413, exact
+    matching inside the sharded step -- which the reference cannot do, run.py:479-480); the set
+    losses with their gradients (criterion.py:157-250); then the backward of both layers (sampler
+    backward, prologue backward kernel and its two GEMMs).  The gradient all-reduce of
+    trainer.py:469 (``psum`` over the batch axis) is an NCCL all-reduce of a Nano-sized fp32
+    gradient buffer in AR_BUCKETS buckets on its own stream: the first after the last layer's
+    backward, the second after the first layer's, the rest (the backbone's gradients, which this
+    stand-in does not compute) after the step's compute.  The dense layers (backbone, FFN,
+    self-attention, value and output projections) are not part of this backend and not run.
+
+    Returns ms per step (max over ranks) for the full step, the compute alone and the
+    all-reduce alone, and images/s for the whole job."""
+    import torch.nn.functional as F  # noqa: F401
+
+    rank = ranks.rank
+    g = torch.Generator(device=device).manual_seed(500 + rank)
+    G, C, POS, K, T, NL = C4_G, C4_C, C4_POS, C4_K, C4_T, C4_LAYERS
+    CH = 256
+    hlp = H * 1 * P
+    st_of = lambda: torch.cuda.current_stream(device).cuda_stream  # noqa: E731
+    enc_logits = torch.randn(G * B, POS, C, generator=g, device=device)
+    enc_feat = torch.randn(G * B, POS, CH, generator=g, device=device).to(torch.bfloat16)
+    scores = torch.empty((G * B, POS), device=device)
+    tvals = torch.empty((G * B, K), device=device)
+    tidx = torch.empty((G * B, K), dtype=torch.int32, device=device)
+    sel = torch.empty((G * B, K, CH), dtype=torch.bfloat16, device=device)
+    sel_status = torch.zeros((1,), dtype=torch.int32, device=device)
+    layers = []
+    for _ in range(2):
+        layers.append({
+            "query": torch.randn(B, LQ, CH, generator=g, device=device).to(torch.bfloat16),
+            "ref": torch.cat([torch.rand(B, LQ, 1, 2, generator=g, device=device),
+                              torch.rand(B, LQ, 1, 2, generator=g, device=device) * 0.4 + 0.02], -1).contiguous(),
+            "weight": (torch.randn(3 * hlp, CH, generator=g, device=device) * 0.05).to(torch.bfloat16),
+            "bias": torch.randn(3 * hlp, generator=g, device=device) * 0.1,
+            "value": torch.randn(B * H, LV, D, generator=g, device=device).to(torch.bfloat16),
+            "loc": torch.empty((B, LQ, H, 1, P, 2), device=device),
+            "attn": torch.empty((B, LQ, H, P), dtype=torch.bfloat16, device=device),
+            "out": torch.empty((B, LQ, H * D), dtype=torch.bfloat16, device=device),
+            "g_out": torch.randn(B, LQ, H * D, generator=g, device=device).to(torch.bfloat16),
+            "g_value": torch.empty((B * H, LV, D), dtype=torch.bfloat16, device=device),
+            "g_loc": torch.empty((B, LQ, H, 1, P, 2), device=device),
+            "g_attn": torch.empty((B, LQ, H, P), dtype=torch.bfloat16, device=device),
+            "g_y": torch.empty((B * LQ, 3 * hlp), device=device),
+            "g_ref": torch.empty((B, LQ, 1, 4), device=device),
+        })
+    rng = np.random.default_rng(600 + rank)
+    sizes_np = rng.integers(1, T + 1, B).astype(np.int32)
+    mask_np = np.arange(T)[None, :] < sizes_np[:, None]
+    labels = torch.tensor(np.where(mask_np, rng.integers(0, C, (B, T)), 0).astype(np.int32), device=device)
+    tb = np.concatenate([rng.uniform(0.05, 0.95, (B, T, 2)), rng.uniform(0.02, 0.5, (B, T, 2))], -1)
+    tboxes = torch.tensor(np.where(mask_np[..., None], tb, 0.0).astype(np.float32), device=device)
+    tmask = torch.tensor(mask_np.astype(np.uint8), device=device)
+    sizes = torch.tensor(sizes_np, device=device)
+    dec_logits = torch.randn(NL, B, LQ, C, generator=g, device=device)
+    dec_boxes = torch.cat([torch.rand(NL, B, LQ, 2, generator=g, device=device) * 0.9 + 0.05,
+                           torch.rand(NL, B, LQ, 2, generator=g, device=device) * 0.48 + 0.02], -1).contiguous()
+    slots = G * T
+    cost = torch.empty((NL, B, LQ, T), device=device)
+    m_rows = torch.empty((NL, B, slots), dtype=torch.int32, device=device)
+    m_cols = torch.empty_like(m_rows)
+    m_valid = torch.empty((NL, B, slots), dtype=torch.uint8, device=device)
+    m_status = torch.zeros((1,), dtype=torch.int32, device=device)
+    num_boxes = torch.tensor([float(G * sizes_np.sum())], device=device)
+    losses = torch.empty((NL, 3), device=device)
+    g_logits = torch.empty_like(dec_logits)
+    g_l1 = torch.empty_like(dec_boxes)
+    g_giou = torch.empty_like(dec_boxes)
+    shapes = N.int64_array([24, 24])
+    grads = torch.randn(NANO_PARAMS, generator=g, device=device)
+    buckets = list(torch.chunk(grads, AR_BUCKETS))
+
+    def forward_and_losses():
+        st = st_of()
+        N.check(lib.rfdetr_topk_select(st, enc_logits.data_ptr(), G * B, POS, C, K, scores.data_ptr(),
+                                       tvals.data_ptr(), tidx.data_ptr()), "topk")
+        N.check(lib.rfdetr_select_rows(st, enc_feat.data_ptr(), 2, G * B, POS, CH, tidx.data_ptr(), K,
+                                       sel.data_ptr(), sel_status.data_ptr()), "select_rows")
+        for ly in layers:
+            N.check(lib.rfdetr_msda_prologue(st, ly["query"].data_ptr(), N.BF16, ly["weight"].data_ptr(),
+                                             ly["bias"].data_ptr(), ly["ref"].data_ptr(), 4, shapes,
+                                             ly["loc"].data_ptr(), ly["attn"].data_ptr(), B, LQ, CH, H, 1, P),
+                    "prologue")
+            N.check(lib.rfdetr_msda_forward(st, ly["value"].data_ptr(), N.BF16, shapes, None, ly["loc"].data_ptr(),
+                                            ly["attn"].data_ptr(), N.BF16, ly["out"].data_ptr(), N.BF16, B, H, D,
+                                            LQ, 1, P), "sampler forward")
+        N.check(lib.rfdetr_match_stacked(st, dec_logits.data_ptr(), N.F32, dec_boxes.data_ptr(), N.F32,
+                                         labels.data_ptr(), tboxes.data_ptr(), tmask.data_ptr(), sizes.data_ptr(),
+                                         NL, B, LQ, C, T, G, 2.0, 5.0, 2.0, 0.25, cost.data_ptr(),
+                                         m_rows.data_ptr(), m_cols.data_ptr(), m_valid.data_ptr(),
+                                         m_status.data_ptr()), "match")
+        N.check(lib.rfdetr_set_losses(st, dec_logits.data_ptr(), dec_boxes.data_ptr(), labels.data_ptr(),
+                                      tboxes.data_ptr(), m_rows.data_ptr(), m_cols.data_ptr(), m_valid.data_ptr(),
+                                      num_boxes.data_ptr(), NL, B, LQ, C, T, slots, 0.25, 1, losses.data_ptr(),
+                                      g_logits.data_ptr(), g_l1.data_ptr(), g_giou.data_ptr()), "losses")
+
+    def backward_layer(ly):
+        st = st_of()
+        w = ly["weight"].float()
+        # The box form's size gradient needs the forward's biased offsets (one GEMM, as the host
+        # API's backward recomputes them).
+        ly["offsets"] = torch.addmm(ly["bias"][:2 * hlp], ly["query"].reshape(-1, CH).float(), w[:2 * hlp].t())
+        N.check(lib.rfdetr_msda_backward(st, ly["value"].data_ptr(), N.BF16, shapes, None, ly["loc"].data_ptr(),
+                                         ly["attn"].data_ptr(), N.BF16, ly["g_out"].data_ptr(), N.BF16,
+                                         ly["g_value"].data_ptr(), ly["g_loc"].data_ptr(), ly["g_attn"].data_ptr(),
+                                         None, 0, B, H, D, LQ, 1, P), "sampler backward")
+        N.check(lib.rfdetr_msda_prologue_backward(st, ly["g_loc"].data_ptr(), ly["g_attn"].data_ptr(),
+                                                  ly["attn"].data_ptr(), N.BF16, ly["ref"].data_ptr(), 4,
+                                                  ly["offsets"].data_ptr(), shapes, ly["g_y"].data_ptr(),
+                                                  ly["g_ref"].data_ptr(), B, LQ, H, 1, P), "prologue backward")
+        ly["g_query"] = torch.matmul(ly["g_y"], w)
+        ly["g_weight"] = torch.matmul(ly["g_y"].t(), ly["query"].reshape(-1, CH).float())
+
+    comp = torch.cuda.Stream(device)
+    comm = torch.cuda.Stream(device)
+    with torch.cuda.stream(comp):
+        for _ in range(2):
+            forward_and_losses()
+            backward_layer(layers[1])
+            backward_layer(layers[0])
+    comp.synchronize()
+    graph_a, graph_b = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_a, stream=comp, capture_error_mode="relaxed"):
+        forward_and_losses()
+        backward_layer(layers[1])
+    with torch.cuda.graph(graph_b, stream=comp, capture_error_mode="relaxed"):
+        backward_layer(layers[0])
+    torch.cuda.synchronize()
+    ev_a, ev_b = torch.cuda.Event(), torch.cuda.Event()
+    multi = ranks.world > 1
+
+    def all_reduce(bucket):
+        dist.all_reduce(bucket)
+
+    def step(compute=True, reduce=True):
+        with torch.cuda.stream(comp):
+            if compute:
+                graph_a.replay()
+            ev_a.record(comp)
+        if reduce and multi:
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev_a)
+                all_reduce(buckets[0])
+        with torch.cuda.stream(comp):
+            if compute:
+                graph_b.replay()
+            ev_b.record(comp)
+        if reduce and multi:
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev_b)
+                for bk in buckets[1:]:
+                    all_reduce(bk)
+        comp.wait_stream(comm)
+
+    def timed(compute, reduce):
+        for _ in range(warmup):
+            step(compute, reduce)
+        torch.cuda.synchronize()
+        ranks.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(comp)
+        for _ in range(steps):
+            step(compute, reduce)
+        e1.record(comp)
+        e1.synchronize()
+        torch.cuda.synchronize()
+        ranks.barrier()
+        return ranks.max_float(e0.elapsed_time(e1)) / steps
+
+    ms_step = timed(True, True)
+    ms_compute = timed(True, False)
+    ms_reduce = timed(False, True) if multi else 0.0
+    N.check(int(m_status.item()), "decoder step: assignment status")
+    del graph_a, graph_b
+    world = ranks.world
+    return {
+        "workload": "config5 stand-in: decoder-side hot path of the Nano train step per GPU (8 images) + NCCL "
+                    f"all-reduce of {NANO_PARAMS / 1e6:.1f}M fp32 gradients in {AR_BUCKETS} buckets",
+        "images_per_s": B * world / (ms_step * 1e-3),
+        "ms_per_step": ms_step,
+        "ms_compute_only": ms_compute,
+        "ms_allreduce_only": ms_reduce,
+        "ms_allreduce_exposed": max(ms_step - ms_compute, 0.0),
+        "allreduce_bytes": NANO_PARAMS * 4 if multi else 0,
+        "allreduce_busbw_GBps": (2 * (world - 1) / world * NANO_PARAMS * 4 / (ms_reduce * 1e-3) / 1e9)
+        if multi and ms_reduce > 0 else None,
+        "steps": steps,
+        "limiter": ("all-reduce" if multi and ms_step - ms_compute > 0.5 * ms_compute else "kernels"),
+        "not_run": "backbone, projector, FFN, self-attention, value/output projections (dense layers outside "
+                   "this backend)",
+    }
+
+
 def cpu_baseline_sample(steps_budget_s=20.0):
     """The oracle (float32) forward + backward on one image of the workload, single thread."""
     from oracle import msda as O
 
-    rng = np.random.default_rng(1)
-    value = rng.standard_normal((H, LV, D)).astype(np.float32)
-    loc = rng.uniform(-0.05, 1.05, (LQ, H, 1, P, 2)).astype(np.float32)
-    attn = np.full((LQ, H, P), 1.0 / P, np.float32)
-    grad = rng.standard_normal((LQ, H * D)).astype(np.float32)
+    value, loc, attn, grad = _reference_inputs(1, 0, 0, LQ)
     reps, t0 = 0, time.perf_counter()
     while True:
         O.forward_image(value, SHAPES, loc, attn, np.float32)
@@ -472,46 +696,65 @@ def cpu_baseline_sample(steps_budget_s=20.0):
             "sample": f"oracle/msda.py float32 fwd+bwd on 1 of {B} images ({LQ} queries), {reps} reps"}
 
 
-def _reference_image(args):
-    seed, b = args
-    from oracle import msda as O
-
+def _reference_inputs(seed, b, q0, q1):
+    """Config 2's inputs for queries [q0, q1) of image b: value N(0,1), locations U(-0.05, 1.05),
+    weights softmax of N(0,1) logits, cotangent N(0,1)."""
     rng = np.random.default_rng(seed * 100 + b)
     value = rng.standard_normal((H, LV, D)).astype(np.float32)
-    loc = rng.uniform(-0.05, 1.05, (LQ, H, 1, P, 2)).astype(np.float32)
-    attn = np.full((LQ, H, P), 1.0 / P, np.float32)
-    grad = rng.standard_normal((LQ, H * D)).astype(np.float32)
+    rng = np.random.default_rng((seed * 100 + b) * 1000 + q0)
+    n = q1 - q0
+    loc = rng.uniform(-0.05, 1.05, (n, H, 1, P, 2)).astype(np.float32)
+    logits = rng.standard_normal((n, H, P))
+    attn = np.exp(logits - logits.max(-1, keepdims=True))
+    attn = (attn / attn.sum(-1, keepdims=True)).astype(np.float32)
+    grad = rng.standard_normal((n, H * D)).astype(np.float32)
+    return value, loc, attn, grad
+
+
+def _reference_task(args):
+    """Forward + backward of one image's query chunk (grad_value is that chunk's partial sum)."""
+    seed, b, q0, q1 = args
+    from oracle import msda as O
+
+    value, loc, attn, grad = _reference_inputs(seed, b, q0, q1)
     O.forward_image(value, SHAPES, loc, attn, np.float32)
     O.backward_image(value, SHAPES, loc, attn, grad, np.float32)
     return b
 
 
+def _reference_tasks(seed, cores):
+    chunks = max(1, -(-cores // B))
+    bounds = np.linspace(0, LQ, chunks + 1).astype(int)
+    return [(seed, b, int(bounds[c]), int(bounds[c + 1])) for b in range(B) for c in range(chunks)]
+
+
 def run_reference(args):
-    """CPU reference arm: the oracle port over all host cores (process pool over images)."""
+    """CPU reference arm: the oracle port over all host cores (a process pool over (image, query
+    chunk) tasks, so every core has work)."""
     import multiprocessing as mp
 
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cores = max(1, min(os.cpu_count() or 1, B))
+    cores = max(1, os.cpu_count() or 1)
     ctx = mp.get_context("spawn")
     with ctx.Pool(cores) as pool:
         for s in range(args.warmup):
-            pool.map(_reference_image, [(s, b) for b in range(B)])
+            pool.map(_reference_task, _reference_tasks(s, cores))
         t0 = time.perf_counter()
         for s in range(args.steps):
-            pool.map(_reference_image, [(1000 + s, b) for b in range(B)])
+            pool.map(_reference_task, _reference_tasks(1000 + s, cores))
         dt = (time.perf_counter() - t0) / max(args.steps, 1)
     value = B * LQ / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2 sampler fwd+bwd", "batch": B, "len_query": LQ, "heads": H, "head_dim": D,
-                   "levels": [list(s) for s in SHAPES], "points": P},
+        "config": workload_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"full workload ({B} images x {LQ} queries) per step, float32 NumPy restatement "
-                                   "of the reference sampler (JAX not installable: XLA-CPU path unavailable)"},
+                         "sample": f"full workload ({B} images x {LQ} queries) per step as {len(_reference_tasks(0, cores))} "
+                                   "(image, query chunk) tasks, float32 NumPy restatement of the reference sampler "
+                                   "(JAX absent here and on the GPU hosts: the XLA-CPU path cannot run)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -538,6 +781,17 @@ class Ranks:
         t = torch.tensor([float(x)], device=self.device, dtype=torch.float64)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
+
+    def gather_floats(self, values):
+        """Every rank's list of floats, in rank order (one all-gather)."""
+        if self.world == 1:
+            return [list(map(float, values))]
+        import torch
+
+        t = torch.tensor([float(v) for v in values], device=self.device, dtype=torch.float64)
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        self.dist.all_gather(out, t)
+        return [[float(v) for v in x.tolist()] for x in out]
 
     def max_int(self, n):
         if self.world == 1:
@@ -586,8 +840,7 @@ def run_ours(args):
     lib = N.lib()
     stream = torch.cuda.Stream(device)
     fwd_bytes, bwd_bytes = algorithmic_bytes()
-    per_set = 2 * (fwd_bytes + bwd_bytes)
-    ring = max(4, int(np.ceil(3 * L2_BYTES / per_set)))
+    ring = ring_size()
     sets = []
     for r in range(ring):
         value, loc, attn, grad = make_inputs(shard_seed(rank, r), torch, device)
@@ -759,6 +1012,30 @@ def run_ours(args):
         e2e_trials.append(ranks.max_float(e_start.elapsed_time(e_end)) / e2e_steps)
     e2e_ms = sorted(e2e_trials)[1]
 
+    # Per-rank copy bandwidth, each direction alone (one step's transfer, CUDA events on its
+    # stream, median of 5): what the end-to-end pipeline is limited by when ranks share the host.
+    def copy_gbps(fn, nbytes, s):
+        samples = []
+        for _ in range(6):
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(s)
+            with torch.cuda.stream(s):
+                fn()
+            c1.record(s)
+            c1.synchronize()
+            samples.append(nbytes / (c0.elapsed_time(c1) * 1e-3) / 1e9)
+        return statistics.median(samples[1:])
+
+    torch.cuda.synchronize()
+    barrier()
+    h2d_gbps = copy_gbps(lambda: dev_slots[0][0].copy_(host_buf, non_blocking=True), h2d, s_h2d)
+    barrier()
+    d2h_gbps = copy_gbps(lambda: h_res[0][0].copy_(d_res[0][0], non_blocking=True), d2h, s_d2h)
+    barrier()
+    copy_bw = ranks.gather_floats([h2d_gbps, d2h_gbps])
+
+    decoder = run_decoder_step(torch, dist, device, ranks, N, lib, max(10, min(args.steps, 30)), args.warmup)
+
     cpu = cpu_baseline_sample() if (rank == 0 and world == 1) else None
     peaks_path_ = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak_ = float(json.load(open(peaks_path_))["hbm_gbs"]) if os.path.exists(peaks_path_) else 6650.0
@@ -781,12 +1058,9 @@ def run_ours(args):
         "metric": METRIC, "value": whole_job_value(B * LQ, world, ms_step), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config2 sampler fwd+bwd (Nano decoder cross-attn, train shape)",
-                   "batch_per_gpu": B, "len_query": LQ, "heads": H, "head_dim": D,
-                   "levels": [list(s) for s in SHAPES], "points": P, "parallelism": f"dp{world} (independent shards)",
-                   "l2": f"ring of {ring} input/output sets ({ring * per_set / 2**20:.0f} MiB) > L2, no flush",
-                   "timing": f"median of {reps_step} timed regions of exactly {args.steps} steps, "
-                             "one CUDA-graph replay per step"},
+        "config": workload_config(world),
+        "timing": f"median of {reps_step} timed regions of exactly {args.steps} steps, one CUDA-graph replay "
+                  "per step",
         "roofline": {"bound": "hbm", "kernel": "msda_backward_owner_kernel", "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "peak_source": peak_src, "algorithmic_bytes": bwd_bytes, "ms_per_launch": ms_bwd},
@@ -796,7 +1070,12 @@ def run_ours(args):
         "e2e": {"value": whole_job_value(B * LQ, world, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "trials_ms_per_step": e2e_trials,
                 "statistic": f"median of 3 trials of {e2e_steps} steps",
-                "pipeline": "copy-in / compute / copy-out on three streams, consecutive steps overlapped"},
+                "pipeline": "copy-in / compute / copy-out on three streams, consecutive steps overlapped",
+                "copy_GBps_per_rank": {"h2d": [round(x[0], 2) for x in copy_bw],
+                                       "d2h": [round(x[1], 2) for x in copy_bw],
+                                       "how": "one step's transfer alone per direction, pinned host buffer, "
+                                              "CUDA events, median of 5, all ranks at once"}},
+        "decoder_step": decoder,
         "gpu_launches": 2 * args.steps,
         "clocks": clock_summary,
     }

@@ -30,11 +30,12 @@ def _rank_main(rank, world, port, out):
         # Each rank times a different step; the job's step time is the slowest rank's.
         step_ms = ranks.max_float(0.05 + 0.01 * rank)
         reps = ranks.max_int(3 + rank)
+        per_rank = ranks.gather_floats([10.0 + rank, 20.0 + rank])
         seeds = [bench.shard_seed(rank, r) for r in range(4)]
         gathered = [None] * world
         dist.all_gather_object(gathered, seeds)
         ranks.barrier()
-        out[rank] = (step_ms, reps, gathered)
+        out[rank] = (step_ms, reps, gathered, per_rank)
     finally:
         dist.destroy_process_group()
 
@@ -45,9 +46,10 @@ def test_two_gloo_ranks():
     out = manager.dict()
     mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world, start_method="spawn", join=True)
     for rank in range(world):
-        step_ms, reps, seeds = out[rank]
+        step_ms, reps, seeds, per_rank = out[rank]
         assert step_ms == pytest.approx(0.06)   # max over ranks, identical on every rank
         assert reps == 4
+        assert per_rank == [[10.0, 20.0], [11.0, 21.0]]  # every rank's figures, in rank order
         assert not set(seeds[0]) & set(seeds[1])  # disjoint input sets per rank
 
 
@@ -62,3 +64,4 @@ def test_single_rank_needs_no_process_group():
     ranks = bench.Ranks(1, 0, torch.device("cpu"))
     ranks.barrier()
     assert ranks.max_float(1.5) == 1.5 and ranks.max_int(7) == 7
+    assert ranks.gather_floats([2, 3]) == [[2.0, 3.0]]
