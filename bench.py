@@ -437,7 +437,7 @@ def run_config3(torch, device, N, lib, peak):
         grad = torch.tensor(rng.standard_normal((b3, lq3, h3 * d3)), dtype=dt, device=device)
         out = torch.empty((b3, lq3, h3 * d3), dtype=dt, device=device)
         gv, gl, ga = torch.empty_like(value), torch.empty_like(loc), torch.empty_like(attn)
-        wsb = lib.rfdetr_msda_backward_workspace_size(code, b3, h3, d3, lv3)
+        wsb = lib.rfdetr_msda_backward_workspace_bytes(code, code, sh, b3, h3, d3, lq3, l3, p3)
         ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=device)
 
         def fwd():

@@ -104,9 +104,18 @@ int rfdetr_msda_forward(void *stream,
                         int64_t batch, int64_t n_heads, int64_t head_dim, int64_t len_query,
                         int64_t n_levels, int64_t n_points);
 
-/* Workspace bytes rfdetr_msda_backward needs (0 when value_dtype is f32). */
+/* Workspace bytes of rfdetr_msda_backward's float32-accumulator path (0 when value_dtype is f32).
+ * A workspace of this size always suffices; rfdetr_msda_backward_workspace_bytes() gives the
+ * size that also enables the position-tile kernels. */
 size_t rfdetr_msda_backward_workspace_size(int value_dtype, int64_t batch, int64_t n_heads,
                                            int64_t head_dim, int64_t len_value);
+
+/* Workspace bytes with which rfdetr_msda_backward can take every kernel it has for this geometry,
+ * the position-tile kernels of multi-level shapes included (their per-corner dot products and
+ * per-slab flags live there): the maximum over its paths.  0 for invalid arguments. */
+size_t rfdetr_msda_backward_workspace_bytes(int value_dtype, int weight_dtype, const int64_t *spatial_shapes,
+                                            int64_t batch, int64_t n_heads, int64_t head_dim,
+                                            int64_t len_query, int64_t n_levels, int64_t n_points);
 
 /*
  * Backward of rfdetr_msda_forward against grad_output ([B, Lq, H*D], the output's dtype):

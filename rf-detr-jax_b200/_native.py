@@ -47,6 +47,8 @@ SIGNATURES = {
     "rfdetr_msda_forward": (_int, [_vp, _vp, _int, _c_int64_p, _c_int64_p, _vp, _vp, _int, _vp, _int,
                                    _i64, _i64, _i64, _i64, _i64, _i64]),
     "rfdetr_msda_backward_workspace_size": (ctypes.c_size_t, [_int, _i64, _i64, _i64, _i64]),
+    "rfdetr_msda_backward_workspace_bytes": (ctypes.c_size_t, [_int, _int, _c_int64_p, _i64, _i64, _i64, _i64, _i64,
+                                                               _i64]),
     "rfdetr_msda_backward": (_int, [_vp, _vp, _int, _c_int64_p, _c_int64_p, _vp, _vp, _int, _vp, _int,
                                     _vp, _vp, _vp, _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64, _i64, _i64]),
     "rfdetr_msda_backward_noalloc": (_int, [_vp, _vp, _int, _c_int64_p, _c_int64_p, _vp, _vp, _int, _vp, _int,

@@ -21,6 +21,8 @@
 // produced in the same pass from team-reduced dot products.
 #include <algorithm>
 #include <initializer_list>
+#include <type_traits>
+#include <cmath>
 #include <cstdio>
 #include <mutex>
 #include <cstdlib>
@@ -2033,6 +2035,588 @@ int try_backward_owner(const Geom &g, const void *value, const float *loc, const
     return -1;
 }
 
+// ------------------------------------------------------------------------------------------
+// Position-tile backward: levels of any size, float32 or bf16 values, no float atomics.
+//
+// K1 (msda_backward_tile_kernel) runs one CTA per (slab, tile); a tile is a run of up to `np`
+// consecutive positions of one level.  Each thread owns one position and CPT channels of it:
+// the value row segment and its gradient accumulator (float32 for bf16 values, float64 for
+// float32 values) stay in registers for the whole launch.  The CTA walks the slab's queries in
+// chunks: it computes the taps of the chunk's samples on its level (a sample whose rows miss the
+// tile's row band is dropped after two FMAs), files each corner landing in the tile into its
+// position's bin in shared memory, and the owners drain their bins -- acc += coef * g[q] and the
+// corner's dot product G = <value row, g[q]> (reduced over the position's lanes), written to a
+// per-corner array in the workspace.  grad_value is written once, from the registers.  Levels
+// where a position collects several records per chunk stage the chunk's location, weight and
+// gradient rows in shared memory (double-buffered cp.async); sparse levels read them from L2.
+//
+// K2 (msda_backward_finish_kernel) is one thread per sample: from the four corners' G it forms
+// the weight gradient and the location gradient (d ix / d loc = W), as the reference's autodiff
+// does (deform_pallas.py:97-120 states the same formulas).
+//
+// The reference's non-finite semantics: an out-of-range corner contributes m * (v . g) = NaN to
+// the weight/location gradients when its clipped value row or the gradient row holds inf/NaN,
+// and scatters 0 * a * w * g (NaN where g is not finite, or where a is) into its clipped row.
+// K1 files such a corner with its (zero or NaN) coefficient when the gradient row or the
+// coefficient is non-finite, so the owner adds exactly that; and K1 raises a per-slab flag when
+// it sees a non-finite value or gradient row, under which K2 recomputes the out-of-range
+// corners' m * (v . g) from the rows themselves.
+// ------------------------------------------------------------------------------------------
+constexpr int kTileThreadsMax = 512;
+constexpr int kTilePoison = 0x8000;  // record flag: out-of-range corner filed for its NaN, no G
+
+struct TilePlan {
+    int segs;                         // threads per position (D / CPT)
+    int tq;                           // queries per chunk
+    int tiles_before[kMaxLevels + 1];  // first tile of each level (per slab)
+    int np[kMaxLevels];               // positions per tile, per level
+    int cap[kMaxLevels];              // bin slots per position, per level
+    int staged[kMaxLevels];           // the level's chunk rows are staged in shared memory
+    int gstride;                      // staged gradient row stride, bytes
+    int gl, ga;                       // cp.async granules of a query's location / weight segment
+    unsigned o_loc, loc_sz, o_attn, attn_sz, o_g, g_sz, o_gbad, o_cnt, o_bins;
+    size_t smem;
+    int nthr;
+};
+
+template <int N>
+__device__ __forceinline__ int select_level(const int (&a)[N], int l) {
+    int r = a[0];
+#pragma unroll
+    for (int i = 1; i < N; ++i)
+        if (i == l) r = a[i];
+    return r;
+}
+
+template <typename TV, typename TW, int P, int CPT>
+__global__ void __launch_bounds__(kTileThreadsMax)
+msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict__ loc, const TW *__restrict__ attn,
+                          const typename OutOf<TV, TW>::T *__restrict__ grad_out, TV *__restrict__ grad_value,
+                          typename AccOf<TV>::T *__restrict__ gcorner, int *__restrict__ flags, const Geom g,
+                          const TilePlan tp) {
+    using TG = typename OutOf<TV, TW>::T;
+    using AT = typename AccOf<TV>::T;
+    constexpr int PS = P == 1 ? 0 : P == 2 ? 1 : P == 4 ? 2 : 3;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int s_bad;
+    const int bh = blockIdx.y;
+    const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
+    const int tile = blockIdx.x;
+    int l = 0;
+    for (int i = 1; i < g.L; ++i)
+        if (select_level(tp.tiles_before, i) <= tile) l = i;
+    const int W = select_level(g.lw, l), Hh = select_level(g.lh, l), ls = select_level(g.ls, l);
+    const float Wf = (float)W, Hf = (float)Hh;
+    const int npl = select_level(tp.np, l);
+    const int p0 = (tile - select_level(tp.tiles_before, l)) * npl;
+    const int np = min(npl, W * Hh - p0);
+    const int cap = select_level(tp.cap, l);
+    const bool staged = select_level(tp.staged, l) != 0;
+    const int row_lo = p0 / W, row_hi = (p0 + np - 1) / W;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int segs = tp.segs;
+    const int pl = tid / segs, seg = tid - (tid / segs) * segs;
+    const bool owner = pl < np;
+    const int LP = g.L * g.P;
+    const int D = g.D;
+    const size_t slab_rows = (size_t)bh * g.Lv;
+    const float qnan = __int_as_float(0x7fc00000);
+
+    int *const counts = reinterpret_cast<int *>(smem + tp.o_cnt);
+    float *const bcoef = reinterpret_cast<float *>(smem + tp.o_bins);
+    unsigned short *const bidx = reinterpret_cast<unsigned short *>(smem + tp.o_bins + (size_t)cap * npl * 4);
+    auto locb = [&](int i) { return reinterpret_cast<float2 *>(smem + tp.o_loc + i * tp.loc_sz); };
+    auto attnb = [&](int i) { return reinterpret_cast<TW *>(smem + tp.o_attn + i * tp.attn_sz); };
+    auto gb = [&](int i) { return smem + tp.o_g + (size_t)i * tp.g_sz; };
+    unsigned char *const gbad = smem + tp.o_gbad;
+
+    if (tid == 0) s_bad = 0;
+    for (int i = tid; i < npl; i += nthr) counts[i] = 0;
+
+    // Owner state.
+    constexpr int NV = CPT / 2;
+    float2 vv[NV];
+    AT acc[CPT];
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) acc[i] = (AT)0;
+    bool vbad = false;
+    {
+        const int pos = ls + p0 + (owner ? pl : 0);
+        const TV *vp = value + (slab_rows + pos) * D + seg * CPT;
+        if constexpr (sizeof(TV) == 2) {
+#pragma unroll
+            for (int k = 0; k < CPT / 8; ++k) {
+                const uint4 r = owner ? __ldg(reinterpret_cast<const uint4 *>(vp) + k) : make_uint4(0, 0, 0, 0);
+                vv[4 * k + 0] = bf16x2_lo_hi(r.x);
+                vv[4 * k + 1] = bf16x2_lo_hi(r.y);
+                vv[4 * k + 2] = bf16x2_lo_hi(r.z);
+                vv[4 * k + 3] = bf16x2_lo_hi(r.w);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < CPT / 4; ++k) {
+                const float4 r = owner ? __ldg(reinterpret_cast<const float4 *>(vp) + k) : make_float4(0, 0, 0, 0);
+                vv[2 * k] = make_float2(r.x, r.y);
+                vv[2 * k + 1] = make_float2(r.z, r.w);
+            }
+        }
+        vbad = any_nonfinite<NV>(vv);
+    }
+    __syncthreads();  // s_bad and counts initialised
+    if (vbad) s_bad = 1;
+
+    const int nchunks = (g.Lq + tp.tq - 1) / tp.tq;
+    auto issue = [&](int c) {
+        const int q0 = c * tp.tq, nq = min(tp.tq, g.Lq - q0);
+        const int buf = c & 1;
+        const int lbytes = P * 8, abytes = P * (int)sizeof(TW), gbytes = D * (int)sizeof(TG);
+        const int ls_ = 31 - __clz(lbytes / tp.gl), as_ = 31 - __clz(abytes / tp.ga);
+        const size_t row0 = ((size_t)b * g.Lq + q0) * g.H + h;
+        for (int i = tid; i < (nq << ls_); i += nthr) {
+            const int qi = i >> ls_, j = i & ((1 << ls_) - 1);
+            cp_async_bytes(reinterpret_cast<char *>(locb(buf)) + (size_t)qi * lbytes + j * tp.gl,
+                           reinterpret_cast<const char *>(loc + ((row0 + (size_t)qi * g.H) * LP + l * P) * 2) +
+                               j * tp.gl,
+                           tp.gl);
+        }
+        for (int i = tid; i < (nq << as_); i += nthr) {
+            const int qi = i >> as_, j = i & ((1 << as_) - 1);
+            cp_async_bytes(reinterpret_cast<char *>(attnb(buf)) + (size_t)qi * abytes + j * tp.ga,
+                           reinterpret_cast<const char *>(attn + (row0 + (size_t)qi * g.H) * LP + l * P) + j * tp.ga,
+                           tp.ga);
+        }
+        const int gch = gbytes / 16;
+        for (int i = tid; i < nq * gch; i += nthr) {
+            const int qi = i / gch, j = i - (i / gch) * gch;
+            cp_async_bytes(gb(buf) + (size_t)qi * tp.gstride + j * 16,
+                           reinterpret_cast<const char *>(grad_out + (row0 + (size_t)qi * g.H) * D) + j * 16, 16);
+        }
+    };
+    if (staged) issue(0);
+    cp_async_commit();
+
+    // A g row segment of CPT channels as float pairs: from shared memory or from L2.
+    auto load_g = [&](const unsigned char *row, float2 *q) {
+        if constexpr (sizeof(TG) == 2) {
+#pragma unroll
+            for (int k = 0; k < CPT / 8; ++k) {
+                const uint4 u = *reinterpret_cast<const uint4 *>(row + k * 16);
+                q[4 * k + 0] = bf16x2_lo_hi(u.x);
+                q[4 * k + 1] = bf16x2_lo_hi(u.y);
+                q[4 * k + 2] = bf16x2_lo_hi(u.z);
+                q[4 * k + 3] = bf16x2_lo_hi(u.w);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < CPT / 4; ++k) {
+                const float4 f = *reinterpret_cast<const float4 *>(row + k * 16);
+                q[2 * k] = make_float2(f.x, f.y);
+                q[2 * k + 1] = make_float2(f.z, f.w);
+            }
+        }
+    };
+    auto load_g_global = [&](const TG *row, float2 *q) {
+        if constexpr (sizeof(TG) == 2) {
+#pragma unroll
+            for (int k = 0; k < CPT / 8; ++k) {
+                const uint4 u = __ldg(reinterpret_cast<const uint4 *>(row) + k);
+                q[4 * k + 0] = bf16x2_lo_hi(u.x);
+                q[4 * k + 1] = bf16x2_lo_hi(u.y);
+                q[4 * k + 2] = bf16x2_lo_hi(u.z);
+                q[4 * k + 3] = bf16x2_lo_hi(u.w);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < CPT / 4; ++k) {
+                const float4 f = __ldg(reinterpret_cast<const float4 *>(row) + k);
+                q[2 * k] = make_float2(f.x, f.y);
+                q[2 * k + 1] = make_float2(f.z, f.w);
+            }
+        }
+    };
+    // True when the gradient row of (image b, query q, head h) holds inf/NaN (read from L2).
+    auto g_row_bad = [&](int q) {
+        const TG *row = grad_out + (((size_t)b * g.Lq + q) * g.H + h) * D;
+        bool bad = false;
+        for (int k = 0; k < D; k += CPT) {
+            float2 x[NV];
+            load_g_global(row + k, x);
+            bad |= any_nonfinite<NV>(x);
+        }
+        return bad;
+    };
+
+    // Files the corners of local sample s (query qi, point p) selected by `want` that land in the
+    // tile; returns those whose bin was full.  `first` also reports whether the sample has an
+    // out-of-range corner whose clipped position is in the tile.
+    auto file = [&](int c, int s, unsigned want) -> unsigned {
+        const int q0 = c * tp.tq;
+        const int qi = s >> PS, p = s & (P - 1);
+        float2 xy;
+        float a;
+        if (staged) {
+            xy = locb(c & 1)[s];
+            a = to_f32(attnb(c & 1)[s]);
+        } else {
+            const size_t srow = (((size_t)b * g.Lq + q0 + qi) * g.H + h) * LP + l * P + p;
+            xy = __ldg(reinterpret_cast<const float2 *>(loc) + srow);
+            a = to_f32(__ldg(attn + srow));
+        }
+        float ix, iy;
+        sample_coords(xy.x, xy.y, Wf, Hf, ix, iy);
+        if (!(fabsf(ix) <= 3.0e38f && fabsf(iy) <= 3.0e38f)) return 0u;
+        const Axis ay = axis_taps(iy, Hf, Hh);
+        if (ay.c1 < row_lo || ay.c0 > row_hi) return 0u;  // both rows outside the tile's band
+        const Axis ax = axis_taps(ix, Wf, W);
+        const float m[4] = {ax.m0 * ay.m0, ax.m1 * ay.m0, ax.m0 * ay.m1, ax.m1 * ay.m1};
+        const float ax0 = a * ax.w0, ax1 = a * ax.w1;
+        const float cf[4] = {ax0 * ay.w0 * m[0], ax1 * ay.w0 * m[1], ax0 * ay.w1 * m[2], ax1 * ay.w1 * m[3]};
+        const int pp[4] = {ay.c0 * W + ax.c0, ay.c0 * W + ax.c1, ay.c1 * W + ax.c0, ay.c1 * W + ax.c1};
+        int gb_state = -1;  // gradient row finiteness, looked up once if needed
+        unsigned failed = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (!((want >> k) & 1u)) continue;
+            const int pt = pp[k] - p0;
+            if ((unsigned)pt >= (unsigned)np) continue;
+            bool filed = m[k] != 0.f;
+            bool poison = false;
+            if (!filed) {
+                if (gb_state < 0) {
+                    gb_state = staged ? (int)gbad[qi] : (g_row_bad(q0 + qi) ? 1 : 0);
+                    if (gb_state) s_bad = 1;
+                }
+                filed = cf[k] != 0.f || gb_state != 0;
+                poison = true;
+            }
+            if (!filed) continue;
+            const int slot = atomicAdd(&counts[pt], 1);
+            if (slot < cap) {
+                bcoef[slot * npl + pt] = cf[k];
+                bidx[slot * npl + pt] = (unsigned short)(((s << 2) | k) | (poison ? kTilePoison : 0));
+            } else {
+                failed |= 1u << k;
+            }
+        }
+        return failed;
+    };
+
+    // Owners drain their bins (and reset their counts).
+    const unsigned group = segs >= 32 ? 0xffffffffu : (((1u << segs) - 1u) << (((tid & 31) / segs) * segs));
+    auto own = [&](int c) {
+        const int q0 = c * tp.tq;
+        int n = 0;
+        if (owner) n = min(counts[pl], cap);
+        __syncwarp();
+        if (owner && seg == 0) counts[pl] = 0;
+        for (int e = 0; e < n; ++e) {
+            const float cfe = bcoef[e * npl + pl];
+            const unsigned idx = bidx[e * npl + pl];
+            const int sl = (int)((idx & 0x7fffu) >> 2), k = (int)(idx & 3u);
+            const int qi = sl >> PS, p = sl & (P - 1);
+            float2 q[NV];
+            if (staged) {
+                load_g(gb(c & 1) + (size_t)qi * tp.gstride + seg * CPT * (int)sizeof(TG), q);
+            } else {
+                load_g_global(grad_out + (((size_t)b * g.Lq + q0 + qi) * g.H + h) * D + seg * CPT, q);
+            }
+            AT dot;
+            if constexpr (sizeof(TV) == 2) {
+                const float2 cc = make_float2(cfe, cfe);
+                float2 d = __fmul2_rn(vv[0], q[0]);
+#pragma unroll
+                for (int i = 1; i < NV; ++i) d = __ffma2_rn(vv[i], q[i], d);
+#pragma unroll
+                for (int i = 0; i < NV; ++i) {
+                    const float2 t = __ffma2_rn(cc, q[i], make_float2(acc[2 * i], acc[2 * i + 1]));
+                    acc[2 * i] = t.x;
+                    acc[2 * i + 1] = t.y;
+                }
+                dot = d.x + d.y;
+            } else {
+                double d = 0.0;
+#pragma unroll
+                for (int i = 0; i < NV; ++i) {
+                    d = fma((double)vv[i].x, (double)q[i].x, d);
+                    d = fma((double)vv[i].y, (double)q[i].y, d);
+                    acc[2 * i] = fma((double)cfe, (double)q[i].x, acc[2 * i]);
+                    acc[2 * i + 1] = fma((double)cfe, (double)q[i].y, acc[2 * i + 1]);
+                }
+                dot = d;
+            }
+            for (int o = segs >> 1; o > 0; o >>= 1) dot += __shfl_xor_sync(group, dot, o);
+            if (seg == 0 && !(idx & kTilePoison))
+                gcorner[((((size_t)b * g.Lq + q0 + qi) * g.H + h) * LP + l * P + p) * 4 + k] = dot;
+        }
+    };
+
+    const int max_per_thread = (tp.tq * P + nthr - 1) / nthr;  // <= 2 (planned)
+    for (int c = 0; c < nchunks; ++c) {
+        const int q0 = c * tp.tq, nq = min(tp.tq, g.Lq - q0);
+        if (staged) {
+            if (c + 1 < nchunks) issue(c + 1);
+            cp_async_commit();
+            cp_async_wait_one();
+        }
+        __syncthreads();  // chunk c landed; the previous chunk's bins are drained
+        if (staged) {
+            // Non-finite gradient rows of the chunk.
+            const unsigned char *gs = gb(c & 1);
+            const int nv = D * (int)sizeof(TG) / 16;
+            for (int i = tid; i < nq; i += nthr) {
+                bool bad = false;
+                for (int j = 0; j < nv; ++j) {
+                    const uint4 u = *reinterpret_cast<const uint4 *>(gs + (size_t)i * tp.gstride + j * 16);
+                    float2 f[4];
+                    if constexpr (sizeof(TG) == 2) {
+                        f[0] = bf16x2_lo_hi(u.x); f[1] = bf16x2_lo_hi(u.y); f[2] = bf16x2_lo_hi(u.z); f[3] = bf16x2_lo_hi(u.w);
+                    } else {
+                        f[0] = make_float2(__uint_as_float(u.x), __uint_as_float(u.y));
+                        f[1] = make_float2(__uint_as_float(u.z), __uint_as_float(u.w));
+                        f[2] = f[3] = make_float2(0.f, 0.f);
+                    }
+                    bad |= any_nonfinite<4>(f);
+                }
+                gbad[i] = bad ? 1 : 0;
+                if (bad) s_bad = 1;
+            }
+            __syncthreads();
+        }
+        unsigned pending = 0;
+        for (int i = 0; i < max_per_thread; ++i) {
+            const int sidx = tid + i * nthr;
+            if (sidx < nq * P) pending |= file(c, sidx, 0xFu) << (4 * i);
+        }
+        bool again = __syncthreads_or(pending != 0u);
+        own(c);
+        for (int round = 0; again && round < 65536; ++round) {  // full bins: refile what did not fit
+            __syncthreads();
+            unsigned left = 0;
+            for (int i = 0; i < max_per_thread; ++i) {
+                const int sidx = tid + i * nthr;
+                const unsigned want = (pending >> (4 * i)) & 0xFu;
+                if (want && sidx < nq * P) left |= file(c, sidx, want) << (4 * i);
+            }
+            pending = left;
+            again = __syncthreads_or(pending != 0u);
+            own(c);
+        }
+    }
+    if (owner) {
+        TV *dst = grad_value + (slab_rows + ls + p0 + pl) * D + seg * CPT;
+        float f[CPT];
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) f[i] = (float)acc[i];
+        store_vec<TV, CPT>(dst, f);
+    }
+    __syncthreads();
+    if (tid == 0 && s_bad) atomicOr(flags + bh, 1);
+}
+
+// K2: weight and location gradients of every sample from its corners' G.
+template <typename TV, typename TW>
+__global__ void __launch_bounds__(256)
+msda_backward_finish_kernel(const TV *__restrict__ value, const float *__restrict__ loc, const TW *__restrict__ attn,
+                            const typename OutOf<TV, TW>::T *__restrict__ grad_out,
+                            const typename AccOf<TV>::T *__restrict__ gcorner, const int *__restrict__ flags,
+                            float *__restrict__ grad_loc, TW *__restrict__ grad_attn, const Geom g) {
+    using AT = typename AccOf<TV>::T;
+    const long long total = (long long)g.B * g.Lq * g.H * g.L * g.P;
+    const float qnan = __int_as_float(0x7fc00000);
+    for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < total;
+         s += (long long)gridDim.x * blockDim.x) {
+        const int p = (int)(s % g.P);
+        const int l = (int)((s / g.P) % g.L);
+        const long long row = s / ((long long)g.L * g.P);  // (b, q, h)
+        const int h = (int)(row % g.H);
+        const int b = (int)(row / ((long long)g.Lq * g.H));
+        const int W = select_level(g.lw, l), Hh = select_level(g.lh, l), ls = select_level(g.ls, l);
+        const float Wf = (float)W, Hf = (float)Hh;
+        const float2 xy = __ldg(reinterpret_cast<const float2 *>(loc) + s);
+        const float a = to_f32(__ldg(attn + s));
+        const OwnTaps t = own_taps(xy, Wf, Hf, W, Hh);
+        float2 out_loc;
+        float out_attn;
+        if (!t.ok) {
+            out_loc = make_float2(qnan, qnan);
+            out_attn = qnan;
+        } else {
+            const float m[4] = {t.m00, t.m10, t.m01, t.m11};
+            AT e[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) e[k] = m[k] != 0.f ? __ldg(gcorner + s * 4 + k) : (AT)0;
+            const int bh = b * g.H + h;
+            if ((m[0] == 0.f || m[1] == 0.f || m[2] == 0.f || m[3] == 0.f) && __ldg(flags + bh)) {
+                // Out-of-range corners: m * (v . g), NaN when the clipped row or g is not finite.
+                const int pp[4] = {t.p00, t.p10, t.p01, t.p11};
+                const auto *grow = grad_out + row * g.D;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (m[k] != 0.f) continue;
+                    const TV *vrow = value + ((size_t)bh * g.Lv + ls + pp[k]) * g.D;
+                    AT d = 0;
+                    for (int ch = 0; ch < g.D; ++ch) d += (AT)to_f32(vrow[ch]) * (AT)to_f32(grow[ch]);
+                    e[k] = (AT)0 * d;
+                }
+            }
+            const AT wx1 = t.wx1, wy1 = t.wy1, wx0 = (AT)1 - wx1, wy0 = (AT)1 - wy1;
+            const AT ds = wy0 * (wx0 * e[0] + wx1 * e[1]) + wy1 * (wx0 * e[2] + wx1 * e[3]);
+            const AT dx = wy0 * (e[1] - e[0]) + wy1 * (e[3] - e[2]);
+            const AT dy = wx0 * (e[2] - e[0]) + wx1 * (e[3] - e[1]);
+            out_attn = (float)ds;
+            out_loc = make_float2((float)((AT)Wf * ((AT)a * dx)), (float)((AT)Hf * ((AT)a * dy)));
+        }
+        grad_attn[s] = from_f32<TW>(out_attn);
+        reinterpret_cast<float2 *>(grad_loc)[s] = out_loc;
+    }
+}
+
+// Host planning of the tile backward.  Returns false when the shape or alignment does not fit.
+template <typename TV, typename TW>
+bool plan_backward_tiles(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
+                         const void *grad_value, int optin, TilePlan &tp, int &cpt) {
+    using TG = typename OutOf<TV, TW>::T;
+    if (!(g.P == 1 || g.P == 2 || g.P == 4 || g.P == 8)) return false;
+    cpt = sizeof(TV) == 2 ? 16 : 8;
+    if (g.D % cpt != 0 && sizeof(TV) == 2 && g.D % 8 == 0) cpt = 8;
+    if (g.D % cpt != 0) return false;
+    tp.segs = g.D / cpt;
+    if (tp.segs > 32 || (tp.segs & (tp.segs - 1)) != 0) return false;
+    if (!aligned(value, 16) || !aligned(grad_value, 16) || !aligned(gout, 16) || !aligned(loc, 8) ||
+        !aligned(attn, sizeof(TW)))
+        return false;
+    if (((size_t)g.D * sizeof(TG)) % 16 != 0) return false;
+    const Tune tune = read_tune(kKnobMsdaTiles);
+    if (tune.stage == 0) return false;
+    // Positions per tile: up to 512 threads' worth, balanced within each level.
+    const int np_max = std::max(1, (tune.threads > 0 ? tune.threads : 512) / tp.segs);
+    int npl_max = 1, total_tiles = 0;
+    for (int l = 0; l < g.L; ++l) {
+        const int hw = g.lh[l] * g.lw[l];
+        const int nt = (hw + np_max - 1) / np_max;
+        tp.np[l] = (hw + nt - 1) / nt;
+        tp.tiles_before[l] = total_tiles;
+        total_tiles += nt;
+        npl_max = std::max(npl_max, tp.np[l]);
+    }
+    for (int l = g.L; l < kMaxLevels; ++l) {
+        tp.np[l] = 1;
+        tp.tiles_before[l] = total_tiles;
+        tp.cap[l] = 1;
+        tp.staged[l] = 0;
+    }
+    tp.tiles_before[kMaxLevels] = total_tiles;
+    if (total_tiles > 65535 || (long long)g.B * g.H > 65535) return false;
+    tp.nthr = ((npl_max * tp.segs + 31) / 32) * 32;
+    if (tp.nthr > kTileThreadsMax) return false;
+    tp.tq = std::max(1, std::min(g.Lq, 2 * tp.nthr / g.P));
+    tp.tq = std::min(tp.tq, 8192 / g.P);
+    auto granule = [](long long seg, const void *base) -> int {
+        for (int gsz = 16; gsz >= 4; gsz >>= 1)
+            if (seg % gsz == 0 && aligned(base, gsz)) return gsz;
+        return 0;
+    };
+    tp.gl = granule((long long)g.P * 8, loc);
+    tp.ga = granule((long long)g.P * sizeof(TW), attn);
+    // Bins: records per position per chunk follow a Poisson law around tq * P * 4 / HW; the cap
+    // leaves room for ~4 standard deviations (a full bin is refiled, so any pattern is exact).
+    size_t bins_bytes = 0;
+    bool any_staged = false;
+    for (int l = 0; l < g.L; ++l) {
+        const int hw = g.lh[l] * g.lw[l];
+        const double per_query = (double)g.P * 4.0 / hw;
+        const double mean = per_query * tp.tq;
+        tp.staged[l] = (tune.acc != 0) && per_query * g.Lq >= 4.0;
+        any_staged |= tp.staged[l] != 0;
+        int cap = (int)std::ceil(mean + 4.0 * std::sqrt(mean) + 4.0);
+        cap = std::max(4, std::min(cap, tune.hsub > 0 ? tune.hsub : 64));
+        tp.cap[l] = cap;
+        bins_bytes = std::max(bins_bytes, (size_t)cap * tp.np[l] * 6);
+    }
+    auto r16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
+    tp.gstride = g.D * (int)sizeof(TG) + 16;
+    size_t o = 0;
+    tp.loc_sz = any_staged ? (unsigned)r16((size_t)tp.tq * g.P * 8) : 0;
+    tp.o_loc = (unsigned)o; o += 2 * (size_t)tp.loc_sz;
+    tp.attn_sz = any_staged ? (unsigned)r16((size_t)tp.tq * g.P * sizeof(TW)) : 0;
+    tp.o_attn = (unsigned)o; o += 2 * (size_t)tp.attn_sz;
+    tp.g_sz = any_staged ? (unsigned)r16((size_t)tp.tq * tp.gstride) : 0;
+    tp.o_g = (unsigned)o; o += 2 * (size_t)tp.g_sz;
+    tp.o_gbad = (unsigned)o; o += r16(any_staged ? (size_t)tp.tq : 0);
+    tp.o_cnt = (unsigned)o; o += r16((size_t)npl_max * 4);
+    tp.o_bins = (unsigned)o; o += r16(bins_bytes);
+    tp.smem = o;
+    if (!tp.gl || !tp.ga) return false;
+    return tp.smem <= (size_t)optin;
+}
+
+// Workspace of the tile backward: the per-corner G array and the per-slab flags.
+size_t tile_workspace_bytes(int value_dtype, const Geom &g) {
+    const size_t gsize = value_dtype == RFDETR_F32 ? sizeof(double) : sizeof(float);
+    const size_t corners = (size_t)g.B * g.Lq * g.H * g.L * g.P * 4;
+    return ((corners * gsize + 255) & ~(size_t)255) + (size_t)g.B * g.H * sizeof(int);
+}
+
+template <typename TV, typename TW, int P, int CPT>
+int launch_backward_tiles_k(const Geom &g, const TilePlan &tp, const void *value, const float *loc, const void *attn,
+                            const void *gout, void *gv, float *gl, void *ga, void *ws, cudaStream_t s) {
+    using TG = typename OutOf<TV, TW>::T;
+    using AT = typename AccOf<TV>::T;
+    const size_t corners = (size_t)g.B * g.Lq * g.H * g.L * g.P * 4;
+    AT *gcorner = static_cast<AT *>(ws);
+    int *flags = reinterpret_cast<int *>(static_cast<char *>(ws) + ((corners * sizeof(AT) + 255) & ~(size_t)255));
+    if (cudaMemsetAsync(flags, 0, (size_t)g.B * g.H * sizeof(int), s) != cudaSuccess) return RFDETR_ERR_CUDA;
+    auto k1 = msda_backward_tile_kernel<TV, TW, P, CPT>;
+    if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tp.smem) != cudaSuccess)
+        return RFDETR_ERR_CUDA;
+    const dim3 grid((unsigned)tp.tiles_before[kMaxLevels], (unsigned)(g.B * g.H));
+    k1<<<grid, tp.nthr, tp.smem, s>>>(static_cast<const TV *>(value), loc, static_cast<const TW *>(attn),
+                                       static_cast<const TG *>(gout), static_cast<TV *>(gv), gcorner, flags, g, tp);
+    if (launch_status() != RFDETR_OK) return RFDETR_ERR_CUDA;
+    const long long samples = (long long)g.B * g.Lq * g.H * g.L * g.P;
+    const unsigned blocks = (unsigned)std::min<long long>((samples + 255) / 256, (long long)num_sms() * 16);
+    msda_backward_finish_kernel<TV, TW><<<std::max(blocks, 1u), 256, 0, s>>>(
+        static_cast<const TV *>(value), loc, static_cast<const TW *>(attn), static_cast<const TG *>(gout), gcorner,
+        flags, gl, static_cast<TW *>(ga), g);
+    return launch_status();
+}
+
+template <typename TV, typename TW>
+int try_backward_tiles(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
+                       void *gv, float *gl, void *ga, void *ws, size_t ws_bytes, int value_dtype, cudaStream_t s) {
+    TilePlan tp;
+    int cpt = 0;
+    if (!plan_backward_tiles<TV, TW>(g, value, loc, attn, gout, gv, max_smem_optin(), tp, cpt)) return -1;
+    if (!ws || ws_bytes < tile_workspace_bytes(value_dtype, g) || !aligned(ws, 256)) return -1;
+    auto go = [&](auto p_tag, auto c_tag) {
+        constexpr int PP = decltype(p_tag)::value, CC = decltype(c_tag)::value;
+        return launch_backward_tiles_k<TV, TW, PP, CC>(g, tp, value, loc, attn, gout, gv, gl, ga, ws, s);
+    };
+    using I1 = std::integral_constant<int, 1>;
+    using I2 = std::integral_constant<int, 2>;
+    using I4 = std::integral_constant<int, 4>;
+    using I8 = std::integral_constant<int, 8>;
+    using I16 = std::integral_constant<int, 16>;
+    if (cpt == 16) {
+        if constexpr (sizeof(TV) == 2) {
+            switch (g.P) {
+                case 1: return go(I1{}, I16{});
+                case 2: return go(I2{}, I16{});
+                case 4: return go(I4{}, I16{});
+                case 8: return go(I8{}, I16{});
+            }
+        }
+        return -1;
+    }
+    switch (g.P) {
+        case 1: return go(I1{}, I8{});
+        case 2: return go(I2{}, I8{});
+        case 4: return go(I4{}, I8{});
+        case 8: return go(I8{}, I8{});
+    }
+    return -1;
+}
+
 }  // namespace
 }  // namespace rfdetr
 
@@ -2096,6 +2680,19 @@ extern "C" size_t rfdetr_msda_backward_workspace_size(int value_dtype, int64_t b
     return (size_t)batch * n_heads * len_value * head_dim * sizeof(float);
 }
 
+extern "C" size_t rfdetr_msda_backward_workspace_bytes(int value_dtype, int weight_dtype,
+                                                       const int64_t *spatial_shapes, int64_t batch, int64_t n_heads,
+                                                       int64_t head_dim, int64_t len_query, int64_t n_levels,
+                                                       int64_t n_points) {
+    if (!dtype_ok(value_dtype) || !dtype_ok(weight_dtype)) return 0;
+    Geom g;
+    if (validate(spatial_shapes, nullptr, batch, n_heads, head_dim, len_query, n_levels, n_points, g) != RFDETR_OK)
+        return 0;
+    if (g.B == 0 || g.Lq == 0) return 0;
+    const size_t generic = rfdetr_msda_backward_workspace_size(value_dtype, batch, n_heads, head_dim, g.Lv);
+    return std::max(generic, tile_workspace_bytes(value_dtype, g));
+}
+
 extern "C" int rfdetr_msda_backward(void *stream, const void *value, int value_dtype,
                                     const int64_t *spatial_shapes, const int64_t *level_start_index,
                                     const float *sampling_locations, const void *attention_weights,
@@ -2131,11 +2728,33 @@ extern "C" int rfdetr_msda_backward(void *stream, const void *value, int value_d
                                             grad_sampling_locations, grad_attention_weights, s);
         if (st2 >= 0) return st2;
         if (weight_dtype == RFDETR_BF16)
+            st2 = try_backward_tiles<bf16, bf16>(g, value, sampling_locations, attention_weights, grad_output,
+                                                 grad_value, grad_sampling_locations, grad_attention_weights,
+                                                 workspace, workspace_bytes, value_dtype, s);
+        else
+            st2 = try_backward_tiles<bf16, float>(g, value, sampling_locations, attention_weights, grad_output,
+                                                  grad_value, grad_sampling_locations, grad_attention_weights,
+                                                  workspace, workspace_bytes, value_dtype, s);
+        if (st2 >= 0) return st2;
+        if (weight_dtype == RFDETR_BF16)
             st2 = try_backward_bins<bf16>(g, value, sampling_locations, attention_weights, grad_output, grad_value,
                                           grad_sampling_locations, grad_attention_weights, s);
         else
             st2 = try_backward_bins<float>(g, value, sampling_locations, attention_weights, grad_output, grad_value,
                                            grad_sampling_locations, grad_attention_weights, s);
+        if (st2 >= 0) return st2;
+    }
+    if (value_dtype == RFDETR_F32 && g.Lq > 0 && aligned(sampling_locations, 8) &&
+        aligned(grad_sampling_locations, 8) && aligned(attention_weights, ws) && aligned(grad_attention_weights, ws)) {
+        const int st2 = weight_dtype == RFDETR_BF16
+                            ? try_backward_tiles<float, bf16>(g, value, sampling_locations, attention_weights,
+                                                              grad_output, grad_value, grad_sampling_locations,
+                                                              grad_attention_weights, workspace, workspace_bytes,
+                                                              value_dtype, s)
+                            : try_backward_tiles<float, float>(g, value, sampling_locations, attention_weights,
+                                                               grad_output, grad_value, grad_sampling_locations,
+                                                               grad_attention_weights, workspace, workspace_bytes,
+                                                               value_dtype, s);
         if (st2 >= 0) return st2;
     }
     if (value_dtype == RFDETR_BF16 && !aligned(grad_value, 16)) return RFDETR_ERR_ALIGN;

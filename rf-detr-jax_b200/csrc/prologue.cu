@@ -298,6 +298,78 @@ msda_prologue_bwd_kernel(const float *__restrict__ g_loc, const TA *__restrict__
     }
 }
 
+// The same backward with one thread per (query row, head), for head counts that are powers of
+// two up to 32: a row's heads are H consecutive lanes of one warp, so the loads of g_loc, the
+// offsets and the weights and the stores of the projection's gradient are contiguous across the
+// warp, and the reference points' gradient (a sum over heads and points) is a shuffle reduction
+// over the row's lanes.  Same formulas as msda_prologue_bwd_kernel; the sum over heads is a
+// butterfly instead of a loop, so float32 rounding may differ in the last bits.
+template <typename TA>
+__global__ void __launch_bounds__(256)
+msda_prologue_bwd_head_kernel(const float *__restrict__ g_loc, const TA *__restrict__ g_attn,
+                              const TA *__restrict__ attn, const float *__restrict__ ref,
+                              const float *__restrict__ offsets, float *__restrict__ g_y, float *__restrict__ g_ref,
+                              const ProGeom g) {
+    const int LP = g.L * g.P;
+    const int hlp = g.H * LP;
+    const long long total = (long long)g.N * g.H;
+    // Whole warps iterate together (H divides 32, so a row's lanes are all active or all not).
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long base = (long long)blockIdx.x * blockDim.x; base < total; base += stride) {
+        const long long it = base + threadIdx.x;
+        const bool act = it < total;
+        const long long n = act ? it / g.H : 0;
+        const int h = act ? (int)(it - n * g.H) : 0;
+        float *gy = g_y + n * g.cout;
+        if (act) {
+            const TA *ah = attn + n * hlp + h * LP;
+            const TA *gh = g_attn + n * hlp + h * LP;
+            float dot = 0.f;
+            for (int k = 0; k < LP; ++k) dot += to_f32(ah[k]) * to_f32(gh[k]);
+            for (int k = 0; k < LP; ++k) gy[2 * hlp + h * LP + k] = to_f32(ah[k]) * (to_f32(gh[k]) - dot);
+        }
+        const float *gl = g_loc + n * hlp * 2;
+        const float *rr = ref + n * g.L * g.R;
+        const float *off = g.R == 4 ? offsets + n * hlp * 2 : nullptr;
+        for (int l = 0; l < g.L; ++l) {
+            float sx = 0.f, sy = 0.f, sw = 0.f, sh = 0.f;
+            if (act) {
+                const float rw = g.R == 4 ? rr[l * g.R + 2] : 0.f, rh = g.R == 4 ? rr[l * g.R + 3] : 0.f;
+                for (int p = 0; p < g.P; ++p) {
+                    const int o = ((h * g.L + l) * g.P + p) * 2;
+                    const float gx = gl[o], gyv = gl[o + 1];
+                    sx += gx;
+                    sy += gyv;
+                    if (g.R == 2) {
+                        gy[o] = __fdiv_rn(gx, g.lw[l]);
+                        gy[o + 1] = __fdiv_rn(gyv, g.lh[l]);
+                    } else {
+                        gy[o] = __fdiv_rn(gx * (rw * 0.5f), (float)g.P);
+                        gy[o + 1] = __fdiv_rn(gyv * (rh * 0.5f), (float)g.P);
+                        sw += gx * (off[o] / (float)g.P) * 0.5f;
+                        sh += gyv * (off[o + 1] / (float)g.P) * 0.5f;
+                    }
+                }
+            }
+            for (int m = g.H >> 1; m > 0; m >>= 1) {
+                sx += __shfl_xor_sync(0xffffffffu, sx, m);
+                sy += __shfl_xor_sync(0xffffffffu, sy, m);
+                sw += __shfl_xor_sync(0xffffffffu, sw, m);
+                sh += __shfl_xor_sync(0xffffffffu, sh, m);
+            }
+            if (act && h == 0) {
+                float *gr = g_ref + (n * g.L + l) * g.R;
+                gr[0] = sx;
+                gr[1] = sy;
+                if (g.R == 4) {
+                    gr[2] = sw;
+                    gr[3] = sh;
+                }
+            }
+        }
+    }
+}
+
 }  // namespace
 }  // namespace rfdetr
 
@@ -415,6 +487,19 @@ extern "C" int rfdetr_msda_prologue_backward(void *stream, const float *grad_loc
         g.lw[l] = (float)wid;
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (g.H <= 32 && (g.H & (g.H - 1)) == 0) {
+        const unsigned grid = (unsigned)std::min<long long>(((long long)g.N * g.H + 255) / 256, 148LL * 64);
+        if (weights_dtype == RFDETR_BF16)
+            msda_prologue_bwd_head_kernel<bf16><<<grid, 256, 0, s>>>(
+                grad_locations, static_cast<const bf16 *>(grad_weights), static_cast<const bf16 *>(attention_weights),
+                reference_points, offsets, grad_projection, grad_reference_points, g);
+        else
+            msda_prologue_bwd_head_kernel<float><<<grid, 256, 0, s>>>(
+                grad_locations, static_cast<const float *>(grad_weights),
+                static_cast<const float *>(attention_weights), reference_points, offsets, grad_projection,
+                grad_reference_points, g);
+        return launch_status();
+    }
     const unsigned grid = (unsigned)std::min<long long>((g.N + 255) / 256, 148LL * 8);
     if (weights_dtype == RFDETR_BF16)
         msda_prologue_bwd_kernel<bf16><<<grid, 256, 0, s>>>(grad_locations, static_cast<const bf16 *>(grad_weights),

@@ -89,7 +89,9 @@ static ffi::Error MsdaBwd(cudaStream_t stream, ffi::ScratchAllocator scratch, ff
     const int64_t Lv = dim(value, 1), D = dim(value, 2);
     if (L != levels_of(shapes)) return status_error(RFDETR_ERR_SHAPE, "RfdetrMsdaBwd");
     const int vd = dtype_code(value.element_type());
-    const size_t bytes = rfdetr_msda_backward_workspace_size(vd, B, H, D, Lv);
+    (void)Lv;
+    const size_t bytes = rfdetr_msda_backward_workspace_bytes(vd, dtype_code(weights.element_type()),
+                                                              shapes.begin(), B, H, D, Lq, L, P);
     void *ws = nullptr;
     if (bytes) {
         auto block = scratch.Allocate(bytes, 256);

@@ -88,9 +88,11 @@ def msda_backward(value, shapes, sampling_locations, attention_weights, grad_out
     grad_loc = torch.empty_like(sampling_locations)
     grad_attn = torch.empty_like(attention_weights)
     lib = N.lib()
-    ws_bytes = lib.rfdetr_msda_backward_workspace_size(N.dtype_code(value.dtype), batch, heads, dim, value.shape[1])
-    workspace = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=value.device) if ws_bytes else None
     flat = [v for hw in shapes for v in hw]
+    ws_bytes = lib.rfdetr_msda_backward_workspace_bytes(N.dtype_code(value.dtype), N.dtype_code(attention_weights.dtype),
+                                                        N.int64_array(flat), batch, heads, dim, len_query, levels,
+                                                        points)
+    workspace = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=value.device) if ws_bytes else None
     status = lib.rfdetr_msda_backward(
         N.stream_of(value), N.ptr(value), N.dtype_code(value.dtype), N.int64_array(flat), None,
         N.ptr(sampling_locations), N.ptr(attention_weights), N.dtype_code(attention_weights.dtype),

@@ -216,8 +216,11 @@ def test_unaligned_views_and_entry_points(pkg):
         ("owner, TMA tile loads", {}),
         ("owner, cp.async tile loads", {"RFDETR_MSDA_OWN": "24,1,0"}),
         ("owner, full bins refiled", {"RFDETR_MSDA_OWN": "2,1,1"}),
-        ("bins", {"RFDETR_MSDA_OWN": "0,0"}),
-        ("float32 workspace", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_BINS": "0,0"}),
+        ("position tiles, staged", {"RFDETR_MSDA_OWN": "0,0"}),
+        ("position tiles, from L2", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1,0"}),
+        ("position tiles, small CTAs, full bins refiled", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "4,1,1,128"}),
+        ("bins", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,0"}),
+        ("float32 workspace", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_BINS": "0,0", "RFDETR_MSDA_TILES": "0,0"}),
     ],
 )
 def test_backward_variants(pkg, tuning, paths, env):
@@ -241,6 +244,8 @@ def test_backward_variants(pkg, tuning, paths, env):
     [
         ("owner, TMA tile loads", {}),
         ("owner, cp.async tile loads", {"RFDETR_MSDA_OWN": "24,1,0"}),
+        ("position tiles, staged", {"RFDETR_MSDA_OWN": "0,0"}),
+        ("position tiles, from L2", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1,0"}),
     ],
 )
 def test_backward_non_finite_rows(pkg, tuning, paths, env):
@@ -268,6 +273,64 @@ def test_backward_non_finite_rows(pkg, tuning, paths, env):
         np.testing.assert_array_equal(fg, fw, err_msg=f"{paths}:{n} finiteness")
         assert_bf16_close(np.where(fw, g, 0.0), np.where(fw, w, 0.0), f"{paths}:{n}")
     assert pkg._native.lib().rfdetr_take_device_fault(torch.cuda.current_stream().cuda_stream) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize(
+    ("paths", "env"),
+    [
+        ("position tiles", {}),
+        ("position tiles, from L2", {"RFDETR_MSDA_TILES": "0,1,0"}),
+        ("position tiles, full bins refiled", {"RFDETR_MSDA_TILES": "3,1,1,64"}),
+        ("accumulate kernels", {"RFDETR_MSDA_TILES": "0,0"}),
+    ],
+)
+def test_backward_non_finite_multilevel(pkg, tuning, paths, env, dtype):
+    """Three levels, four points, 32 channels (the config-3 layout, smaller): inf/NaN in value rows
+    (border rows that out-of-range corners clip to, an interior row) and in gradient rows, with
+    locations reaching outside the map.  Non-finite outputs where the float64 oracle has them, the
+    rest within the contract."""
+    for k, v in env.items():
+        tuning(k, v)
+    shapes = ((16, 20), (8, 10), (4, 5))
+    args = dict(seed=13, batch=2, len_query=300, heads=4, shapes=shapes, points=4, dim=32, lo=-0.1, hi=1.1)
+    value, loc, attn, grad = sampler_inputs(**args)
+    bf16 = dtype == torch.bfloat16
+    if bf16:
+        value, attn, grad = O.bf16_round(value), O.bf16_round(attn), O.bf16_round(grad)
+    value[0, 0, 3] = np.inf           # level 0, corner position (0, 0) of slab 0
+    value[3, 320 + 9, 7] = np.nan     # level 1, position (0, 9) of slab 3
+    value[6, 400 + 12, 0] = -np.inf   # level 2, interior position
+    grad[0, 7, 1 * 32 + 2] = np.inf   # image 0, query 7, head 1
+    grad[1, 250, 3 * 32 + 31] = np.nan
+    with np.errstate(invalid="ignore", over="ignore"):
+        want = (O.ms_deform_attn_forward(value, shapes, loc, attn),) + O.ms_deform_attn_backward(
+            value, shapes, loc, attn, grad)
+    got = _run(pkg, value, shapes, loc, attn, grad, dtype)
+    for g, w, n in zip(got, want, ("out", "grad_value", "grad_loc", "grad_attn"), strict=True):
+        fw, fg = np.isfinite(w), np.isfinite(g)
+        assert (~fw).any(), f"{n}: the case should produce non-finite entries"
+        np.testing.assert_array_equal(fg, fw, err_msg=f"{paths}:{n} finiteness")
+        if bf16:
+            assert_bf16_close(np.where(fw, g, 0.0), np.where(fw, w, 0.0), f"{paths}:{n}")
+        else:
+            assert_fp32_close(np.where(fw, g, 0.0), np.where(fw, w, 0.0), f"{paths}:{n}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_tile_backward_ragged_levels(pkg, tuning, dtype):
+    """Level sizes that do not divide into the CTA's positions, one query, and more queries than
+    a chunk: the tile kernels against the oracle."""
+    tuning("RFDETR_MSDA_TILES", "0,1,1,128")
+    for lq, shapes in ((1, ((7, 9), (3, 5))), (1500, ((13, 11), (1, 1), (5, 2)))):
+        args = dict(seed=lq, batch=2, len_query=lq, heads=2, shapes=shapes, points=2, dim=16, lo=-0.2, hi=1.2)
+        value, loc, attn, grad = sampler_inputs(**args)
+        bf16 = dtype == torch.bfloat16
+        if bf16:
+            value, attn, grad = O.bf16_round(value), O.bf16_round(attn), O.bf16_round(grad)
+        want = (O.ms_deform_attn_forward(value, shapes, loc, attn),) + O.ms_deform_attn_backward(
+            value, shapes, loc, attn, grad)
+        _check(_run(pkg, value, shapes, loc, attn, grad, dtype), want, bf16, f"ragged-{lq}")
 
 
 def test_error_behaviour(pkg):

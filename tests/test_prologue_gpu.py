@@ -56,6 +56,7 @@ CASES = [  # (C, H, L, P, shapes, B, Lq)
     (256, 16, 1, 2, ((24, 24),), 2, 700),                          # the Nano decoder (config 2 layout)
     (256, 8, 4, 4, ((80, 80), (40, 40), (20, 20), (10, 10)), 2, 300),  # four levels (config 3 layout)
     (64, 4, 2, 1, ((7, 9), (3, 5)), 1, 37),                        # ragged row tail, odd level shapes
+    (48, 6, 1, 4, ((9, 7),), 1, 29),                               # 6 heads: the per-row backward kernel
 ]
 
 
@@ -88,7 +89,7 @@ def test_forward(pkg, dtype, ref_dim, case):
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("ref_dim", [2, 4])
-@pytest.mark.parametrize("case", [0, 1])
+@pytest.mark.parametrize("case", [0, 1, 3])
 def test_backward(pkg, dtype, ref_dim, case):
     """Gradients with respect to the query, both projections and the reference points against
     the oracle's float64 gradient, at the config-2 and config-3 layouts."""

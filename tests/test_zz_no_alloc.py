@@ -178,5 +178,7 @@ def test_noalloc_serves_large_scratch_free_shapes(pkg):
         N.check(st, "noalloc" if noalloc else "backward")
         torch.cuda.synchronize()
         out.append([x.float().cpu().numpy() for x in (gv, gl, ga)])
+    # The owner kernel's float32 accumulation order follows its shared-memory slot order, so two
+    # runs can differ by one bf16 unit in grad_value: compare within the bf16 tolerance.
     for name, x, y in zip(("grad_value", "grad_loc", "grad_attn"), out[1], out[0], strict=True):
-        np.testing.assert_array_equal(x, y, err_msg=name)
+        assert_bf16_close(x, y, name)
