@@ -204,7 +204,7 @@ msda_forward_kernel(const TV *__restrict__ value, const float *__restrict__ loc,
                     continue;
                 }
                 const Taps t = make_taps(ix, iy, W, H);
-                if (!active_lane || t.mask == 0) continue;
+                if (!active_lane) continue;
                 AT s[VEC];
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) s[i] = 0;
@@ -234,6 +234,21 @@ msda_forward_kernel(const TV *__restrict__ value, const float *__restrict__ loc,
                     load_vec<TV, VEC, kNC>(p00 + (size_t)(W + 1) * g.D, v);
 #pragma unroll
                     for (int i = 0; i < VEC; ++i) s[i] = fma(w, (AT)v[i], s[i]);
+                }
+                if (t.mask != 0xFu) {
+                    // Out-of-range corners: the reference reads their clipped rows and weights them
+                    // by 0 (ops.py:98-106,123-128), which changes the sum only where a row holds
+                    // inf/NaN (0 * inf = NaN).
+                    const float fx0 = floorf(ix), fy0 = floorf(iy);
+                    const int cx[2] = {(int)fminf(fmaxf(fx0, 0.f), wf - 1.f), (int)fminf(fmaxf(fx0 + 1.f, 0.f), wf - 1.f)};
+                    const int cy[2] = {(int)fminf(fmaxf(fy0, 0.f), hf - 1.f), (int)fminf(fmaxf(fy0 + 1.f, 0.f), hf - 1.f)};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        if (t.mask & (1u << k)) continue;
+                        load_vec<TV, VEC, kNC>(vl + ((size_t)cy[k >> 1] * W + cx[k & 1]) * g.D, v);
+#pragma unroll
+                        for (int i = 0; i < VEC; ++i) s[i] = fma((AT)0, (AT)v[i], s[i]);
+                    }
                 }
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) acc[i] = fma((AT)a, s[i], acc[i]);
@@ -362,14 +377,36 @@ msda_backward_kernel(const TV *__restrict__ value, const float *__restrict__ loc
                     t.mask = 0u;
                 }
                 const bool tap = ok && active_lane;
+                // Corner rows at the reference's clipped positions (ops.py:98-106); an out-of-range
+                // corner's row enters multiplied by its 0 mask, as in the reference (0 * inf = NaN).
+                long long offs[4] = {0, 0, 0, 0};
+                if (ok) {
+                    const float fx0 = floorf(ix), fy0 = floorf(iy);
+                    const int cx0 = (int)fminf(fmaxf(fx0, 0.f), wf - 1.f), cx1 = (int)fminf(fmaxf(fx0 + 1.f, 0.f), wf - 1.f);
+                    const int cy0 = (int)fminf(fmaxf(fy0, 0.f), hf - 1.f), cy1 = (int)fminf(fmaxf(fy0 + 1.f, 0.f), hf - 1.f);
+                    offs[0] = (long long)cy0 * W + cx0;
+                    offs[1] = (long long)cy0 * W + cx1;
+                    offs[2] = (long long)cy1 * W + cx0;
+                    offs[3] = (long long)cy1 * W + cx1;
+                }
                 float v00[VEC], v10[VEC], v01[VEC], v11[VEC];
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) v00[i] = v10[i] = v01[i] = v11[i] = 0.f;
-                const TV *p00 = vl + t.off00 * g.D;
-                if (tap && (t.mask & 1u)) load_vec<TV, VEC, kNC>(p00, v00);
-                if (tap && (t.mask & 2u)) load_vec<TV, VEC, kNC>(p00 + g.D, v10);
-                if (tap && (t.mask & 4u)) load_vec<TV, VEC, kNC>(p00 + (size_t)W * g.D, v01);
-                if (tap && (t.mask & 8u)) load_vec<TV, VEC, kNC>(p00 + (size_t)(W + 1) * g.D, v11);
+                if (tap) {
+                    load_vec<TV, VEC, kNC>(vl + offs[0] * g.D, v00);
+                    load_vec<TV, VEC, kNC>(vl + offs[1] * g.D, v10);
+                    load_vec<TV, VEC, kNC>(vl + offs[2] * g.D, v01);
+                    load_vec<TV, VEC, kNC>(vl + offs[3] * g.D, v11);
+                    if (t.mask != 0xFu) {
+#pragma unroll
+                        for (int i = 0; i < VEC; ++i) {
+                            if (!(t.mask & 1u)) v00[i] *= 0.f;
+                            if (!(t.mask & 2u)) v10[i] *= 0.f;
+                            if (!(t.mask & 4u)) v01[i] *= 0.f;
+                            if (!(t.mask & 8u)) v11[i] *= 0.f;
+                        }
+                    }
+                }
 
                 const float w00 = t.wx0 * t.wy0, w10 = t.wx1 * t.wy0;
                 const float w01 = t.wx0 * t.wy1, w11 = t.wx1 * t.wy1;
@@ -398,15 +435,26 @@ msda_backward_kernel(const TV *__restrict__ value, const float *__restrict__ loc
                     gl.y = ok ? (float)((AT)hf * ((AT)a * dy)) : qnan;
                     reinterpret_cast<float2 *>(grad_loc)[s_idx] = gl;
                 }
-                if (!tap || t.mask == 0u) continue;
+                if (!tap) continue;
+                // A masked corner adds 0 * a * w * g to its clipped row: nothing, unless a or g is
+                // not finite (then NaN, as the reference's scatter-add gives).
+                unsigned scatter = t.mask;
+                if (t.mask != 0xFu) {
+                    bool gbad = false;
+#pragma unroll
+                    for (int i = 0; i < VEC; ++i) gbad |= !(fabsf(gr[i]) <= 3.4028235e38f);
+                    if (gbad || !(fabsf(a) <= 3.4028235e38f)) scatter = 0xFu;
+                }
+                if (scatter == 0u) continue;
 
-                const float c[4] = {a * w00, a * w10, a * w01, a * w11};
-                const long long offs[4] = {t.off00, t.off00 + 1, t.off00 + W, t.off00 + W + 1};
+                const float mk[4] = {t.mask & 1u ? 1.f : 0.f, t.mask & 2u ? 1.f : 0.f, t.mask & 4u ? 1.f : 0.f,
+                                     t.mask & 8u ? 1.f : 0.f};
+                const float c[4] = {a * w00 * mk[0], a * w10 * mk[1], a * w01 * mk[2], a * w11 * mk[3]};
                 if constexpr (SMEM_ACC) {
                     float *sb = gsm + hs * slab + (size_t)lv.s[l] * g.D + chunk;
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
-                        if (!(t.mask & (1u << k))) continue;
+                        if (!(scatter & (1u << k))) continue;
                         float *p = sb + offs[k] * g.D;
 #pragma unroll
                         for (int i = 0; i < VEC; ++i) atomicAdd(p + ((i + rot) & (VEC - 1)), c[k] * grot[i]);
@@ -415,7 +463,7 @@ msda_backward_kernel(const TV *__restrict__ value, const float *__restrict__ loc
                     float *gb = gdst + hs * slab + (size_t)lv.s[l] * g.D + chunk;
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
-                        if (!(t.mask & (1u << k))) continue;
+                        if (!(scatter & (1u << k))) continue;
                         float add[VEC];
 #pragma unroll
                         for (int i = 0; i < VEC; ++i) add[i] = c[k] * gr[i];
@@ -2038,17 +2086,22 @@ int try_backward_owner(const Geom &g, const void *value, const float *loc, const
 // ------------------------------------------------------------------------------------------
 // Position-tile backward: levels of any size, float32 or bf16 values, no float atomics.
 //
+// K0 (msda_backward_rowsort_kernel), one CTA per (slab, level): a counting sort of the level's
+// samples by the first row their bilinear taps touch (floor(iy), clamped to [-1, H-1]; samples
+// with non-finite positions go to a last bucket that no tile reads).  A tile then finds every
+// sample that can touch its rows in one contiguous range of the sorted list.
+//
 // K1 (msda_backward_tile_kernel) runs one CTA per (slab, tile); a tile is a run of up to `np`
 // consecutive positions of one level.  Each thread owns one position and CPT channels of it:
 // the value row segment and its gradient accumulator (float32 for bf16 values, float64 for
-// float32 values) stay in registers for the whole launch.  The CTA walks the slab's queries in
-// chunks: it computes the taps of the chunk's samples on its level (a sample whose rows miss the
-// tile's row band is dropped after two FMAs), files each corner landing in the tile into its
-// position's bin in shared memory, and the owners drain their bins -- acc += coef * g[q] and the
-// corner's dot product G = <value row, g[q]> (reduced over the position's lanes), written to a
-// per-corner array in the workspace.  grad_value is written once, from the registers.  Levels
-// where a position collects several records per chunk stage the chunk's location, weight and
-// gradient rows in shared memory (double-buffered cp.async); sparse levels read them from L2.
+// float32 values) stay in registers for the whole launch; dense small levels spread a
+// position's records over R replica owners whose accumulators are summed at the end.  The CTA
+// walks its sample range in chunks: it computes the taps, files each corner landing in the tile
+// into its position's bin in shared memory, and the owners drain their bins -- acc += coef * g[q]
+// and the corner's dot product G = <value row, g[q]> (reduced over the position's lanes),
+// written to a per-corner array in the workspace.  grad_value is written once, from the
+// registers.  Gradient rows come from shared memory (all of the slab's rows, staged once) when
+// they fit, else from L2.
 //
 // K2 (msda_backward_finish_kernel) is one thread per sample: from the four corners' G it forms
 // the weight gradient and the location gradient (d ix / d loc = W), as the reference's autodiff
@@ -2063,18 +2116,25 @@ int try_backward_owner(const Geom &g, const void *value, const float *loc, const
 // corners' m * (v . g) from the rows themselves.
 // ------------------------------------------------------------------------------------------
 constexpr int kTileThreadsMax = 512;
-constexpr int kTilePoison = 0x8000;  // record flag: out-of-range corner filed for its NaN, no G
+#ifndef RFDETR_TILE_MIN_BLOCKS
+#define RFDETR_TILE_MIN_BLOCKS 2  // two 512-thread CTAs per SM: 64 registers a thread
+#endif
+constexpr int kTileMaxPerThread = 8;     // samples a thread files per chunk (4 pending bits each)
+constexpr int kTilePoison = 0x8000;      // record flag: out-of-range corner filed for its NaN, no G
+constexpr int kTileMaxRows = 8192;       // rows of a level the row sort handles
+constexpr int kTileMaxReplicas = 8;
 
 struct TilePlan {
-    int segs;                         // threads per position (D / CPT)
-    int tq;                           // queries per chunk
+    int segs;                          // threads per position (D / CPT)
+    int chunk;                         // samples per chunk (<= kTileMaxPerThread * threads)
     int tiles_before[kMaxLevels + 1];  // first tile of each level (per slab)
-    int np[kMaxLevels];               // positions per tile, per level
-    int cap[kMaxLevels];              // bin slots per position, per level
-    int staged[kMaxLevels];           // the level's chunk rows are staged in shared memory
-    int gstride;                      // staged gradient row stride, bytes
-    int gl, ga;                       // cp.async granules of a query's location / weight segment
-    unsigned o_loc, loc_sz, o_attn, attn_sz, o_g, g_sz, o_gbad, o_cnt, o_bins;
+    int np[kMaxLevels];                // positions per tile, per level
+    int cap[kMaxLevels];               // bin slots per position, per level
+    int rep[kMaxLevels];               // replica owners per position, per level
+    int stage_g;                       // the slab's gradient rows are staged in shared memory
+    int gstride;                       // staged gradient row stride, bytes
+    int roff[kMaxLevels + 1];          // first row-offset entry of each level (per slab)
+    unsigned o_g, o_ids, o_cnt, o_bins;
     size_t smem;
     int nthr;
 };
@@ -2088,12 +2148,70 @@ __device__ __forceinline__ int select_level(const int (&a)[N], int l) {
     return r;
 }
 
+// Clamped first row of a sample's taps, plus one: a key in [0, H]; H + 1 for non-finite positions.
+__device__ __forceinline__ int row_key(float ly, float hf, int H) {
+    const float gy = __fmaf_rn(2.f, ly, -1.f);
+    const float iy = __fmaf_rn(__fmul_rn(__fadd_rn(gy, 1.f), hf), 0.5f, -0.5f);
+    if (!(fabsf(iy) <= 3.0e38f)) return H + 1;
+    const float f = fminf(fmaxf(floorf(iy), -1.f), (float)(H - 1));
+    return (int)f + 1;
+}
+
+template <int P>
+__global__ void __launch_bounds__(512)
+msda_backward_rowsort_kernel(const float *__restrict__ loc, int *__restrict__ list, int *__restrict__ roffs,
+                             const Geom g, const TilePlan tp) {
+    constexpr int PS = P == 1 ? 0 : P == 2 ? 1 : P == 4 ? 2 : 3;
+    __shared__ int cnt[kTileMaxRows + 2];
+    const int l = blockIdx.x, bh = blockIdx.y;
+    const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
+    const int Hh = select_level(g.lh, l);
+    const float hf = (float)Hh;
+    const int nb = Hh + 2;
+    const int LP = g.L * P;
+    const int n = g.Lq * P;
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) cnt[i] = 0;
+    __syncthreads();
+    auto key_of = [&](int i) {
+        const int q = i >> PS, p = i & (P - 1);
+        const size_t srow = (((size_t)b * g.Lq + q) * g.H + h) * LP + l * P + p;
+        return row_key(__ldg(reinterpret_cast<const float2 *>(loc) + srow).y, hf, Hh);
+    };
+    for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&cnt[key_of(i)], 1);
+    __syncthreads();
+    // Exclusive scan of the nb counts by warp 0: each lane sums a contiguous run.
+    int *ro = roffs + (size_t)bh * tp.roff[kMaxLevels] + select_level(tp.roff, l);
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const int per = (nb + 31) / 32, k0 = min(lane * per, nb), k1 = min(k0 + per, nb);
+        int sum = 0;
+        for (int k = k0; k < k1; ++k) sum += cnt[k];
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        int run = incl - sum;
+        for (int k = k0; k < k1; ++k) {
+            const int c = cnt[k];
+            cnt[k] = run;
+            ro[k] = run;
+            run += c;
+        }
+        if (lane == 31) ro[nb] = incl;
+    }
+    __syncthreads();
+    int *dst = list + ((size_t)bh * g.L + l) * n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[atomicAdd(&cnt[key_of(i)], 1)] = i;
+}
+
 template <typename TV, typename TW, int P, int CPT>
-__global__ void __launch_bounds__(kTileThreadsMax)
+__global__ void __launch_bounds__(kTileThreadsMax, RFDETR_TILE_MIN_BLOCKS)
 msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict__ loc, const TW *__restrict__ attn,
                           const typename OutOf<TV, TW>::T *__restrict__ grad_out, TV *__restrict__ grad_value,
-                          typename AccOf<TV>::T *__restrict__ gcorner, int *__restrict__ flags, const Geom g,
-                          const TilePlan tp) {
+                          typename AccOf<TV>::T *__restrict__ gcorner, int *__restrict__ flags,
+                          const int *__restrict__ list, const int *__restrict__ roffs, const Geom g, const TilePlan tp) {
     using TG = typename OutOf<TV, TW>::T;
     using AT = typename AccOf<TV>::T;
     constexpr int PS = P == 1 ? 0 : P == 2 ? 1 : P == 4 ? 2 : 3;
@@ -2111,27 +2229,41 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
     const int p0 = (tile - select_level(tp.tiles_before, l)) * npl;
     const int np = min(npl, W * Hh - p0);
     const int cap = select_level(tp.cap, l);
-    const bool staged = select_level(tp.staged, l) != 0;
+    const int R = select_level(tp.rep, l);
     const int row_lo = p0 / W, row_hi = (p0 + np - 1) / W;
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int segs = tp.segs;
-    const int pl = tid / segs, seg = tid - (tid / segs) * segs;
-    const bool owner = pl < np;
-    const int LP = g.L * g.P;
+    const int seg = tid % segs, u = tid / segs;
+    const int pl = u % npl, rep = u / npl;
+    const bool owner = pl < np && rep < R;
+    const int LP = g.L * P;
     const int D = g.D;
     const size_t slab_rows = (size_t)bh * g.Lv;
-    const float qnan = __int_as_float(0x7fc00000);
 
     int *const counts = reinterpret_cast<int *>(smem + tp.o_cnt);
     float *const bcoef = reinterpret_cast<float *>(smem + tp.o_bins);
     unsigned short *const bidx = reinterpret_cast<unsigned short *>(smem + tp.o_bins + (size_t)cap * npl * 4);
-    auto locb = [&](int i) { return reinterpret_cast<float2 *>(smem + tp.o_loc + i * tp.loc_sz); };
-    auto attnb = [&](int i) { return reinterpret_cast<TW *>(smem + tp.o_attn + i * tp.attn_sz); };
-    auto gb = [&](int i) { return smem + tp.o_g + (size_t)i * tp.g_sz; };
-    unsigned char *const gbad = smem + tp.o_gbad;
+    int *const ids = reinterpret_cast<int *>(smem + tp.o_ids);
+    unsigned char *const gst = smem + tp.o_g;
+
+    // The tile's samples: keys [row_lo, row_hi + 1] of the level's row-sorted list.
+    const int *ro = roffs + (size_t)bh * tp.roff[kMaxLevels] + select_level(tp.roff, l);
+    const int s_begin = __ldg(ro + max(row_lo, 0)), s_end = __ldg(ro + min(row_hi + 1, Hh) + 1);
+    const int *slist = list + ((size_t)bh * g.L + l) * (g.Lq * P);
 
     if (tid == 0) s_bad = 0;
     for (int i = tid; i < npl; i += nthr) counts[i] = 0;
+    // The slab's gradient rows, staged once (all queries), when they fit.
+    if (tp.stage_g) {
+        const int gch = D * (int)sizeof(TG) / 16;
+        for (int i = tid; i < g.Lq * gch; i += nthr) {
+            const int q = i / gch, j = i - (i / gch) * gch;
+            cp_async_bytes(gst + (size_t)q * tp.gstride + j * 16,
+                           reinterpret_cast<const char *>(grad_out + (((size_t)b * g.Lq + q) * g.H + h) * D) + j * 16,
+                           16);
+        }
+    }
+    cp_async_commit();
 
     // Owner state.
     constexpr int NV = CPT / 2;
@@ -2162,106 +2294,52 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
         }
         vbad = any_nonfinite<NV>(vv);
     }
-    __syncthreads();  // s_bad and counts initialised
+    cp_async_wait_all();
+    __syncthreads();  // s_bad, counts and the staged rows are ready
     if (vbad) s_bad = 1;
 
-    const int nchunks = (g.Lq + tp.tq - 1) / tp.tq;
-    auto issue = [&](int c) {
-        const int q0 = c * tp.tq, nq = min(tp.tq, g.Lq - q0);
-        const int buf = c & 1;
-        const int lbytes = P * 8, abytes = P * (int)sizeof(TW), gbytes = D * (int)sizeof(TG);
-        const int ls_ = 31 - __clz(lbytes / tp.gl), as_ = 31 - __clz(abytes / tp.ga);
-        const size_t row0 = ((size_t)b * g.Lq + q0) * g.H + h;
-        for (int i = tid; i < (nq << ls_); i += nthr) {
-            const int qi = i >> ls_, j = i & ((1 << ls_) - 1);
-            cp_async_bytes(reinterpret_cast<char *>(locb(buf)) + (size_t)qi * lbytes + j * tp.gl,
-                           reinterpret_cast<const char *>(loc + ((row0 + (size_t)qi * g.H) * LP + l * P) * 2) +
-                               j * tp.gl,
-                           tp.gl);
-        }
-        for (int i = tid; i < (nq << as_); i += nthr) {
-            const int qi = i >> as_, j = i & ((1 << as_) - 1);
-            cp_async_bytes(reinterpret_cast<char *>(attnb(buf)) + (size_t)qi * abytes + j * tp.ga,
-                           reinterpret_cast<const char *>(attn + (row0 + (size_t)qi * g.H) * LP + l * P) + j * tp.ga,
-                           tp.ga);
-        }
-        const int gch = gbytes / 16;
-        for (int i = tid; i < nq * gch; i += nthr) {
-            const int qi = i / gch, j = i - (i / gch) * gch;
-            cp_async_bytes(gb(buf) + (size_t)qi * tp.gstride + j * 16,
-                           reinterpret_cast<const char *>(grad_out + (row0 + (size_t)qi * g.H) * D) + j * 16, 16);
-        }
-    };
-    if (staged) issue(0);
-    cp_async_commit();
-
-    // A g row segment of CPT channels as float pairs: from shared memory or from L2.
-    auto load_g = [&](const unsigned char *row, float2 *q) {
+    auto to_pairs = [&](const uint4 *src, float2 *q, bool global) {
         if constexpr (sizeof(TG) == 2) {
 #pragma unroll
             for (int k = 0; k < CPT / 8; ++k) {
-                const uint4 u = *reinterpret_cast<const uint4 *>(row + k * 16);
-                q[4 * k + 0] = bf16x2_lo_hi(u.x);
-                q[4 * k + 1] = bf16x2_lo_hi(u.y);
-                q[4 * k + 2] = bf16x2_lo_hi(u.z);
-                q[4 * k + 3] = bf16x2_lo_hi(u.w);
+                const uint4 x = global ? __ldg(src + k) : src[k];
+                q[4 * k + 0] = bf16x2_lo_hi(x.x);
+                q[4 * k + 1] = bf16x2_lo_hi(x.y);
+                q[4 * k + 2] = bf16x2_lo_hi(x.z);
+                q[4 * k + 3] = bf16x2_lo_hi(x.w);
             }
         } else {
 #pragma unroll
             for (int k = 0; k < CPT / 4; ++k) {
-                const float4 f = *reinterpret_cast<const float4 *>(row + k * 16);
-                q[2 * k] = make_float2(f.x, f.y);
-                q[2 * k + 1] = make_float2(f.z, f.w);
+                const uint4 x = global ? __ldg(src + k) : src[k];
+                q[2 * k] = make_float2(__uint_as_float(x.x), __uint_as_float(x.y));
+                q[2 * k + 1] = make_float2(__uint_as_float(x.z), __uint_as_float(x.w));
             }
         }
     };
-    auto load_g_global = [&](const TG *row, float2 *q) {
-        if constexpr (sizeof(TG) == 2) {
-#pragma unroll
-            for (int k = 0; k < CPT / 8; ++k) {
-                const uint4 u = __ldg(reinterpret_cast<const uint4 *>(row) + k);
-                q[4 * k + 0] = bf16x2_lo_hi(u.x);
-                q[4 * k + 1] = bf16x2_lo_hi(u.y);
-                q[4 * k + 2] = bf16x2_lo_hi(u.z);
-                q[4 * k + 3] = bf16x2_lo_hi(u.w);
-            }
-        } else {
-#pragma unroll
-            for (int k = 0; k < CPT / 4; ++k) {
-                const float4 f = __ldg(reinterpret_cast<const float4 *>(row) + k);
-                q[2 * k] = make_float2(f.x, f.y);
-                q[2 * k + 1] = make_float2(f.z, f.w);
-            }
-        }
+    auto g_row = [&](int q, int chan) -> const uint4 * {
+        if (tp.stage_g) return reinterpret_cast<const uint4 *>(gst + (size_t)q * tp.gstride + chan * sizeof(TG));
+        return reinterpret_cast<const uint4 *>(grad_out + (((size_t)b * g.Lq + q) * g.H + h) * D + chan);
     };
-    // True when the gradient row of (image b, query q, head h) holds inf/NaN (read from L2).
+    // True when the gradient row of query q holds inf/NaN.
     auto g_row_bad = [&](int q) {
-        const TG *row = grad_out + (((size_t)b * g.Lq + q) * g.H + h) * D;
         bool bad = false;
         for (int k = 0; k < D; k += CPT) {
             float2 x[NV];
-            load_g_global(row + k, x);
+            to_pairs(g_row(q, k), x, !tp.stage_g);
             bad |= any_nonfinite<NV>(x);
         }
         return bad;
     };
 
-    // Files the corners of local sample s (query qi, point p) selected by `want` that land in the
-    // tile; returns those whose bin was full.  `first` also reports whether the sample has an
-    // out-of-range corner whose clipped position is in the tile.
-    auto file = [&](int c, int s, unsigned want) -> unsigned {
-        const int q0 = c * tp.tq;
-        const int qi = s >> PS, p = s & (P - 1);
-        float2 xy;
-        float a;
-        if (staged) {
-            xy = locb(c & 1)[s];
-            a = to_f32(attnb(c & 1)[s]);
-        } else {
-            const size_t srow = (((size_t)b * g.Lq + q0 + qi) * g.H + h) * LP + l * P + p;
-            xy = __ldg(reinterpret_cast<const float2 *>(loc) + srow);
-            a = to_f32(__ldg(attn + srow));
-        }
+    // Files the corners of chunk slot j (selected by `want`) that land in the tile; returns those
+    // whose bin was full.
+    auto file = [&](int j, unsigned want) -> unsigned {
+        const int id = ids[j];
+        const int q = id >> PS, p = id & (P - 1);
+        const size_t srow = (((size_t)b * g.Lq + q) * g.H + h) * LP + l * P + p;
+        const float2 xy = __ldg(reinterpret_cast<const float2 *>(loc) + srow);
+        const float a = to_f32(__ldg(attn + srow));
         float ix, iy;
         sample_coords(xy.x, xy.y, Wf, Hf, ix, iy);
         if (!(fabsf(ix) <= 3.0e38f && fabsf(iy) <= 3.0e38f)) return 0u;
@@ -2283,7 +2361,7 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
             bool poison = false;
             if (!filed) {
                 if (gb_state < 0) {
-                    gb_state = staged ? (int)gbad[qi] : (g_row_bad(q0 + qi) ? 1 : 0);
+                    gb_state = g_row_bad(q) ? 1 : 0;
                     if (gb_state) s_bad = 1;
                 }
                 filed = cf[k] != 0.f || gb_state != 0;
@@ -2293,7 +2371,7 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
             const int slot = atomicAdd(&counts[pt], 1);
             if (slot < cap) {
                 bcoef[slot * npl + pt] = cf[k];
-                bidx[slot * npl + pt] = (unsigned short)(((s << 2) | k) | (poison ? kTilePoison : 0));
+                bidx[slot * npl + pt] = (unsigned short)(((j << 2) | k) | (poison ? kTilePoison : 0));
             } else {
                 failed |= 1u << k;
             }
@@ -2301,34 +2379,30 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
         return failed;
     };
 
-    // Owners drain their bins (and reset their counts).
+    // Owners drain their bins: replica r takes slots r, r + R, ...
     const unsigned group = segs >= 32 ? 0xffffffffu : (((1u << segs) - 1u) << (((tid & 31) / segs) * segs));
-    auto own = [&](int c) {
-        const int q0 = c * tp.tq;
+    auto own = [&]() {
         int n = 0;
         if (owner) n = min(counts[pl], cap);
-        __syncwarp();
-        if (owner && seg == 0) counts[pl] = 0;
-        for (int e = 0; e < n; ++e) {
+        __syncthreads();  // every replica has read its count
+        if (owner && rep == 0 && seg == 0) counts[pl] = 0;
+        for (int e = rep; e < n; e += R) {
             const float cfe = bcoef[e * npl + pl];
             const unsigned idx = bidx[e * npl + pl];
-            const int sl = (int)((idx & 0x7fffu) >> 2), k = (int)(idx & 3u);
-            const int qi = sl >> PS, p = sl & (P - 1);
-            float2 q[NV];
-            if (staged) {
-                load_g(gb(c & 1) + (size_t)qi * tp.gstride + seg * CPT * (int)sizeof(TG), q);
-            } else {
-                load_g_global(grad_out + (((size_t)b * g.Lq + q0 + qi) * g.H + h) * D + seg * CPT, q);
-            }
+            const int j = (int)((idx & 0x7fffu) >> 2), k = (int)(idx & 3u);
+            const int id = ids[j];
+            const int q = id >> PS, p = id & (P - 1);
+            float2 qv[NV];
+            to_pairs(g_row(q, seg * CPT), qv, !tp.stage_g);
             AT dot;
             if constexpr (sizeof(TV) == 2) {
                 const float2 cc = make_float2(cfe, cfe);
-                float2 d = __fmul2_rn(vv[0], q[0]);
+                float2 d = __fmul2_rn(vv[0], qv[0]);
 #pragma unroll
-                for (int i = 1; i < NV; ++i) d = __ffma2_rn(vv[i], q[i], d);
+                for (int i = 1; i < NV; ++i) d = __ffma2_rn(vv[i], qv[i], d);
 #pragma unroll
                 for (int i = 0; i < NV; ++i) {
-                    const float2 t = __ffma2_rn(cc, q[i], make_float2(acc[2 * i], acc[2 * i + 1]));
+                    const float2 t = __ffma2_rn(cc, qv[i], make_float2(acc[2 * i], acc[2 * i + 1]));
                     acc[2 * i] = t.x;
                     acc[2 * i + 1] = t.y;
                 }
@@ -2337,72 +2411,63 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
                 double d = 0.0;
 #pragma unroll
                 for (int i = 0; i < NV; ++i) {
-                    d = fma((double)vv[i].x, (double)q[i].x, d);
-                    d = fma((double)vv[i].y, (double)q[i].y, d);
-                    acc[2 * i] = fma((double)cfe, (double)q[i].x, acc[2 * i]);
-                    acc[2 * i + 1] = fma((double)cfe, (double)q[i].y, acc[2 * i + 1]);
+                    d = fma((double)vv[i].x, (double)qv[i].x, d);
+                    d = fma((double)vv[i].y, (double)qv[i].y, d);
+                    acc[2 * i] = fma((double)cfe, (double)qv[i].x, acc[2 * i]);
+                    acc[2 * i + 1] = fma((double)cfe, (double)qv[i].y, acc[2 * i + 1]);
                 }
                 dot = d;
             }
             for (int o = segs >> 1; o > 0; o >>= 1) dot += __shfl_xor_sync(group, dot, o);
             if (seg == 0 && !(idx & kTilePoison))
-                gcorner[((((size_t)b * g.Lq + q0 + qi) * g.H + h) * LP + l * P + p) * 4 + k] = dot;
+                gcorner[((((size_t)b * g.Lq + q) * g.H + h) * LP + l * P + p) * 4 + k] = dot;
         }
     };
 
-    const int max_per_thread = (tp.tq * P + nthr - 1) / nthr;  // <= 2 (planned)
-    for (int c = 0; c < nchunks; ++c) {
-        const int q0 = c * tp.tq, nq = min(tp.tq, g.Lq - q0);
-        if (staged) {
-            if (c + 1 < nchunks) issue(c + 1);
-            cp_async_commit();
-            cp_async_wait_one();
-        }
-        __syncthreads();  // chunk c landed; the previous chunk's bins are drained
-        if (staged) {
-            // Non-finite gradient rows of the chunk.
-            const unsigned char *gs = gb(c & 1);
-            const int nv = D * (int)sizeof(TG) / 16;
-            for (int i = tid; i < nq; i += nthr) {
-                bool bad = false;
-                for (int j = 0; j < nv; ++j) {
-                    const uint4 u = *reinterpret_cast<const uint4 *>(gs + (size_t)i * tp.gstride + j * 16);
-                    float2 f[4];
-                    if constexpr (sizeof(TG) == 2) {
-                        f[0] = bf16x2_lo_hi(u.x); f[1] = bf16x2_lo_hi(u.y); f[2] = bf16x2_lo_hi(u.z); f[3] = bf16x2_lo_hi(u.w);
-                    } else {
-                        f[0] = make_float2(__uint_as_float(u.x), __uint_as_float(u.y));
-                        f[1] = make_float2(__uint_as_float(u.z), __uint_as_float(u.w));
-                        f[2] = f[3] = make_float2(0.f, 0.f);
-                    }
-                    bad |= any_nonfinite<4>(f);
-                }
-                gbad[i] = bad ? 1 : 0;
-                if (bad) s_bad = 1;
-            }
-            __syncthreads();
-        }
+    const int per_thread = (tp.chunk + nthr - 1) / nthr;
+    for (int c0 = s_begin; c0 < s_end; c0 += tp.chunk) {
+        const int nc = min(tp.chunk, s_end - c0);
+        __syncthreads();  // the previous chunk is drained (its ids and bins are free)
+        for (int j = tid; j < nc; j += nthr) ids[j] = __ldg(slist + c0 + j);
+        __syncthreads();
         unsigned pending = 0;
-        for (int i = 0; i < max_per_thread; ++i) {
-            const int sidx = tid + i * nthr;
-            if (sidx < nq * P) pending |= file(c, sidx, 0xFu) << (4 * i);
+        for (int i = 0; i < per_thread; ++i) {
+            const int j = tid + i * nthr;
+            if (j < nc) pending |= file(j, 0xFu) << (4 * i);
         }
         bool again = __syncthreads_or(pending != 0u);
-        own(c);
+        own();
         for (int round = 0; again && round < 65536; ++round) {  // full bins: refile what did not fit
             __syncthreads();
             unsigned left = 0;
-            for (int i = 0; i < max_per_thread; ++i) {
-                const int sidx = tid + i * nthr;
+            for (int i = 0; i < per_thread; ++i) {
+                const int j = tid + i * nthr;
                 const unsigned want = (pending >> (4 * i)) & 0xFu;
-                if (want && sidx < nq * P) left |= file(c, sidx, want) << (4 * i);
+                if (want && j < nc) left |= file(j, want) << (4 * i);
             }
             pending = left;
             again = __syncthreads_or(pending != 0u);
-            own(c);
+            own();
         }
     }
-    if (owner) {
+    // Replicas r > 0 hand their accumulators to replica 0 through shared memory (the bins are no
+    // longer needed), which adds them in replica order.
+    AT *red = reinterpret_cast<AT *>(smem + tp.o_bins);
+    if (R > 1) {
+        __syncthreads();
+        if (owner && rep > 0) {
+#pragma unroll
+            for (int i = 0; i < CPT; ++i) red[((size_t)(rep - 1) * npl + pl) * D + seg * CPT + i] = acc[i];
+        }
+        __syncthreads();
+        if (owner && rep == 0) {
+            for (int r = 1; r < R; ++r) {
+#pragma unroll
+                for (int i = 0; i < CPT; ++i) acc[i] += red[((size_t)(r - 1) * npl + pl) * D + seg * CPT + i];
+            }
+        }
+    }
+    if (owner && rep == 0) {
         TV *dst = grad_value + (slab_rows + ls + p0 + pl) * D + seg * CPT;
         float f[CPT];
 #pragma unroll
@@ -2414,23 +2479,25 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
 }
 
 // K2: weight and location gradients of every sample from its corners' G.
-template <typename TV, typename TW>
+template <typename TV, typename TW, int P>
 __global__ void __launch_bounds__(256)
 msda_backward_finish_kernel(const TV *__restrict__ value, const float *__restrict__ loc, const TW *__restrict__ attn,
                             const typename OutOf<TV, TW>::T *__restrict__ grad_out,
                             const typename AccOf<TV>::T *__restrict__ gcorner, const int *__restrict__ flags,
                             float *__restrict__ grad_loc, TW *__restrict__ grad_attn, const Geom g) {
     using AT = typename AccOf<TV>::T;
-    const long long total = (long long)g.B * g.Lq * g.H * g.L * g.P;
+    constexpr int PS = P == 1 ? 0 : P == 2 ? 1 : P == 4 ? 2 : 3;
+    __shared__ LevelTable lv;
+    load_levels(lv, g);
+    __syncthreads();
+    // Sample indices fit in 31 bits (validated), so the decoding below is 32-bit arithmetic.
+    const int total = g.B * g.Lq * g.H * g.L * P;
+    const int LP = g.L * P;
     const float qnan = __int_as_float(0x7fc00000);
-    for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < total;
-         s += (long long)gridDim.x * blockDim.x) {
-        const int p = (int)(s % g.P);
-        const int l = (int)((s / g.P) % g.L);
-        const long long row = s / ((long long)g.L * g.P);  // (b, q, h)
-        const int h = (int)(row % g.H);
-        const int b = (int)(row / ((long long)g.Lq * g.H));
-        const int W = select_level(g.lw, l), Hh = select_level(g.lh, l), ls = select_level(g.ls, l);
+    for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < total; s += gridDim.x * blockDim.x) {
+        const int row = s / LP;  // (b, q, h)
+        const int l = (s - row * LP) >> PS;
+        const int W = lv.w[l], Hh = lv.h[l];
         const float Wf = (float)W, Hf = (float)Hh;
         const float2 xy = __ldg(reinterpret_cast<const float2 *>(loc) + s);
         const float a = to_f32(__ldg(attn + s));
@@ -2444,19 +2511,22 @@ msda_backward_finish_kernel(const TV *__restrict__ value, const float *__restric
             const float m[4] = {t.m00, t.m10, t.m01, t.m11};
             AT e[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) e[k] = m[k] != 0.f ? __ldg(gcorner + s * 4 + k) : (AT)0;
-            const int bh = b * g.H + h;
-            if ((m[0] == 0.f || m[1] == 0.f || m[2] == 0.f || m[3] == 0.f) && __ldg(flags + bh)) {
-                // Out-of-range corners: m * (v . g), NaN when the clipped row or g is not finite.
-                const int pp[4] = {t.p00, t.p10, t.p01, t.p11};
-                const auto *grow = grad_out + row * g.D;
+            for (int k = 0; k < 4; ++k) e[k] = m[k] != 0.f ? __ldg(gcorner + (size_t)s * 4 + k) : (AT)0;
+            if (m[0] == 0.f || m[1] == 0.f || m[2] == 0.f || m[3] == 0.f) {
+                const int b = row / (g.Lq * g.H), h = row - (row / g.H) * g.H;
+                const int bh = b * g.H + h;
+                if (__ldg(flags + bh)) {
+                    // Out-of-range corners: m * (v . g), NaN when the clipped row or g is not finite.
+                    const int pp[4] = {t.p00, t.p10, t.p01, t.p11};
+                    const auto *grow = grad_out + (size_t)row * g.D;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    if (m[k] != 0.f) continue;
-                    const TV *vrow = value + ((size_t)bh * g.Lv + ls + pp[k]) * g.D;
-                    AT d = 0;
-                    for (int ch = 0; ch < g.D; ++ch) d += (AT)to_f32(vrow[ch]) * (AT)to_f32(grow[ch]);
-                    e[k] = (AT)0 * d;
+                    for (int k = 0; k < 4; ++k) {
+                        if (m[k] != 0.f) continue;
+                        const TV *vrow = value + ((size_t)bh * g.Lv + lv.s[l] + pp[k]) * g.D;
+                        AT d = 0;
+                        for (int ch = 0; ch < g.D; ++ch) d += (AT)to_f32(vrow[ch]) * (AT)to_f32(grow[ch]);
+                        e[k] = (AT)0 * d;
+                    }
                 }
             }
             const AT wx1 = t.wx1, wy1 = t.wy1, wx0 = (AT)1 - wx1, wy0 = (AT)1 - wy1;
@@ -2471,11 +2541,13 @@ msda_backward_finish_kernel(const TV *__restrict__ value, const float *__restric
     }
 }
 
-// Host planning of the tile backward.  Returns false when the shape or alignment does not fit.
+// Host planning of the tile backward (one plan for every level).  Returns false when the shape or
+// alignment does not fit.
 template <typename TV, typename TW>
 bool plan_backward_tiles(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
                          const void *grad_value, int optin, TilePlan &tp, int &cpt) {
     using TG = typename OutOf<TV, TW>::T;
+    using AT = typename AccOf<TV>::T;
     if (!(g.P == 1 || g.P == 2 || g.P == 4 || g.P == 8)) return false;
     cpt = sizeof(TV) == 2 ? 16 : 8;
     if (g.D % cpt != 0 && sizeof(TV) == 2 && g.D % 8 == 0) cpt = 8;
@@ -2488,94 +2560,134 @@ bool plan_backward_tiles(const Geom &g, const void *value, const float *loc, con
     if (((size_t)g.D * sizeof(TG)) % 16 != 0) return false;
     const Tune tune = read_tune(kKnobMsdaTiles);
     if (tune.stage == 0) return false;
-    // Positions per tile: up to 512 threads' worth, balanced within each level.
-    const int np_max = std::max(1, (tune.threads > 0 ? tune.threads : 512) / tp.segs);
-    int npl_max = 1, total_tiles = 0;
+    const int nthr_max = tune.threads > 0 ? std::min(tune.threads, kTileThreadsMax) : kTileThreadsMax;
+    const int np_max = std::max(1, nthr_max / tp.segs);
+    int npl_max = 1, total_tiles = 0, roff = 0;
     for (int l = 0; l < g.L; ++l) {
         const int hw = g.lh[l] * g.lw[l];
+        if (g.lh[l] > kTileMaxRows) return false;
         const int nt = (hw + np_max - 1) / np_max;
         tp.np[l] = (hw + nt - 1) / nt;
         tp.tiles_before[l] = total_tiles;
+        tp.roff[l] = roff;
+        roff += g.lh[l] + 3;
         total_tiles += nt;
         npl_max = std::max(npl_max, tp.np[l]);
     }
     for (int l = g.L; l < kMaxLevels; ++l) {
         tp.np[l] = 1;
         tp.tiles_before[l] = total_tiles;
+        tp.roff[l] = roff;
         tp.cap[l] = 1;
-        tp.staged[l] = 0;
+        tp.rep[l] = 1;
     }
     tp.tiles_before[kMaxLevels] = total_tiles;
+    tp.roff[kMaxLevels] = roff;
     if (total_tiles > 65535 || (long long)g.B * g.H > 65535) return false;
     tp.nthr = ((npl_max * tp.segs + 31) / 32) * 32;
     if (tp.nthr > kTileThreadsMax) return false;
-    tp.tq = std::max(1, std::min(g.Lq, 2 * tp.nthr / g.P));
-    tp.tq = std::min(tp.tq, 8192 / g.P);
-    auto granule = [](long long seg, const void *base) -> int {
-        for (int gsz = 16; gsz >= 4; gsz >>= 1)
-            if (seg % gsz == 0 && aligned(base, gsz)) return gsz;
-        return 0;
-    };
-    tp.gl = granule((long long)g.P * 8, loc);
-    tp.ga = granule((long long)g.P * sizeof(TW), attn);
-    // Bins: records per position per chunk follow a Poisson law around tq * P * 4 / HW; the cap
-    // leaves room for ~4 standard deviations (a full bin is refiled, so any pattern is exact).
-    size_t bins_bytes = 0;
-    bool any_staged = false;
+    // Replica owners for levels whose tile leaves threads idle and whose positions collect many
+    // records: up to as many replicas as fit the CTA.
     for (int l = 0; l < g.L; ++l) {
-        const int hw = g.lh[l] * g.lw[l];
-        const double per_query = (double)g.P * 4.0 / hw;
-        const double mean = per_query * tp.tq;
-        tp.staged[l] = (tune.acc != 0) && per_query * g.Lq >= 4.0;
-        any_staged |= tp.staged[l] != 0;
-        int cap = (int)std::ceil(mean + 4.0 * std::sqrt(mean) + 4.0);
-        cap = std::max(4, std::min(cap, tune.hsub > 0 ? tune.hsub : 64));
-        tp.cap[l] = cap;
-        bins_bytes = std::max(bins_bytes, (size_t)cap * tp.np[l] * 6);
+        const int fit = tp.nthr / (tp.np[l] * tp.segs);
+        const double records = (double)g.P * 4.0 * g.Lq / (g.lh[l] * g.lw[l]);
+        int r = 1;
+        while (r * 2 <= std::min(fit, kTileMaxReplicas) && records >= 16.0 * r) r *= 2;
+        tp.rep[l] = r;
     }
-    auto r16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
     tp.gstride = g.D * (int)sizeof(TG) + 16;
+    auto r16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
+    // Bins: records per position per chunk follow a Poisson law around (chunk samples of the
+    // tile's row band) * 4 / (band positions); the cap leaves room for ~4 standard deviations (a
+    // full bin is refiled, so any sampling pattern stays exact).  The chunk is the largest of
+    // 8, 4, 2 or 1 samples per thread with which the slab's gradient rows can be staged and the
+    // CTA still fits two to an SM; when none can, 4 per thread and rows read from L2.
+    const size_t two_per_sm = std::min<size_t>((size_t)optin, 113 * 1024);
+    const size_t gbytes = r16((size_t)g.Lq * tp.gstride);
+    auto fixed_bytes = [&](int chunk) {
+        size_t bins_bytes = 0;
+        for (int l = 0; l < g.L; ++l) {
+            const int hw = g.lh[l] * g.lw[l];
+            const double band = std::min<double>(g.lh[l], (double)tp.np[l] / g.lw[l] + 2.0);
+            const double in_band = std::min<double>((double)chunk, (double)g.Lq * g.P * band / g.lh[l]);
+            const double mean = in_band * 4.0 / std::min<double>(band * g.lw[l], hw);
+            int cap = (int)std::ceil(mean + 4.0 * std::sqrt(mean) + 4.0);
+            cap = std::max(4, std::min(cap, tune.hsub > 0 ? tune.hsub : 96));
+            tp.cap[l] = cap;
+            bins_bytes = std::max(bins_bytes, (size_t)cap * tp.np[l] * 6);
+            bins_bytes = std::max(bins_bytes, (size_t)(tp.rep[l] - 1) * tp.np[l] * g.D * sizeof(AT));
+        }
+        return r16((size_t)chunk * 4) + r16((size_t)npl_max * 4) + r16(bins_bytes);
+    };
+    tp.stage_g = 0;
+    tp.chunk = 0;
+    if (tune.acc != 0) {
+        for (int per = kTileMaxPerThread; per >= 1 && !tp.chunk; per /= 2) {
+            const int chunk = per * tp.nthr;
+            if (fixed_bytes(chunk) + gbytes <= two_per_sm) {
+                tp.chunk = chunk;
+                tp.stage_g = 1;
+            }
+        }
+    }
+    if (!tp.chunk) tp.chunk = 4 * tp.nthr;
+    const size_t fixed = fixed_bytes(tp.chunk);  // sets the caps of the chosen chunk
     size_t o = 0;
-    tp.loc_sz = any_staged ? (unsigned)r16((size_t)tp.tq * g.P * 8) : 0;
-    tp.o_loc = (unsigned)o; o += 2 * (size_t)tp.loc_sz;
-    tp.attn_sz = any_staged ? (unsigned)r16((size_t)tp.tq * g.P * sizeof(TW)) : 0;
-    tp.o_attn = (unsigned)o; o += 2 * (size_t)tp.attn_sz;
-    tp.g_sz = any_staged ? (unsigned)r16((size_t)tp.tq * tp.gstride) : 0;
-    tp.o_g = (unsigned)o; o += 2 * (size_t)tp.g_sz;
-    tp.o_gbad = (unsigned)o; o += r16(any_staged ? (size_t)tp.tq : 0);
-    tp.o_cnt = (unsigned)o; o += r16((size_t)npl_max * 4);
-    tp.o_bins = (unsigned)o; o += r16(bins_bytes);
+    tp.o_g = (unsigned)o; o += tp.stage_g ? gbytes : 0;
+    tp.o_ids = (unsigned)o;
+    tp.o_cnt = (unsigned)(tp.o_ids + r16((size_t)tp.chunk * 4));
+    tp.o_bins = (unsigned)(tp.o_cnt + r16((size_t)npl_max * 4));
+    o += fixed;
     tp.smem = o;
-    if (!tp.gl || !tp.ga) return false;
     return tp.smem <= (size_t)optin;
 }
 
-// Workspace of the tile backward: the per-corner G array and the per-slab flags.
-size_t tile_workspace_bytes(int value_dtype, const Geom &g) {
+// Workspace of the tile backward: the per-corner G array, the per-slab flags, the row-sorted
+// sample lists and their row offsets.
+struct TileWs {
+    size_t o_flags, o_list, o_roff, bytes;
+};
+TileWs tile_workspace(int value_dtype, const Geom &g) {
+    auto r256 = [](size_t x) { return (x + 255) & ~(size_t)255; };
     const size_t gsize = value_dtype == RFDETR_F32 ? sizeof(double) : sizeof(float);
-    const size_t corners = (size_t)g.B * g.Lq * g.H * g.L * g.P * 4;
-    return ((corners * gsize + 255) & ~(size_t)255) + (size_t)g.B * g.H * sizeof(int);
+    const size_t samples = (size_t)g.B * g.Lq * g.H * g.L * g.P;
+    size_t rows = 0;
+    for (int l = 0; l < g.L; ++l) rows += g.lh[l] + 3;
+    TileWs w;
+    w.o_flags = r256(samples * 4 * gsize);
+    w.o_list = w.o_flags + r256((size_t)g.B * g.H * sizeof(int));
+    w.o_roff = w.o_list + r256(samples * sizeof(int));
+    w.bytes = w.o_roff + r256((size_t)g.B * g.H * rows * sizeof(int));
+    return w;
 }
+size_t tile_workspace_bytes(int value_dtype, const Geom &g) { return tile_workspace(value_dtype, g).bytes; }
 
 template <typename TV, typename TW, int P, int CPT>
 int launch_backward_tiles_k(const Geom &g, const TilePlan &tp, const void *value, const float *loc, const void *attn,
-                            const void *gout, void *gv, float *gl, void *ga, void *ws, cudaStream_t s) {
+                            const void *gout, void *gv, float *gl, void *ga, void *ws, int value_dtype,
+                            cudaStream_t s) {
     using TG = typename OutOf<TV, TW>::T;
     using AT = typename AccOf<TV>::T;
-    const size_t corners = (size_t)g.B * g.Lq * g.H * g.L * g.P * 4;
-    AT *gcorner = static_cast<AT *>(ws);
-    int *flags = reinterpret_cast<int *>(static_cast<char *>(ws) + ((corners * sizeof(AT) + 255) & ~(size_t)255));
+    const TileWs w = tile_workspace(value_dtype, g);
+    char *base = static_cast<char *>(ws);
+    AT *gcorner = reinterpret_cast<AT *>(base);
+    int *flags = reinterpret_cast<int *>(base + w.o_flags);
+    int *list = reinterpret_cast<int *>(base + w.o_list);
+    int *roffs = reinterpret_cast<int *>(base + w.o_roff);
     if (cudaMemsetAsync(flags, 0, (size_t)g.B * g.H * sizeof(int), s) != cudaSuccess) return RFDETR_ERR_CUDA;
+    msda_backward_rowsort_kernel<P><<<dim3((unsigned)g.L, (unsigned)(g.B * g.H)), 512, 0, s>>>(loc, list, roffs, g, tp);
+    if (launch_status() != RFDETR_OK) return RFDETR_ERR_CUDA;
     auto k1 = msda_backward_tile_kernel<TV, TW, P, CPT>;
     if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tp.smem) != cudaSuccess)
         return RFDETR_ERR_CUDA;
     const dim3 grid((unsigned)tp.tiles_before[kMaxLevels], (unsigned)(g.B * g.H));
     k1<<<grid, tp.nthr, tp.smem, s>>>(static_cast<const TV *>(value), loc, static_cast<const TW *>(attn),
-                                       static_cast<const TG *>(gout), static_cast<TV *>(gv), gcorner, flags, g, tp);
+                                       static_cast<const TG *>(gout), static_cast<TV *>(gv), gcorner, flags, list, roffs,
+                                       g, tp);
     if (launch_status() != RFDETR_OK) return RFDETR_ERR_CUDA;
     const long long samples = (long long)g.B * g.Lq * g.H * g.L * g.P;
     const unsigned blocks = (unsigned)std::min<long long>((samples + 255) / 256, (long long)num_sms() * 16);
-    msda_backward_finish_kernel<TV, TW><<<std::max(blocks, 1u), 256, 0, s>>>(
+    msda_backward_finish_kernel<TV, TW, P><<<std::max(blocks, 1u), 256, 0, s>>>(
         static_cast<const TV *>(value), loc, static_cast<const TW *>(attn), static_cast<const TG *>(gout), gcorner,
         flags, gl, static_cast<TW *>(ga), g);
     return launch_status();
@@ -2590,7 +2702,7 @@ int try_backward_tiles(const Geom &g, const void *value, const float *loc, const
     if (!ws || ws_bytes < tile_workspace_bytes(value_dtype, g) || !aligned(ws, 256)) return -1;
     auto go = [&](auto p_tag, auto c_tag) {
         constexpr int PP = decltype(p_tag)::value, CC = decltype(c_tag)::value;
-        return launch_backward_tiles_k<TV, TW, PP, CC>(g, tp, value, loc, attn, gout, gv, gl, ga, ws, s);
+        return launch_backward_tiles_k<TV, TW, PP, CC>(g, tp, value, loc, attn, gout, gv, gl, ga, ws, value_dtype, s);
     };
     using I1 = std::integral_constant<int, 1>;
     using I2 = std::integral_constant<int, 2>;
