@@ -2127,17 +2127,23 @@ constexpr int kTileMaxReplicas = 8;
 struct TilePlan {
     int segs;                          // threads per position (D / CPT)
     int chunk;                         // samples per chunk (<= kTileMaxPerThread * threads)
-    int tiles_before[kMaxLevels + 1];  // first tile of each level (per slab)
+    int tiles_before[kMaxLevels + 1];  // first CTA of each level (per slab): tiles x splits
     int np[kMaxLevels];                // positions per tile, per level
     int cap[kMaxLevels];               // bin slots per position, per level
     int rep[kMaxLevels];               // replica owners per position, per level
-    int stage_g;                       // the slab's gradient rows are staged in shared memory
+    int split[kMaxLevels];             // CTAs sharing a tile's samples (partial sums reduced after)
+    int stage[kMaxLevels];             // the slab's gradient rows are staged in shared memory
+    int part[kMaxLevels + 1];          // first partial-sum row of each level (per slab; S rows a position)
+    int ppos[kMaxLevels + 1];          // first split-level position of each level (per slab)
     int gstride;                       // staged gradient row stride, bytes
     int roff[kMaxLevels + 1];          // first row-offset entry of each level (per slab)
     unsigned o_g, o_ids, o_cnt, o_bins;
     size_t smem;
     int nthr;
 };
+
+// Per-level fields of a TilePlan and a Geom, copied to shared memory once per CTA.
+enum { kLvW, kLvH, kLvS, kLvNp, kLvCap, kLvRep, kLvSplit, kLvStage, kLvTiles, kLvRoff, kLvPart, kLvFields };
 
 template <int N>
 __device__ __forceinline__ int select_level(const int (&a)[N], int l) {
@@ -2211,25 +2217,46 @@ __global__ void __launch_bounds__(kTileThreadsMax, RFDETR_TILE_MIN_BLOCKS)
 msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict__ loc, const TW *__restrict__ attn,
                           const typename OutOf<TV, TW>::T *__restrict__ grad_out, TV *__restrict__ grad_value,
                           typename AccOf<TV>::T *__restrict__ gcorner, int *__restrict__ flags,
-                          const int *__restrict__ list, const int *__restrict__ roffs, const Geom g, const TilePlan tp) {
+                          const int *__restrict__ list, const int *__restrict__ roffs,
+                          typename AccOf<TV>::T *__restrict__ partial, const Geom g, const TilePlan tp) {
     using TG = typename OutOf<TV, TW>::T;
     using AT = typename AccOf<TV>::T;
     constexpr int PS = P == 1 ? 0 : P == 2 ? 1 : P == 4 ? 2 : 3;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int s_bad;
+    __shared__ int lvt[kMaxLevels][kLvFields];
+    if (threadIdx.x < g.L) {
+        const int i = threadIdx.x;
+        lvt[i][kLvW] = g.lw[i];
+        lvt[i][kLvH] = g.lh[i];
+        lvt[i][kLvS] = g.ls[i];
+        lvt[i][kLvNp] = tp.np[i];
+        lvt[i][kLvCap] = tp.cap[i];
+        lvt[i][kLvRep] = tp.rep[i];
+        lvt[i][kLvSplit] = tp.split[i];
+        lvt[i][kLvStage] = tp.stage[i];
+        lvt[i][kLvTiles] = tp.tiles_before[i];
+        lvt[i][kLvRoff] = tp.roff[i];
+        lvt[i][kLvPart] = tp.part[i];
+    }
+    __syncthreads();
     const int bh = blockIdx.y;
     const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
-    const int tile = blockIdx.x;
+    const int cta = blockIdx.x;
     int l = 0;
     for (int i = 1; i < g.L; ++i)
-        if (select_level(tp.tiles_before, i) <= tile) l = i;
-    const int W = select_level(g.lw, l), Hh = select_level(g.lh, l), ls = select_level(g.ls, l);
+        if (lvt[i][kLvTiles] <= cta) l = i;
+    const int W = lvt[l][kLvW], Hh = lvt[l][kLvH], ls = lvt[l][kLvS];
     const float Wf = (float)W, Hf = (float)Hh;
-    const int npl = select_level(tp.np, l);
-    const int p0 = (tile - select_level(tp.tiles_before, l)) * npl;
+    const int npl = lvt[l][kLvNp];
+    const int S = lvt[l][kLvSplit];
+    const int local = cta - lvt[l][kLvTiles];
+    const int tl = local / S, sp = local - (local / S) * S;
+    const int p0 = tl * npl;
     const int np = min(npl, W * Hh - p0);
-    const int cap = select_level(tp.cap, l);
-    const int R = select_level(tp.rep, l);
+    const int cap = lvt[l][kLvCap];
+    const int R = lvt[l][kLvRep];
+    const bool stage_g = lvt[l][kLvStage] != 0;
     const int row_lo = p0 / W, row_hi = (p0 + np - 1) / W;
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int segs = tp.segs;
@@ -2246,15 +2273,18 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
     int *const ids = reinterpret_cast<int *>(smem + tp.o_ids);
     unsigned char *const gst = smem + tp.o_g;
 
-    // The tile's samples: keys [row_lo, row_hi + 1] of the level's row-sorted list.
-    const int *ro = roffs + (size_t)bh * tp.roff[kMaxLevels] + select_level(tp.roff, l);
-    const int s_begin = __ldg(ro + max(row_lo, 0)), s_end = __ldg(ro + min(row_hi + 1, Hh) + 1);
+    // The tile's samples: keys [row_lo, row_hi + 1] of the level's row-sorted list; split CTAs
+    // take equal shares of that range.
+    const int *ro = roffs + (size_t)bh * tp.roff[kMaxLevels] + lvt[l][kLvRoff];
+    const int r_begin = __ldg(ro + max(row_lo, 0)), r_end = __ldg(ro + min(row_hi + 1, Hh) + 1);
+    const int s_begin = r_begin + (int)(((long long)(r_end - r_begin) * sp) / S);
+    const int s_end = r_begin + (int)(((long long)(r_end - r_begin) * (sp + 1)) / S);
     const int *slist = list + ((size_t)bh * g.L + l) * (g.Lq * P);
 
     if (tid == 0) s_bad = 0;
     for (int i = tid; i < npl; i += nthr) counts[i] = 0;
-    // The slab's gradient rows, staged once (all queries), when they fit.
-    if (tp.stage_g) {
+    // The slab's gradient rows, staged once (all queries), for dense levels.
+    if (stage_g) {
         const int gch = D * (int)sizeof(TG) / 16;
         for (int i = tid; i < g.Lq * gch; i += nthr) {
             const int q = i / gch, j = i - (i / gch) * gch;
@@ -2318,7 +2348,7 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
         }
     };
     auto g_row = [&](int q, int chan) -> const uint4 * {
-        if (tp.stage_g) return reinterpret_cast<const uint4 *>(gst + (size_t)q * tp.gstride + chan * sizeof(TG));
+        if (stage_g) return reinterpret_cast<const uint4 *>(gst + (size_t)q * tp.gstride + chan * sizeof(TG));
         return reinterpret_cast<const uint4 *>(grad_out + (((size_t)b * g.Lq + q) * g.H + h) * D + chan);
     };
     // True when the gradient row of query q holds inf/NaN.
@@ -2326,7 +2356,7 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
         bool bad = false;
         for (int k = 0; k < D; k += CPT) {
             float2 x[NV];
-            to_pairs(g_row(q, k), x, !tp.stage_g);
+            to_pairs(g_row(q, k), x, !stage_g);
             bad |= any_nonfinite<NV>(x);
         }
         return bad;
@@ -2393,7 +2423,7 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
             const int id = ids[j];
             const int q = id >> PS, p = id & (P - 1);
             float2 qv[NV];
-            to_pairs(g_row(q, seg * CPT), qv, !tp.stage_g);
+            to_pairs(g_row(q, seg * CPT), qv, !stage_g);
             AT dot;
             if constexpr (sizeof(TV) == 2) {
                 const float2 cc = make_float2(cfe, cfe);
@@ -2468,14 +2498,44 @@ msda_backward_tile_kernel(const TV *__restrict__ value, const float *__restrict_
         }
     }
     if (owner && rep == 0) {
-        TV *dst = grad_value + (slab_rows + ls + p0 + pl) * D + seg * CPT;
-        float f[CPT];
+        if (S == 1) {
+            TV *dst = grad_value + (slab_rows + ls + p0 + pl) * D + seg * CPT;
+            float f[CPT];
 #pragma unroll
-        for (int i = 0; i < CPT; ++i) f[i] = (float)acc[i];
-        store_vec<TV, CPT>(dst, f);
+            for (int i = 0; i < CPT; ++i) f[i] = (float)acc[i];
+            store_vec<TV, CPT>(dst, f);
+        } else {
+            // Partial sum of this split: row (level partial base + position) * S + split.
+            AT *dst = partial + ((size_t)bh * tp.part[kMaxLevels] + lvt[l][kLvPart] + (size_t)(p0 + pl) * S + sp) * D +
+                      seg * CPT;
+#pragma unroll
+            for (int i = 0; i < CPT; ++i) dst[i] = acc[i];
+        }
     }
     __syncthreads();
     if (tid == 0 && s_bad) atomicOr(flags + bh, 1);
+}
+
+// Sums the split partials of the split levels in split order and writes grad_value.
+template <typename TV>
+__global__ void __launch_bounds__(256)
+msda_backward_split_reduce_kernel(const typename AccOf<TV>::T *__restrict__ partial, TV *__restrict__ grad_value,
+                                  const Geom g, const TilePlan tp) {
+    using AT = typename AccOf<TV>::T;
+    const int bh = blockIdx.y;
+    const int positions = tp.ppos[kMaxLevels];
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < positions * g.D; i += gridDim.x * blockDim.x) {
+        const int r = i / g.D, ch = i - (i / g.D) * g.D;
+        int l = 0;
+        for (int k = 1; k < g.L; ++k)
+            if (tp.ppos[k] <= r) l = k;
+        const int S = tp.split[l];
+        const int pos = r - tp.ppos[l];
+        const AT *src = partial + ((size_t)bh * tp.part[kMaxLevels] + tp.part[l] + (size_t)pos * S) * g.D + ch;
+        AT sum = src[0];
+        for (int k = 1; k < S; ++k) sum += src[(size_t)k * g.D];
+        grad_value[((size_t)bh * g.Lv + g.ls[l] + pos) * g.D + ch] = from_f32<TV>((float)sum);
+    }
 }
 
 // K2: weight and location gradients of every sample from its corners' G.
@@ -2558,58 +2618,81 @@ bool plan_backward_tiles(const Geom &g, const void *value, const float *loc, con
         !aligned(attn, sizeof(TW)))
         return false;
     if (((size_t)g.D * sizeof(TG)) % 16 != 0) return false;
+    // Opt-in (the knob's second field set to 1): at config 3 this path measured 192 us (bf16) and
+    // 280 us (float32) against 104 / 106 us for the accumulate kernel, so it is not the default.
     const Tune tune = read_tune(kKnobMsdaTiles);
-    if (tune.stage == 0) return false;
+    if (tune.stage != 1) return false;
     const int nthr_max = tune.threads > 0 ? std::min(tune.threads, kTileThreadsMax) : kTileThreadsMax;
     const int np_max = std::max(1, nthr_max / tp.segs);
-    int npl_max = 1, total_tiles = 0, roff = 0;
+    int npl_max = 1;
     for (int l = 0; l < g.L; ++l) {
         const int hw = g.lh[l] * g.lw[l];
         if (g.lh[l] > kTileMaxRows) return false;
         const int nt = (hw + np_max - 1) / np_max;
         tp.np[l] = (hw + nt - 1) / nt;
-        tp.tiles_before[l] = total_tiles;
-        tp.roff[l] = roff;
-        roff += g.lh[l] + 3;
-        total_tiles += nt;
         npl_max = std::max(npl_max, tp.np[l]);
     }
-    for (int l = g.L; l < kMaxLevels; ++l) {
-        tp.np[l] = 1;
-        tp.tiles_before[l] = total_tiles;
-        tp.roff[l] = roff;
-        tp.cap[l] = 1;
-        tp.rep[l] = 1;
-    }
-    tp.tiles_before[kMaxLevels] = total_tiles;
-    tp.roff[kMaxLevels] = roff;
-    if (total_tiles > 65535 || (long long)g.B * g.H > 65535) return false;
     tp.nthr = ((npl_max * tp.segs + 31) / 32) * 32;
     if (tp.nthr > kTileThreadsMax) return false;
-    // Replica owners for levels whose tile leaves threads idle and whose positions collect many
-    // records: up to as many replicas as fit the CTA.
+    // Dense levels (many records per position): replica owners where the tile leaves threads
+    // idle, then splits of the tile's samples over several CTAs so that an owner drains about 16
+    // records; their gradient rows are staged.
+    int total = 0, roff = 0, part = 0, ppos = 0;
     for (int l = 0; l < g.L; ++l) {
+        const int hw = g.lh[l] * g.lw[l];
+        const double records = (double)g.P * 4.0 * g.Lq / hw;
         const int fit = tp.nthr / (tp.np[l] * tp.segs);
-        const double records = (double)g.P * 4.0 * g.Lq / (g.lh[l] * g.lw[l]);
         int r = 1;
         while (r * 2 <= std::min(fit, kTileMaxReplicas) && records >= 16.0 * r) r *= 2;
         tp.rep[l] = r;
+        int sp = 1;
+        while (sp < 16 && records / (r * sp) > 24.0) sp *= 2;
+        tp.split[l] = sp;
+        tp.stage[l] = tune.acc != 0 && records >= 4.0;
+        tp.tiles_before[l] = total;
+        total += ((hw + tp.np[l] - 1) / tp.np[l]) * sp;
+        tp.roff[l] = roff;
+        roff += g.lh[l] + 3;
+        tp.part[l] = part;
+        tp.ppos[l] = ppos;
+        if (sp > 1) {
+            part += hw * sp;
+            ppos += hw;
+        }
     }
+    for (int l = g.L; l < kMaxLevels; ++l) {
+        tp.np[l] = 1;
+        tp.tiles_before[l] = total;
+        tp.roff[l] = roff;
+        tp.part[l] = part;
+        tp.ppos[l] = ppos;
+        tp.cap[l] = 1;
+        tp.rep[l] = 1;
+        tp.split[l] = 1;
+        tp.stage[l] = 0;
+    }
+    tp.tiles_before[kMaxLevels] = total;
+    tp.roff[kMaxLevels] = roff;
+    tp.part[kMaxLevels] = part;
+    tp.ppos[kMaxLevels] = ppos;
+    if (total > 65535 || (long long)g.B * g.H > 65535) return false;
     tp.gstride = g.D * (int)sizeof(TG) + 16;
     auto r16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
     // Bins: records per position per chunk follow a Poisson law around (chunk samples of the
     // tile's row band) * 4 / (band positions); the cap leaves room for ~4 standard deviations (a
     // full bin is refiled, so any sampling pattern stays exact).  The chunk is the largest of
-    // 8, 4, 2 or 1 samples per thread with which the slab's gradient rows can be staged and the
-    // CTA still fits two to an SM; when none can, 4 per thread and rows read from L2.
+    // 8, 4, 2 or 1 samples per thread that keeps the CTA two to an SM with the staged rows.
     const size_t two_per_sm = std::min<size_t>((size_t)optin, 113 * 1024);
-    const size_t gbytes = r16((size_t)g.Lq * tp.gstride);
+    bool any_stage = false;
+    for (int l = 0; l < g.L; ++l) any_stage |= tp.stage[l] != 0;
+    const size_t gbytes = any_stage ? r16((size_t)g.Lq * tp.gstride) : 0;
     auto fixed_bytes = [&](int chunk) {
         size_t bins_bytes = 0;
         for (int l = 0; l < g.L; ++l) {
             const int hw = g.lh[l] * g.lw[l];
             const double band = std::min<double>(g.lh[l], (double)tp.np[l] / g.lw[l] + 2.0);
-            const double in_band = std::min<double>((double)chunk, (double)g.Lq * g.P * band / g.lh[l]);
+            const double in_band =
+                std::min<double>((double)chunk, (double)g.Lq * g.P * band / g.lh[l] / tp.split[l]);
             const double mean = in_band * 4.0 / std::min<double>(band * g.lw[l], hw);
             int cap = (int)std::ceil(mean + 4.0 * std::sqrt(mean) + 4.0);
             cap = std::max(4, std::min(cap, tune.hsub > 0 ? tune.hsub : 96));
@@ -2619,21 +2702,19 @@ bool plan_backward_tiles(const Geom &g, const void *value, const float *loc, con
         }
         return r16((size_t)chunk * 4) + r16((size_t)npl_max * 4) + r16(bins_bytes);
     };
-    tp.stage_g = 0;
     tp.chunk = 0;
-    if (tune.acc != 0) {
-        for (int per = kTileMaxPerThread; per >= 1 && !tp.chunk; per /= 2) {
-            const int chunk = per * tp.nthr;
-            if (fixed_bytes(chunk) + gbytes <= two_per_sm) {
-                tp.chunk = chunk;
-                tp.stage_g = 1;
-            }
-        }
+    for (int per = kTileMaxPerThread; per >= 1 && !tp.chunk; per /= 2)
+        if (fixed_bytes(per * tp.nthr) + gbytes <= two_per_sm) tp.chunk = per * tp.nthr;
+    if (!tp.chunk) {
+        // The staged rows do not fit beside the bins: read them from L2 instead.
+        for (int l = 0; l < g.L; ++l) tp.stage[l] = 0;
+        tp.chunk = 4 * tp.nthr;
     }
-    if (!tp.chunk) tp.chunk = 4 * tp.nthr;
     const size_t fixed = fixed_bytes(tp.chunk);  // sets the caps of the chosen chunk
+    bool staged = false;
+    for (int l = 0; l < g.L; ++l) staged |= tp.stage[l] != 0;
     size_t o = 0;
-    tp.o_g = (unsigned)o; o += tp.stage_g ? gbytes : 0;
+    tp.o_g = (unsigned)o; o += staged ? gbytes : 0;
     tp.o_ids = (unsigned)o;
     tp.o_cnt = (unsigned)(tp.o_ids + r16((size_t)tp.chunk * 4));
     tp.o_bins = (unsigned)(tp.o_cnt + r16((size_t)npl_max * 4));
@@ -2645,9 +2726,10 @@ bool plan_backward_tiles(const Geom &g, const void *value, const float *loc, con
 // Workspace of the tile backward: the per-corner G array, the per-slab flags, the row-sorted
 // sample lists and their row offsets.
 struct TileWs {
-    size_t o_flags, o_list, o_roff, bytes;
+    size_t o_flags, o_list, o_roff, o_part, bytes;
 };
-TileWs tile_workspace(int value_dtype, const Geom &g) {
+// `split_rows`: partial-sum rows per slab (sum of the split levels' positions times their splits).
+TileWs tile_workspace(int value_dtype, const Geom &g, size_t split_rows) {
     auto r256 = [](size_t x) { return (x + 255) & ~(size_t)255; };
     const size_t gsize = value_dtype == RFDETR_F32 ? sizeof(double) : sizeof(float);
     const size_t samples = (size_t)g.B * g.Lq * g.H * g.L * g.P;
@@ -2657,10 +2739,11 @@ TileWs tile_workspace(int value_dtype, const Geom &g) {
     w.o_flags = r256(samples * 4 * gsize);
     w.o_list = w.o_flags + r256((size_t)g.B * g.H * sizeof(int));
     w.o_roff = w.o_list + r256(samples * sizeof(int));
-    w.bytes = w.o_roff + r256((size_t)g.B * g.H * rows * sizeof(int));
+    w.o_part = w.o_roff + r256((size_t)g.B * g.H * rows * sizeof(int));
+    w.bytes = w.o_part + r256((size_t)g.B * g.H * split_rows * g.D * gsize);
     return w;
 }
-size_t tile_workspace_bytes(int value_dtype, const Geom &g) { return tile_workspace(value_dtype, g).bytes; }
+size_t split_rows_of(const TilePlan &tp, const Geom &) { return (size_t)tp.part[kMaxLevels]; }
 
 template <typename TV, typename TW, int P, int CPT>
 int launch_backward_tiles_k(const Geom &g, const TilePlan &tp, const void *value, const float *loc, const void *attn,
@@ -2668,12 +2751,13 @@ int launch_backward_tiles_k(const Geom &g, const TilePlan &tp, const void *value
                             cudaStream_t s) {
     using TG = typename OutOf<TV, TW>::T;
     using AT = typename AccOf<TV>::T;
-    const TileWs w = tile_workspace(value_dtype, g);
+    const TileWs w = tile_workspace(value_dtype, g, split_rows_of(tp, g));
     char *base = static_cast<char *>(ws);
     AT *gcorner = reinterpret_cast<AT *>(base);
     int *flags = reinterpret_cast<int *>(base + w.o_flags);
     int *list = reinterpret_cast<int *>(base + w.o_list);
     int *roffs = reinterpret_cast<int *>(base + w.o_roff);
+    AT *partial = reinterpret_cast<AT *>(base + w.o_part);
     if (cudaMemsetAsync(flags, 0, (size_t)g.B * g.H * sizeof(int), s) != cudaSuccess) return RFDETR_ERR_CUDA;
     msda_backward_rowsort_kernel<P><<<dim3((unsigned)g.L, (unsigned)(g.B * g.H)), 512, 0, s>>>(loc, list, roffs, g, tp);
     if (launch_status() != RFDETR_OK) return RFDETR_ERR_CUDA;
@@ -2683,8 +2767,14 @@ int launch_backward_tiles_k(const Geom &g, const TilePlan &tp, const void *value
     const dim3 grid((unsigned)tp.tiles_before[kMaxLevels], (unsigned)(g.B * g.H));
     k1<<<grid, tp.nthr, tp.smem, s>>>(static_cast<const TV *>(value), loc, static_cast<const TW *>(attn),
                                        static_cast<const TG *>(gout), static_cast<TV *>(gv), gcorner, flags, list, roffs,
-                                       g, tp);
+                                       partial, g, tp);
     if (launch_status() != RFDETR_OK) return RFDETR_ERR_CUDA;
+    if (tp.ppos[kMaxLevels] > 0) {
+        const unsigned blocks = (unsigned)std::max(1, std::min(64, (tp.ppos[kMaxLevels] * g.D + 255) / 256));
+        msda_backward_split_reduce_kernel<TV><<<dim3(blocks, (unsigned)(g.B * g.H)), 256, 0, s>>>(
+            partial, static_cast<TV *>(gv), g, tp);
+        if (launch_status() != RFDETR_OK) return RFDETR_ERR_CUDA;
+    }
     const long long samples = (long long)g.B * g.Lq * g.H * g.L * g.P;
     const unsigned blocks = (unsigned)std::min<long long>((samples + 255) / 256, (long long)num_sms() * 16);
     msda_backward_finish_kernel<TV, TW, P><<<std::max(blocks, 1u), 256, 0, s>>>(
@@ -2699,7 +2789,7 @@ int try_backward_tiles(const Geom &g, const void *value, const float *loc, const
     TilePlan tp;
     int cpt = 0;
     if (!plan_backward_tiles<TV, TW>(g, value, loc, attn, gout, gv, max_smem_optin(), tp, cpt)) return -1;
-    if (!ws || ws_bytes < tile_workspace_bytes(value_dtype, g) || !aligned(ws, 256)) return -1;
+    if (!ws || ws_bytes < tile_workspace(value_dtype, g, split_rows_of(tp, g)).bytes || !aligned(ws, 256)) return -1;
     auto go = [&](auto p_tag, auto c_tag) {
         constexpr int PP = decltype(p_tag)::value, CC = decltype(c_tag)::value;
         return launch_backward_tiles_k<TV, TW, PP, CC>(g, tp, value, loc, attn, gout, gv, gl, ga, ws, value_dtype, s);
@@ -2727,6 +2817,25 @@ int try_backward_tiles(const Geom &g, const void *value, const float *loc, const
         case 8: return go(I8{}, I8{});
     }
     return -1;
+}
+
+// Workspace bytes the tile backward's plan for this geometry needs (0 when the plan does not
+// apply), planned as for 256-byte-aligned buffers.
+template <typename TV, typename TW>
+size_t tile_workspace_bytes_t(const Geom &g, int value_dtype) {
+    TilePlan tp;
+    int cpt = 0;
+    const void *a = reinterpret_cast<const void *>((uintptr_t)256);
+    if (!plan_backward_tiles<TV, TW>(g, a, static_cast<const float *>(a), a, a, a, max_smem_optin(), tp, cpt))
+        return 0;
+    return tile_workspace(value_dtype, g, split_rows_of(tp, g)).bytes;
+}
+size_t tile_workspace_bytes(int value_dtype, int weight_dtype, const Geom &g) {
+    if (value_dtype == RFDETR_BF16)
+        return weight_dtype == RFDETR_BF16 ? tile_workspace_bytes_t<bf16, bf16>(g, value_dtype)
+                                           : tile_workspace_bytes_t<bf16, float>(g, value_dtype);
+    return weight_dtype == RFDETR_BF16 ? tile_workspace_bytes_t<float, bf16>(g, value_dtype)
+                                       : tile_workspace_bytes_t<float, float>(g, value_dtype);
 }
 
 }  // namespace
@@ -2802,7 +2911,7 @@ extern "C" size_t rfdetr_msda_backward_workspace_bytes(int value_dtype, int weig
         return 0;
     if (g.B == 0 || g.Lq == 0) return 0;
     const size_t generic = rfdetr_msda_backward_workspace_size(value_dtype, batch, n_heads, head_dim, g.Lv);
-    return std::max(generic, tile_workspace_bytes(value_dtype, g));
+    return std::max(generic, tile_workspace_bytes(value_dtype, weight_dtype, g));
 }
 
 extern "C" int rfdetr_msda_backward(void *stream, const void *value, int value_dtype,

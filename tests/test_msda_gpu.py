@@ -89,10 +89,15 @@ def test_reference_pallas_case(pkg, dtype):
 
 @pytest.mark.parametrize(
     ("cfg", "dtype"),
-    [("c2", torch.bfloat16), ("c3", torch.float32), ("c3", torch.bfloat16), ("c1", torch.float32)],
+    [("c2", torch.bfloat16), ("c3", torch.float32), ("c3", torch.bfloat16), ("c1", torch.float32),
+     ("c3-tiles", torch.float32), ("c3-tiles", torch.bfloat16)],
 )
-def test_full_config_parity(pkg, cfg, dtype):
-    """Configs 1-3 at their benchmark sizes against the float64 oracle."""
+def test_full_config_parity(pkg, tuning, cfg, dtype):
+    """Configs 1-3 at their benchmark sizes against the float64 oracle (config 3 also through the
+    opt-in position-tile backward)."""
+    if cfg == "c3-tiles":
+        tuning("RFDETR_MSDA_TILES", "0,1")
+        cfg = "c3"
     if cfg == "c1":
         args = dict(seed=0, batch=2, len_query=300, heads=16, shapes=((24, 24),), points=2, dim=16)
     elif cfg == "c2":
@@ -216,10 +221,10 @@ def test_unaligned_views_and_entry_points(pkg):
         ("owner, TMA tile loads", {}),
         ("owner, cp.async tile loads", {"RFDETR_MSDA_OWN": "24,1,0"}),
         ("owner, full bins refiled", {"RFDETR_MSDA_OWN": "2,1,1"}),
-        ("position tiles, staged", {"RFDETR_MSDA_OWN": "0,0"}),
+        ("position tiles, staged", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1"}),
         ("position tiles, from L2", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1,0"}),
         ("position tiles, small CTAs, full bins refiled", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "4,1,1,128"}),
-        ("bins", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,0"}),
+        ("bins", {"RFDETR_MSDA_OWN": "0,0"}),
         ("float32 workspace", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_BINS": "0,0", "RFDETR_MSDA_TILES": "0,0"}),
     ],
 )
@@ -244,7 +249,7 @@ def test_backward_variants(pkg, tuning, paths, env):
     [
         ("owner, TMA tile loads", {}),
         ("owner, cp.async tile loads", {"RFDETR_MSDA_OWN": "24,1,0"}),
-        ("position tiles, staged", {"RFDETR_MSDA_OWN": "0,0"}),
+        ("position tiles, staged", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1"}),
         ("position tiles, from L2", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1,0"}),
     ],
 )
@@ -279,10 +284,10 @@ def test_backward_non_finite_rows(pkg, tuning, paths, env):
 @pytest.mark.parametrize(
     ("paths", "env"),
     [
-        ("position tiles", {}),
+        ("position tiles", {"RFDETR_MSDA_TILES": "0,1"}),
         ("position tiles, from L2", {"RFDETR_MSDA_TILES": "0,1,0"}),
         ("position tiles, full bins refiled", {"RFDETR_MSDA_TILES": "3,1,1,64"}),
-        ("accumulate kernels", {"RFDETR_MSDA_TILES": "0,0"}),
+        ("accumulate kernels", {}),
     ],
 )
 def test_backward_non_finite_multilevel(pkg, tuning, paths, env, dtype):
