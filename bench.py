@@ -581,12 +581,13 @@ def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
                                       num_boxes.data_ptr(), NL, B, LQ, C, T, slots, 0.25, 1, losses.data_ptr(),
                                       g_logits.data_ptr(), g_l1.data_ptr(), g_giou.data_ptr()), "losses")
 
+    from rfdetr_jax_b200.ops import projection_backward, projection_offsets
+
     def backward_layer(ly):
         st = st_of()
-        w = ly["weight"].float()
         # The box form's size gradient needs the forward's biased offsets (one GEMM, as the host
         # API's backward recomputes them).
-        ly["offsets"] = torch.addmm(ly["bias"][:2 * hlp], ly["query"].reshape(-1, CH).float(), w[:2 * hlp].t())
+        ly["offsets"] = projection_offsets(ly["query"], ly["weight"], ly["bias"], hlp)
         N.check(lib.rfdetr_msda_backward(st, ly["value"].data_ptr(), N.BF16, shapes, None, ly["loc"].data_ptr(),
                                          ly["attn"].data_ptr(), N.BF16, ly["g_out"].data_ptr(), N.BF16,
                                          ly["g_value"].data_ptr(), ly["g_loc"].data_ptr(), ly["g_attn"].data_ptr(),
@@ -595,8 +596,7 @@ def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
                                                   ly["attn"].data_ptr(), N.BF16, ly["ref"].data_ptr(), 4,
                                                   ly["offsets"].data_ptr(), shapes, ly["g_y"].data_ptr(),
                                                   ly["g_ref"].data_ptr(), B, LQ, H, 1, P), "prologue backward")
-        ly["g_query"] = torch.matmul(ly["g_y"], w)
-        ly["g_weight"] = torch.matmul(ly["g_y"].t(), ly["query"].reshape(-1, CH).float())
+        ly["g_query"], ly["g_weight"], ly["g_bias"] = projection_backward(ly["g_y"], ly["query"], ly["weight"])
 
     comp = torch.cuda.Stream(device)
     comm = torch.cuda.Stream(device)

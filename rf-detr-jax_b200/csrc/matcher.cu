@@ -16,9 +16,11 @@
 //     distance, ties going to an unassigned column (the later one in the work list), else to the
 //     earliest one in the work list.
 // One CTA solves one block: the column scan of each augmenting step is spread over the CTA's
-// threads and the arg-min is a CTA reduction under that tie order.  The block's costs are staged
-// in shared memory when they fit the largest per-CTA budget that keeps two CTAs on an SM,
-// otherwise read through L1.
+// threads and the arg-min is a CTA reduction under that tie order.  Blocks of up to 384 columns
+// run lsap_reg_kernel (each column's state in its thread's registers; its leading rows staged in
+// shared memory up to the largest per-CTA budget that keeps two CTAs on an SM, the rest read
+// through L1); wider blocks run lsap_list_kernel (state and work list in shared memory, the block
+// staged when it fits that budget).
 #include <algorithm>
 
 #include "common.cuh"
@@ -176,7 +178,49 @@ struct LsapArgs {
     int32_t *status;
 };
 
-__global__ void __launch_bounds__(kLsapThreads) lsap_kernel(const LsapArgs a) {
+// Writes a solved block's assignment: a wide or square block by row; a transposed one with the
+// assigned queries in ascending order (a block-wide compaction).
+__device__ void report_assignment(const LsapArgs &a, size_t obase, int start, bool tr, int nr, int nc,
+                                  const int *col4row, const int *row4col) {
+    const int tid = threadIdx.x;
+    if (!tr) {
+        for (int i = tid; i < nr; i += kLsapThreads) {
+            a.rows[obase + i] = start + i;
+            a.cols[obase + i] = col4row[i];
+            a.valid[obase + i] = 1;
+        }
+        return;
+    }
+    __shared__ int s_warp_count[kLsapWarps];
+    __shared__ int s_base;
+    if (tid == 0) s_base = 0;
+    __syncthreads();
+    for (int j0 = 0; j0 < nc; j0 += kLsapThreads) {
+        const int j = j0 + tid;
+        const bool on = j < nc && row4col[j] >= 0;
+        const unsigned bal = __ballot_sync(0xffffffffu, on);
+        const int lane = tid & 31, w = tid >> 5;
+        if (lane == 0) s_warp_count[w] = __popc(bal);
+        __syncthreads();
+        int before = s_base;
+        for (int k = 0; k < w; ++k) before += s_warp_count[k];
+        if (on) {
+            const int slot = before + __popc(bal & ((1u << lane) - 1u));
+            a.rows[obase + slot] = start + j;
+            a.cols[obase + slot] = row4col[j];
+            a.valid[obase + slot] = 1;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int total = 0;
+            for (int k = 0; k < kLsapWarps; ++k) total += s_warp_count[k];
+            s_base += total;
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(kLsapThreads) lsap_list_kernel(const LsapArgs a) {
     extern __shared__ __align__(16) unsigned char sm[];
     const int tid = threadIdx.x;
     const int prob = blockIdx.x;
@@ -372,6 +416,7 @@ __global__ void __launch_bounds__(kLsapThreads) lsap_kernel(const LsapArgs a) {
             if (rseen[r] && r != cur) u[r] = __dadd_rn(u[r], __dsub_rn(minv, dist[col4row[r]]));
         for (int c = tid; c < nc; c += kLsapThreads)
             if (cseen[c]) v[c] = __dsub_rn(v[c], __dsub_rn(minv, dist[c]));
+        __syncthreads();  // the dual update reads col4row, which the path walk rewrites
         if (tid == 0) {
             u[cur] = __dadd_rn(u[cur], minv);
             int j = s_sink;
@@ -393,42 +438,267 @@ __global__ void __launch_bounds__(kLsapThreads) lsap_kernel(const LsapArgs a) {
         if (tid == 0) atomicExch(a.status, (int)RFDETR_ERR_LIMIT);
         return;
     }
-    if (!tr) {
-        for (int i = tid; i < nr; i += kLsapThreads) {
-            a.rows[obase + i] = start + i;
-            a.cols[obase + i] = col4row[i];
-            a.valid[obase + i] = 1;
-        }
-        return;
+    report_assignment(a, obase, start, tr, nr, nc, col4row, row4col);
+}
+
+// Order-preserving 64-bit key of a float64 distance (+0 and -0 share one key, as they compare
+// equal), and its inverse.
+__device__ __forceinline__ unsigned long long dist_key(double d) {
+    const unsigned long long bits = (unsigned long long)__double_as_longlong(d + 0.0);
+    return bits ^ ((bits >> 63) ? 0xffffffffffffffffull : 0x8000000000000000ull);
+}
+__device__ __forceinline__ double dist_of_key(unsigned long long key) {
+    key ^= (key >> 63) ? 0x8000000000000000ull : 0xffffffffffffffffull;
+    return __longlong_as_double((long long)key);
+}
+
+// Tie key of a column at work-list position `pos`: smaller wins; unassigned columns first, the
+// later one among them, else the earliest (the order of `beats`).
+__device__ __forceinline__ unsigned tie_key(bool free, int pos) {
+    return free ? (0xffffu - (unsigned)pos) : (0x10000u | (unsigned)pos);
+}
+
+// The solver for blocks of up to R * 128 columns: the same method, tie rules and float64
+// arithmetic as lsap_list_kernel, with each column owned by a fixed thread (column c by thread
+// c % 128) that keeps the column's dual, tentative distance, owner row and work-list position in
+// registers.  The work list exists only as those positions (SciPy's swap-remove moves the list's
+// last column into the retired column's slot, so each step updates one position), which keeps
+// the tie order exact.  A scan step then reads from shared memory only the row's dual and its
+// costs: its candidate is the minimum of a 96-bit key (distance, tie key) over the CTA -- three
+// redux.sync minimums per warp, then every thread combines the four warp minimums itself, and
+// the winning column's owner publishes the next row.  The dual update runs from the column side
+// (a row seen by the search, other than the inserted one, owns exactly one retired column) before
+// the path is flipped.
+template <int R>
+__global__ void __launch_bounds__(kLsapThreads) lsap_reg_kernel(const LsapArgs a) {
+    extern __shared__ __align__(16) unsigned char sm[];
+    const int tid = threadIdx.x;
+    const int prob = blockIdx.x;
+    const int n = prob / a.G, g = prob - (prob / a.G) * a.G;
+    const int Qg = a.Qg, T = a.T;
+    const int start = g * Qg;
+    const size_t obase = ((size_t)n * a.G + g) * T;
+    for (int k = tid; k < T; k += kLsapThreads) {
+        a.rows[obase + k] = 0;
+        a.cols[obase + k] = 0;
+        a.valid[obase + k] = 0;
     }
-    // Transposed: report the assigned queries in ascending order (a block-wide compaction).
-    __shared__ int s_warp_count[kLsapWarps];
-    __shared__ int s_base;
-    if (tid == 0) s_base = 0;
-    __syncthreads();
-    for (int j0 = 0; j0 < nc; j0 += kLsapThreads) {
-        const int j = j0 + tid;
-        const bool on = j < nc && row4col[j] >= 0;
-        const unsigned bal = __ballot_sync(0xffffffffu, on);
-        const int lane = tid & 31, w = tid >> 5;
-        if (lane == 0) s_warp_count[w] = __popc(bal);
-        __syncthreads();
-        int before = s_base;
-        for (int k = 0; k < w; ++k) before += s_warp_count[k];
-        if (on) {
-            const int slot = before + __popc(bal & ((1u << lane) - 1u));
-            a.rows[obase + slot] = start + j;
-            a.cols[obase + slot] = row4col[j];
-            a.valid[obase + slot] = 1;
-        }
+    int size = __ldg(a.sizes + n % a.size_mod);
+    size = max(0, min(size, T));
+    if (size == 0) return;
+
+    const bool tr = size < Qg;  // solve transposed: rows = targets, columns = queries
+    const int nr = tr ? size : Qg;
+    const int nc = tr ? Qg : size;
+    const int M = max(Qg, T);
+
+    double *u = reinterpret_cast<double *>(sm);
+    int *path = reinterpret_cast<int *>(u + M);
+    int *col4row = path + M;
+    int *row4col = col4row + M;
+    float *csm = reinterpret_cast<float *>(row4col + M);
+    csm = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(csm) + 15) & ~(uintptr_t)15);
+    __shared__ int s_next, s_sink, s_bad;
+    __shared__ float s_sentinel;
+    __shared__ unsigned s_red[kLsapWarps][4];
+
+    // Stage the block's first rows (solver orientation) row-major, so a step reads consecutive
+    // columns; rows past the stage are read from global memory.  Also find non-finite entries
+    // and the finite max.
+    const float *gblock = a.cost + ((size_t)n * a.Q + start) * T;
+    const int srows = min(nr, a.smem_cost_floats / nc);
+    float fmax_local = -INFINITY;
+    int bad_local = 0;
+    for (int e = tid; e < Qg * size; e += kLsapThreads) {
+        const int qi = e / size, ti = e - (e / size) * size;
+        const float c = __ldg(gblock + (size_t)qi * T + ti);
+        const int i = tr ? ti : qi, j = tr ? qi : ti;
+        if (i < srows) csm[i * nc + j] = c;
+        if (isfinite(c)) fmax_local = fmaxf(fmax_local, c);
+        else bad_local = 1;
+    }
+    const int any_bad = __syncthreads_or(bad_local);
+    float sentinel = 0.f;
+    if (any_bad) {
+        // matcher.py:169-172: non-finite entries become max(finite) + 1 (float32), or 1.
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) fmax_local = fmaxf(fmax_local, __shfl_xor_sync(0xffffffffu, fmax_local, o));
+        __shared__ float s_wmax[kLsapWarps];
+        if ((tid & 31) == 0) s_wmax[tid >> 5] = fmax_local;
         __syncthreads();
         if (tid == 0) {
-            int total = 0;
-            for (int k = 0; k < kLsapWarps; ++k) total += s_warp_count[k];
-            s_base += total;
+            float m = -INFINITY;
+            for (int w = 0; w < kLsapWarps; ++w) m = fmaxf(m, s_wmax[w]);
+            s_sentinel = (m == -INFINITY) ? 1.f : __fadd_rn(m, 1.f);
         }
         __syncthreads();
+        sentinel = s_sentinel;
+        for (int e = tid; e < srows * nc; e += kLsapThreads)
+            if (!isfinite(csm[e])) csm[e] = sentinel;
     }
+    const int gstride = tr ? T : 1;
+
+    // Column state, column c = tid + q * kLsapThreads.
+    double cv[R], cd[R];
+    int cpos[R], cown[R];
+    unsigned live = 0, seen = 0;  // bit q: column in the work list / retired in this insertion
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+        const int c = tid + q * kLsapThreads;
+        cv[q] = 0.0;
+        cd[q] = INFINITY;
+        cpos[q] = nc - 1 - c;  // the work list starts in descending column order
+        cown[q] = -1;
+        if (c < nc) live |= 1u << q;
+    }
+    const unsigned all_live = live;
+    for (int r = tid; r < M; r += kLsapThreads) {
+        u[r] = 0.0;
+        col4row[r] = -1;
+        row4col[r] = -1;
+    }
+    if (tid == 0) {
+        s_sink = -1;
+        s_bad = 0;
+    }
+    __syncthreads();
+
+    bool fail = false;
+    const int steps = min(nc, a.step_cap - 1);
+    for (int cur = 0; cur < nr && !fail; ++cur) {
+        int i = cur, left = nc, sink = -1;
+        double minv = 0.0;
+        for (int step = 0; step <= steps; ++step) {  // each step retires one column
+            const double ui = u[i];
+            const float *srow = i < srows ? csm + i * nc : nullptr;
+            const float *grow = tr ? gblock + i : gblock + (size_t)i * T;
+            unsigned long long bkey = ~0ull;
+            unsigned btie = 0xffffffffu;
+#pragma unroll
+            for (int q = 0; q < R; ++q) {
+                if (!((live >> q) & 1u)) continue;
+                const int c = tid + q * kLsapThreads;
+                float cc;
+                if (srow) {
+                    cc = srow[c];
+                } else {
+                    cc = __ldg(grow + (size_t)c * gstride);
+                    if (any_bad && !isfinite(cc)) cc = sentinel;
+                }
+                const double r = __dsub_rn(__dsub_rn(__dadd_rn(minv, (double)cc), ui), cv[q]);
+                if (r < cd[q]) {
+                    cd[q] = r;
+                    path[c] = i;
+                }
+                const unsigned long long key = dist_key(cd[q]);
+                const unsigned tk = tie_key(cown[q] == -1, cpos[q]);
+                if (key < bkey || (key == bkey && tk < btie)) {
+                    bkey = key;
+                    btie = tk;
+                }
+            }
+            const unsigned w1 = (unsigned)(bkey >> 32), w2 = (unsigned)bkey;
+            const unsigned m1 = __reduce_min_sync(0xffffffffu, w1);
+            const bool e1 = w1 == m1;
+            const unsigned m2 = __reduce_min_sync(0xffffffffu, e1 ? w2 : 0xffffffffu);
+            const bool e2 = e1 && w2 == m2;
+            const unsigned m3 = __reduce_min_sync(0xffffffffu, e2 ? btie : 0xffffffffu);
+            if ((tid & 31) == 0) {
+                s_red[tid >> 5][0] = m1;
+                s_red[tid >> 5][1] = m2;
+                s_red[tid >> 5][2] = m3;
+            }
+            __syncthreads();
+            unsigned b1 = s_red[0][0], b2 = s_red[0][1], b3 = s_red[0][2];
+#pragma unroll
+            for (int w = 1; w < kLsapWarps; ++w) {
+                const unsigned x1 = s_red[w][0], x2 = s_red[w][1], x3 = s_red[w][2];
+                if (x1 < b1 || (x1 == b1 && (x2 < b2 || (x2 == b2 && x3 < b3)))) {
+                    b1 = x1;
+                    b2 = x2;
+                    b3 = x3;
+                }
+            }
+            const unsigned long long wkey = ((unsigned long long)b1 << 32) | b2;
+            if (b3 == 0xffffffffu || wkey >= dist_key(INFINITY)) {  // no column, or none reachable
+                fail = true;
+                break;
+            }
+            const int kwin = (b3 & 0x10000u) ? (int)(b3 & 0xffffu) : (int)(0xffffu - b3);
+            // The winning column leaves the list; the column in the list's last slot takes its
+            // position.
+#pragma unroll
+            for (int q = 0; q < R; ++q) {
+                if (!((live >> q) & 1u)) continue;
+                if (cpos[q] == kwin) {
+                    live &= ~(1u << q);
+                    seen |= 1u << q;
+                    if (cown[q] == -1) s_sink = tid + q * kLsapThreads;
+                    else s_next = cown[q];
+                } else if (cpos[q] == left - 1) {
+                    cpos[q] = kwin;
+                }
+            }
+            --left;
+            minv = dist_of_key(wkey);
+            __syncthreads();
+            sink = s_sink;
+            if (sink != -1) break;
+            i = s_next;
+        }
+        if (sink == -1) fail = true;  // no reachable column, or the scan cap was reached
+        if (fail) break;
+
+        // Dual update, then the next insertion's column state; the path flips after a barrier.
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            if ((seen >> q) & 1u) {
+                const double dm = __dsub_rn(minv, cd[q]);
+                cv[q] = __dsub_rn(cv[q], dm);
+                if (cown[q] >= 0) u[cown[q]] = __dadd_rn(u[cown[q]], dm);
+            }
+            cd[q] = INFINITY;
+            cpos[q] = nc - 1 - (tid + q * kLsapThreads);
+        }
+        seen = 0;
+        live = all_live;
+        __syncthreads();
+        if (tid == 0) {
+            u[cur] = __dadd_rn(u[cur], minv);
+            int j = sink;
+            for (int hop = 0; hop <= nr; ++hop) {
+                const int r = path[j];
+                row4col[j] = r;
+                const int t = col4row[r];
+                col4row[r] = j;
+                j = t;
+                if (r == cur) break;
+                if (hop == nr) s_bad = 1;
+            }
+            s_sink = -1;
+        }
+        __syncthreads();
+        if (s_bad) {
+            fail = true;
+            break;
+        }
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const int c = tid + q * kLsapThreads;
+            if (c < nc) cown[q] = row4col[c];
+        }
+    }
+
+    if (fail) {
+        if (tid == 0) atomicExch(a.status, (int)RFDETR_ERR_LIMIT);
+        return;
+    }
+    report_assignment(a, obase, start, tr, nr, nc, col4row, row4col);
+}
+
+// Shared-memory state of lsap_reg_kernel, before the cost stage.
+size_t lsap_reg_state_bytes(int M) {
+    return ((size_t)M * sizeof(double) + 3 * (size_t)M * sizeof(int) + 15 + 15) & ~(size_t)15;
 }
 
 size_t lsap_state_bytes(int M) {
@@ -509,19 +779,25 @@ int launch_lsap(void *stream, const float *cost, const int32_t *sizes, int64_t s
     a.valid = valid;
     a.status = status_out;
     const int M = std::max(a.Qg, a.T);
-    const size_t state = lsap_state_bytes(M);
+    // Blocks of up to 384 columns (the column count of a block is at most max(Qg, T)) take the
+    // register-resident solver; wider ones the work-list solver.
+    const int R = M <= kLsapThreads ? 1 : M <= 2 * kLsapThreads ? 2 : M <= 3 * kLsapThreads ? 3 : 0;
+    const void *fn = R == 1 ? (const void *)lsap_reg_kernel<1>
+                   : R == 2 ? (const void *)lsap_reg_kernel<2>
+                   : R == 3 ? (const void *)lsap_reg_kernel<3>
+                            : (const void *)lsap_list_kernel;
+    const size_t state = R ? lsap_reg_state_bytes(M) : lsap_state_bytes(M);
     // Stage budget: the most shared memory a CTA can take while two still fit an SM.  A
-    // transposed solve reads one target's cost for every query per scan step (a column of the
-    // [Q, T] block: one cache line per query from L2), so staging the block cuts the step; the
-    // largest blocks, which set the launch's duration, need ~90 KB at config 4 (235 us with this
-    // budget, 261 us unstaged, 274 us at 100 KB, 398 us once only one CTA fits an SM).
-    // The RFDETR_LSAP_STAGE_KB knob overrides it.
+    // transposed solve reads one target's cost for every query per scan step, so staging the
+    // block's rows keeps the step in shared memory; two CTAs per SM (one short second wave at
+    // config 4) measured faster than three with smaller stages.  The RFDETR_LSAP_STAGE_KB knob
+    // overrides it.
     int dev = 0, optin = 0, per_sm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     cudaFuncAttributes fa{};
-    const size_t static_bytes = cudaFuncGetAttributes(&fa, lsap_kernel) == cudaSuccess ? fa.sharedSizeBytes : 0;
+    const size_t static_bytes = cudaFuncGetAttributes(&fa, fn) == cudaSuccess ? fa.sharedSizeBytes : 0;
     const size_t half = (size_t)per_sm / 2;
     size_t budget = half > 1024 + static_bytes ? ((half - 1024 - static_bytes) & ~(size_t)15) : 0;
     const KnobValue stage_kb = knob(kKnobLsapStageKb);
@@ -531,13 +807,21 @@ int launch_lsap(void *stream, const float *cost, const int32_t *sizes, int64_t s
     const size_t want = (size_t)a.Qg * a.T * sizeof(float);
     size_t stage = std::min(want, budget > state ? budget - state : 0);
     if (state + stage > (size_t)optin) stage = (size_t)optin > state ? (size_t)optin - state : 0;
+    stage &= ~(size_t)15;
     a.smem_cost_floats = (int)(stage / sizeof(float));
     const size_t smem = state + stage;
     if (smem > (size_t)optin) return RFDETR_ERR_SHAPE;
     if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(lsap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return RFDETR_ERR_CUDA;
-    lsap_kernel<<<(unsigned)(problems * group_detr), kLsapThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    const dim3 grid((unsigned)(problems * group_detr)), block(kLsapThreads);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (R) {
+        case 1: lsap_reg_kernel<1><<<grid, block, smem, s>>>(a); break;
+        case 2: lsap_reg_kernel<2><<<grid, block, smem, s>>>(a); break;
+        case 3: lsap_reg_kernel<3><<<grid, block, smem, s>>>(a); break;
+        default: lsap_list_kernel<<<grid, block, smem, s>>>(a); break;
+    }
     return launch_status();
 }
 

@@ -187,11 +187,55 @@ def _prologue_launch(query, reference_points, shapes, weight, bias, n_heads, n_l
     return loc, attn
 
 
+_ONES: dict = {}
+
+
+def _ones(n: int, device) -> torch.Tensor:
+    """A cached float32 vector of n ones on `device`."""
+    key = (n, str(device))
+    t = _ONES.get(key)
+    if t is None:
+        t = _ONES[key] = torch.ones(n, device=device)
+    return t
+
+
+def projection_offsets(query: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, hlp: int) -> torch.Tensor:
+    """The forward's biased offsets ``[B*Lq, 2*H*L*P]`` (float32 values), recomputed for the box
+    form's size gradient in the forward's own arithmetic: the projection rounded to the query
+    dtype, then the bias added in it (``layers.py:276-279``).  bf16 queries: one bf16 tensor-core
+    GEMM (cuBLAS)."""
+    x = query.reshape(-1, query.shape[-1])
+    w = weight[:2 * hlp]
+    if query.dtype == torch.bfloat16:
+        return (torch.matmul(x, w.t()) + bias[:2 * hlp].to(torch.bfloat16)).float().contiguous()
+    return (torch.matmul(x.float(), w.float().t()) + bias[:2 * hlp]).contiguous()
+
+
+def projection_backward(g_y: torch.Tensor, query: torch.Tensor, weight: torch.Tensor):
+    """The Linear layer's gradients from the projection's gradient ``g_y [B*Lq, H*L*P*3]``
+    (float32): ``(d query [B*Lq, C], d weight, d bias)``.  For bf16 queries these are the
+    reference's own bf16 products -- JAX differentiates its bf16 ``einsum`` (``layers.py:276``)
+    into bf16 dot products with float32 accumulation -- so they run as bf16 tensor-core GEMMs
+    (cuBLAS) straight from the bf16 operands; float32 queries keep float32 GEMMs."""
+    x = query.reshape(-1, query.shape[-1])
+    # The column sum as a matrix-vector product (cuBLAS reads the [rows, 3*H*L*P] gradient once at
+    # full bandwidth; a column reduction of this narrow matrix does not).
+    g_bias = torch.mv(g_y.t(), _ones(g_y.shape[0], g_y.device))
+    if query.dtype == torch.bfloat16:
+        gb = g_y.to(torch.bfloat16)
+        g_query = torch.matmul(gb, weight.to(torch.bfloat16))
+        g_weight = torch.matmul(gb.t(), x).to(weight.dtype)
+        return g_query, g_weight, g_bias
+    g_query = torch.matmul(g_y, weight.float()).to(query.dtype)
+    g_weight = torch.matmul(g_y.t(), x.float()).to(weight.dtype)
+    return g_query, g_weight, g_bias
+
+
 class MSDeformAttnPrologueFunction(torch.autograd.Function):
     """Forward: one ``rfdetr_msda_prologue`` launch.  Backward (with respect to the query, both
     projections and the reference points) from the saved attention weights: one
     ``rfdetr_msda_prologue_backward`` launch for the softmax and location derivatives, then the
-    projection's two GEMMs (cuBLAS)."""
+    projection's two GEMMs (:func:`projection_backward`, cuBLAS)."""
 
     @staticmethod
     def forward(ctx, query, reference_points, weight, bias, shapes, n_heads, n_levels, n_points):
@@ -212,8 +256,7 @@ class MSDeformAttnPrologueFunction(torch.autograd.Function):
         g_attn = torch.zeros_like(attn) if g_attn is None else g_attn.to(attn.dtype).contiguous()
         offsets = None
         if ref.shape[-1] == 4:  # the box form's size gradient needs the offsets
-            offsets = (torch.matmul(query.reshape(-1, C).float(), weight[:2 * hlp].float().t())
-                       + bias[:2 * hlp]).contiguous()
+            offsets = projection_offsets(query, weight, bias, hlp)
         g_y = torch.empty((B * Lq, 3 * hlp), dtype=torch.float32, device=dev)
         g_ref = torch.empty_like(ref)
         status = N.lib().rfdetr_msda_prologue_backward(
@@ -221,11 +264,8 @@ class MSDeformAttnPrologueFunction(torch.autograd.Function):
             ref.shape[-1], N.ptr(offsets) if offsets is not None else None,
             N.int64_array([v for hw in shapes for v in hw]), N.ptr(g_y), N.ptr(g_ref), B, Lq, H, L, P)
         N.check(status, "rfdetr_msda_prologue_backward")
-        # The projection's gradients: two plain GEMMs (cuBLAS) and a column sum.
-        g_query = torch.matmul(g_y, weight.float()).reshape(B, Lq, C).to(query.dtype)
-        g_weight = torch.matmul(g_y.t(), query.reshape(-1, C).float()).to(weight.dtype)
-        g_bias = g_y.sum(0)
-        return g_query, g_ref, g_weight, g_bias, None, None, None, None
+        g_query, g_weight, g_bias = projection_backward(g_y, query, weight)
+        return g_query.reshape(B, Lq, C), g_ref, g_weight, g_bias, None, None, None, None
 
 
 def msda_prologue(query: torch.Tensor, reference_points: torch.Tensor, spatial_shapes, sampling_offsets_weight,

@@ -200,11 +200,11 @@ def test_stacked_single_layer_shape(pkg):
     _assert_same([x.cpu().numpy() for x in (rows, cols, valid)], OM.hungarian_match(cost.cpu().numpy(), sizes, 2))
 
 
-@pytest.mark.parametrize("budget_kb", ["0", "100"])
+@pytest.mark.parametrize("budget_kb", ["0", "3", "100"])
 def test_stage_budgets(pkg, tuning, budget_kb):
-    """The solver with no shared-memory stage (costs read through L1, the path of blocks too big
-    to stage) and with a smaller stage than the default, set through RFDETR_LSAP_STAGE_KB: SciPy's
-    assignment either way."""
+    """The solver with no shared-memory stage (costs read through L1, the path of rows past the
+    stage), with a stage that holds only a block's first rows (3 KB), and with a smaller stage
+    than the default, set through RFDETR_LSAP_STAGE_KB: SciPy's assignment every time."""
     tuning("RFDETR_LSAP_STAGE_KB", budget_kb)
     rng = np.random.default_rng(5)
     groups, per_group, max_targets = 4, 60, 30
@@ -293,3 +293,20 @@ def test_step_cap_reports_and_leaves_no_stale_slots(pkg, tuning):
     got = pkg.hungarian_match(dev_cost, dev_sizes, groups, status=word)
     pkg.check_device_status(word)
     _assert_same([x.cpu().numpy() for x in got], OM.hungarian_match(cost, sizes, groups))
+
+
+@pytest.mark.parametrize("per_group,max_targets", [(100, 30), (200, 30), (384, 12), (385, 12), (450, 20)])
+@pytest.mark.parametrize("kind", ["normal", "integer"])
+def test_column_counts(pkg, per_group, max_targets, kind):
+    """Blocks of 1, 2 and 3 columns per thread (the register-resident solver, up to 384 columns)
+    and wider ones (the work-list solver), with random and tie-heavy costs: SciPy's
+    assignment."""
+    rng = np.random.default_rng(per_group + max_targets)
+    groups, n = 2, 3
+    shape = (n, groups * per_group, max_targets)
+    if kind == "normal":
+        cost = rng.standard_normal(shape).astype(np.float32)
+    else:
+        cost = rng.integers(0, 3, shape).astype(np.float32)
+    sizes = np.array([max_targets, 1, max_targets // 2], np.int32)
+    _assert_same(_match(pkg, cost, sizes, groups), OM.hungarian_match(cost, sizes, groups))
