@@ -46,7 +46,8 @@ int rfdetr_abi_version(void);
 /* Sets a process-wide tuning knob.  Knobs exist for experiments and tests; every default is the
  * tuned production choice.  `name` is one of
  *   "RFDETR_MSDA_FWD", "RFDETR_MSDA_BWD", "RFDETR_MSDA_SLAB_FWD", "RFDETR_MSDA_BINS",
- *   "RFDETR_MSDA_OWN" (sampler kernel selection and launch shapes, "a,b,c,d,e"),
+ *   "RFDETR_MSDA_OWN", "RFDETR_MSDA_TILES", "RFDETR_MSDA_CELL" (sampler kernel selection and
+ *   launch shapes, "a,b,c,d,e"),
  *   "RFDETR_LSAP_STAGE_KB" (the assignment's shared-memory cost stage, KiB),
  *   "RFDETR_LSAP_STEP_CAP" (scan steps an augmenting path may take before the solve gives up with
  *   RFDETR_ERR_LIMIT; default: the block's column count, which finite costs never exceed),

@@ -13,8 +13,8 @@ namespace {
 
 const char *const kKnobNames[kKnobCount] = {
     "RFDETR_MSDA_FWD",      "RFDETR_MSDA_BWD",      "RFDETR_MSDA_SLAB_FWD", "RFDETR_MSDA_BINS",
-    "RFDETR_MSDA_OWN",      "RFDETR_MSDA_TILES",    "RFDETR_LSAP_STAGE_KB", "RFDETR_LSAP_STEP_CAP",
-    "RFDETR_TOPK_SORT",     "RFDETR_TOPK_UNSTAGED"};
+    "RFDETR_MSDA_OWN",      "RFDETR_MSDA_TILES",    "RFDETR_MSDA_CELL",     "RFDETR_LSAP_STAGE_KB",
+    "RFDETR_LSAP_STEP_CAP", "RFDETR_TOPK_SORT",     "RFDETR_TOPK_UNSTAGED"};
 
 struct AtomicKnob {
     std::atomic<int> count{0};

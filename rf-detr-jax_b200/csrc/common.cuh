@@ -110,6 +110,7 @@ enum Knob {
     kKnobMsdaBins,      // "RFDETR_MSDA_BINS": capped-bin backward (stage = 0 disables)
     kKnobMsdaOwn,       // "RFDETR_MSDA_OWN": owner backward (hsub = bin cap, stage = 0 disables, acc = 0 no TMA, threads = tile)
     kKnobMsdaTiles,     // "RFDETR_MSDA_TILES": tile backward, opt-in (hsub = bin cap, stage = 1 enables, acc = 0 never stages, threads = per CTA)
+    kKnobMsdaCell,      // "RFDETR_MSDA_CELL": cell-owner backward (stage = 0 disables)
     kKnobLsapStageKb,   // "RFDETR_LSAP_STAGE_KB": shared-memory cost stage budget of the solver, KiB
     kKnobLsapStepCap,   // "RFDETR_LSAP_STEP_CAP": scan steps an augmenting path may take (default: the column count)
     kKnobTopkSort,      // "RFDETR_TOPK_SORT": any value selects the one-CTA sort kernels

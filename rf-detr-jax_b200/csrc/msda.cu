@@ -789,6 +789,7 @@ __device__ __forceinline__ void floor_split(float x, int &xi, float &xf) {
 struct Axis {
     float w0, w1, m0, m1;
     int c0, c1;
+    int i0;  // floor of the clamped coordinate, in [-2, size + 1]
 };
 __device__ __forceinline__ Axis axis_taps(float x, float sizef, int size) {
     Axis a;
@@ -796,6 +797,7 @@ __device__ __forceinline__ Axis axis_taps(float x, float sizef, int size) {
     int i0;
     float f0;
     floor_split(xc, i0, f0);
+    a.i0 = i0;
     a.w1 = xc - f0;
     a.w0 = 1.f - a.w1;
     a.m0 = (unsigned)i0 < (unsigned)size ? 1.f : 0.f;
@@ -2084,6 +2086,314 @@ int try_backward_owner(const Geom &g, const void *value, const float *loc, const
 }
 
 // ------------------------------------------------------------------------------------------
+// Cell-owner backward: one level, bf16 values, weights and gradient rows, 16 channels, and
+// (W+1)(H+1) <= 640 bilinear cells (the Nano decoder's 24 x 24 map: 625).
+//
+// A sample's four taps are the corners of one cell of the map extended by a row and a column
+// of out-of-range positions on the low side: the cell of (floor(x), floor(y)), both in [-1, size-1]
+// when any corner is in range.  One 640-thread CTA per (image, head) slab, two passes:
+//   1. one thread per sample (the next sample's inputs in flight): taps; the four corners' dot
+//      products <value row, g> against the slab staged in shared memory (bf16 x bf16 products,
+//      exact in float32, accumulated in float32 -- so equal to unpacking); the weight and location
+//      gradients, written directly; the sample's cell and its {wx1, wy1, a} kept in shared memory,
+//      and a counting sort of the samples by cell (counts, scan, filing);
+//   2. one owner thread per cell walks its samples and accumulates the four corner vectors
+//      c_k * g (c = a * wx * wy per corner) in registers: a sample's gradient row is read once
+//      (from L2) instead of once per corner;
+// then grad_value[y][x] = A[y][x] + B[y][x-1] + C[y-1][x] + D[y-1][x-1] from the cells'
+// corner accumulators, through shared memory one corner at a time, written once in bf16.
+// Corners outside the map land in extended-grid slots that no output reads.  The reference's
+// non-finite semantics: an out-of-range corner's dot product enters as m * dot (0, or NaN when
+// the clipped row or g is not finite), and the (g * a) * 0 it scatters into its clipped row is
+// NaN in the channels where g * a is not finite -- per-row poison bits applied at the write.
+// Value rows are staged with their two 16-byte halves swapped when bit 2 of the row is set, so
+// the first half of random rows spreads over all eight 16-byte bank groups.
+// ------------------------------------------------------------------------------------------
+constexpr int kCellThreads = 640;
+
+struct CellPlan {
+    unsigned o_vs, o_stash, o_rec, o_cnt, o_off, o_pois;
+    size_t smem;
+};
+
+// d0 += v.lo * g.lo and d1 += v.hi * g.hi for bf16 pairs, float32 accumulation.
+__device__ __forceinline__ void dot2_bf16(unsigned v, unsigned g, float &d0, float &d1) {
+    asm("{\n.reg .b16 vl, vh, gl, gh;\nmov.b32 {vl, vh}, %2;\nmov.b32 {gl, gh}, %3;\n"
+        "fma.rn.f32.bf16 %0, vl, gl, %0;\nfma.rn.f32.bf16 %1, vh, gh, %1;\n}"
+        : "+f"(d0), "+f"(d1)
+        : "r"(v), "r"(g));
+}
+
+// Byte offset of half `hf` of staged 32-byte value row r (halves swapped when bit 2 of r is set).
+__device__ __forceinline__ unsigned cell_row_half(unsigned r, unsigned hf) {
+    return r * 32u + ((hf ^ ((r >> 2) & 1u)) << 4);
+}
+
+template <int P>
+__global__ void __launch_bounds__(kCellThreads, 1)
+msda_backward_cell_kernel(const bf16 *__restrict__ value, const float *__restrict__ loc, const bf16 *__restrict__ attn,
+                          const bf16 *__restrict__ grad_out, bf16 *__restrict__ grad_value,
+                          float *__restrict__ grad_loc, bf16 *__restrict__ grad_attn, const Geom g, const CellPlan cp) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    constexpr int PS = P == 1 ? 0 : P == 2 ? 1 : P == 4 ? 2 : 3;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int bh = blockIdx.x;
+    const int b = bh / g.H, h = bh - (bh / g.H) * g.H;
+    const int W = g.lw[0], Hh = g.lh[0], Lv = g.Lv;
+    const int EW = W + 1, E = (W + 1) * (Hh + 1);
+    const int S = g.Lq * P;
+    const float Wf = (float)W, Hf = (float)Hh;
+    const float qnan = __int_as_float(0x7fc00000);
+
+    const unsigned vs_s = smem_u32(smem + cp.o_vs);
+    float4 *stash = reinterpret_cast<float4 *>(smem + cp.o_stash);
+    unsigned short *rec = reinterpret_cast<unsigned short *>(smem + cp.o_rec);
+    int *cnt = reinterpret_cast<int *>(smem + cp.o_cnt);
+    int *off = reinterpret_cast<int *>(smem + cp.o_off);
+    unsigned *pois = reinterpret_cast<unsigned *>(smem + cp.o_pois);
+    __shared__ int wsum[kCellThreads / 32];
+
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(value + (size_t)bh * Lv * 16);
+        for (int i = tid; i < Lv * 2; i += nthr)
+            *reinterpret_cast<uint4 *>(smem + cp.o_vs + cell_row_half((unsigned)i >> 1, (unsigned)i & 1u)) = __ldg(src + i);
+        for (int p = tid; p < Lv; p += nthr) pois[p] = 0;
+        for (int e = tid; e < E; e += nthr) cnt[e] = 0;
+    }
+    __syncthreads();
+
+    // Pass 1: one thread per sample.
+    const size_t row0 = (size_t)b * g.Lq * g.H + h;  // (image, query 0, head)
+    float2 xy_n = make_float2(0.f, 0.f);
+    unsigned short a_n = 0;
+    uint4 g0_n = make_uint4(0, 0, 0, 0), g1_n = make_uint4(0, 0, 0, 0);
+    auto fetch = [&](int s) {
+        const size_t row = row0 + (size_t)(s >> PS) * g.H;
+        const size_t ri = row * P + (s & (P - 1));
+        xy_n = __ldg(reinterpret_cast<const float2 *>(loc) + ri);
+        a_n = __ldg(reinterpret_cast<const unsigned short *>(attn) + ri);
+        const uint4 *gp = reinterpret_cast<const uint4 *>(grad_out + row * 16);
+        g0_n = __ldg(gp);
+        g1_n = __ldg(gp + 1);
+    };
+    if (tid < S) fetch(tid);
+    for (int s = tid; s < S; s += nthr) {
+        const size_t ri = (row0 + (size_t)(s >> PS) * g.H) * P + (s & (P - 1));
+        const float2 xy = xy_n;
+        const float a = __uint_as_float((unsigned)a_n << 16);
+        const unsigned gw[8] = {g0_n.x, g0_n.y, g0_n.z, g0_n.w, g1_n.x, g1_n.y, g1_n.z, g1_n.w};
+        if (s + nthr < S) fetch(s + nthr);
+        float ix, iy;
+        sample_coords(xy.x, xy.y, Wf, Hf, ix, iy);
+        const bool ok = fabsf(ix) <= 3.0e38f && fabsf(iy) <= 3.0e38f;
+        const Axis ax = axis_taps(ix, Wf, W), ay = axis_taps(iy, Hf, Hh);
+        const int pk[4] = {ay.c0 * W + ax.c0, ay.c0 * W + ax.c1, ay.c1 * W + ax.c0, ay.c1 * W + ax.c1};
+        const float mk[4] = {ax.m0 * ay.m0, ax.m1 * ay.m0, ax.m0 * ay.m1, ax.m1 * ay.m1};
+        float e[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 v0 = lds128(vs_s + cell_row_half((unsigned)pk[k], 0u));
+            const uint4 v1 = lds128(vs_s + cell_row_half((unsigned)pk[k], 1u));
+            float d0 = 0.f, d1 = 0.f;
+            dot2_bf16(v0.x, gw[0], d0, d1);
+            dot2_bf16(v0.y, gw[1], d0, d1);
+            dot2_bf16(v0.z, gw[2], d0, d1);
+            dot2_bf16(v0.w, gw[3], d0, d1);
+            dot2_bf16(v1.x, gw[4], d0, d1);
+            dot2_bf16(v1.y, gw[5], d0, d1);
+            dot2_bf16(v1.z, gw[6], d0, d1);
+            dot2_bf16(v1.w, gw[7], d0, d1);
+            e[k] = mk[k] * (d0 + d1);  // out of range: 0, or NaN when the product is not finite
+        }
+        const float wx0 = ax.w0, wx1 = ax.w1, wy0 = ay.w0, wy1 = ay.w1;
+        const float ds = wy0 * (wx0 * e[0] + wx1 * e[1]) + wy1 * (wx0 * e[2] + wx1 * e[3]);
+        const float dx = wy0 * (e[1] - e[0]) + wy1 * (e[3] - e[2]);
+        const float dy = wx0 * (e[2] - e[0]) + wx1 * (e[3] - e[1]);
+        grad_attn[ri] = __float2bfloat16_rn(ok ? ds : qnan);
+        reinterpret_cast<float2 *>(grad_loc)[ri] =
+            ok ? make_float2(Wf * (a * dx), Hf * (a * dy)) : make_float2(qnan, qnan);
+        int cell = -1;
+        if (ok && ax.i0 >= -1 && ax.i0 < W && ay.i0 >= -1 && ay.i0 < Hh) {
+            cell = (ay.i0 + 1) * EW + (ax.i0 + 1);
+            atomicAdd(&cnt[cell], 1);
+        }
+        stash[s] = make_float4(wx1, wy1, a, __int_as_float(cell));
+        if (ok && (mk[0] == 0.f || mk[1] == 0.f || mk[2] == 0.f || mk[3] == 0.f)) {
+            // An out-of-range corner scatters (g * a) * 0 into its clipped row.
+            unsigned bad = 0;
+            if (!(fabsf(a) <= 3.4028235e38f)) {
+                bad = 0xffffu;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    if ((gw[i] & 0x7f80u) == 0x7f80u) bad |= 1u << (2 * i);
+                    if ((gw[i] & 0x7f800000u) == 0x7f800000u) bad |= 1u << (2 * i + 1);
+                }
+            }
+            if (bad) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (mk[k] == 0.f) atomicOr(&pois[pk[k]], bad);
+            }
+        }
+    }
+    __syncthreads();
+    // Bin starts (exclusive scan of the counts; the counts become cursors), then the filing.
+    {
+        const int lane = tid & 31, w = tid >> 5;
+        const int v = tid < E ? cnt[tid] : 0;
+        int x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) wsum[w] = x;
+        __syncthreads();
+        int before = 0;
+        for (int k = 0; k < w; ++k) before += wsum[k];
+        const int excl = before + x - v;
+        if (tid < E) {
+            off[tid] = excl;
+            cnt[tid] = excl;
+        }
+        if (tid == E - 1) off[E] = excl + v;
+    }
+    __syncthreads();
+    for (int sl = tid; sl < S; sl += nthr) {
+        const int cell = __float_as_int(stash[sl].w);
+        if (cell >= 0) rec[atomicAdd(&cnt[cell], 1)] = (unsigned short)sl;
+    }
+    __syncthreads();
+
+    // Pass 2: the owner of cell `tid` accumulates its samples' four corner vectors.
+    float2 acc[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[k][i] = make_float2(0.f, 0.f);
+    if (tid < E) {
+        const int beg = off[tid], end = off[tid + 1];
+        for (int r = beg; r < end; ++r) {
+            const int sl = rec[r];
+            const float4 st = stash[sl];
+            const uint4 *gp = reinterpret_cast<const uint4 *>(grad_out + (row0 + (size_t)(sl >> PS) * g.H) * 16);
+            const uint4 g0 = __ldg(gp), g1 = __ldg(gp + 1);
+            const unsigned gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            const float wx1 = st.x, wy1 = st.y, a = st.z;
+            const float ax0 = a * (1.f - wx1), ax1 = a * wx1;
+            const float2 c0 = make_float2(ax0 * (1.f - wy1), ax0 * (1.f - wy1));
+            const float2 c1 = make_float2(ax1 * (1.f - wy1), ax1 * (1.f - wy1));
+            const float2 c2 = make_float2(ax0 * wy1, ax0 * wy1);
+            const float2 c3 = make_float2(ax1 * wy1, ax1 * wy1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float2 gp2 = bf16x2_lo_hi(gw[i]);
+                acc[0][i] = __ffma2_rn(c0, gp2, acc[0][i]);
+                acc[1][i] = __ffma2_rn(c1, gp2, acc[1][i]);
+                acc[2][i] = __ffma2_rn(c2, gp2, acc[2][i]);
+                acc[3][i] = __ffma2_rn(c3, gp2, acc[3][i]);
+            }
+        }
+    }
+    __syncthreads();
+
+    // grad_value from the corner accumulators, one corner at a time through the (now free)
+    // sample stash, laid out chunk-major so both sides are conflict-free.
+    float2 out[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = make_float2(0.f, 0.f);
+    float4 *X = stash;
+    const int y = tid / W, x = tid - (tid / W) * W;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        if (tid < E) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                X[i * E + tid] = make_float4(acc[k][2 * i].x, acc[k][2 * i].y, acc[k][2 * i + 1].x, acc[k][2 * i + 1].y);
+        }
+        __syncthreads();
+        if (tid < Lv) {
+            const int src = (y - (k >> 1) + 1) * EW + (x - (k & 1) + 1);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 f = X[i * E + src];
+                out[2 * i] = __fadd2_rn(out[2 * i], make_float2(f.x, f.y));
+                out[2 * i + 1] = __fadd2_rn(out[2 * i + 1], make_float2(f.z, f.w));
+            }
+        }
+        __syncthreads();
+    }
+    if (tid < Lv) {
+        const unsigned pm = pois[tid];
+        float f[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            f[2 * i] = (pm >> (2 * i)) & 1u ? qnan : out[i].x;
+            f[2 * i + 1] = (pm >> (2 * i + 1)) & 1u ? qnan : out[i].y;
+        }
+        store_vec<bf16, 16>(grad_value + ((size_t)bh * Lv + tid) * 16, f);
+    }
+}
+
+// The cell-owner kernel's shared-memory plan, or false when the shape or alignment is not its.
+bool plan_backward_cell(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
+                        const void *grad_value, const float *grad_loc, const void *grad_attn, int optin,
+                        CellPlan &cp) {
+    if (g.L != 1 || g.D != 16) return false;
+    if (!(g.P == 1 || g.P == 2 || g.P == 4 || g.P == 8)) return false;
+    const long long W = g.lw[0], Hh = g.lh[0];
+    const long long E = (W + 1) * (Hh + 1), S = (long long)g.Lq * g.P;
+    if (E > kCellThreads || g.Lv > kCellThreads || S < 1 || S > 65535) return false;
+    if (!aligned(value, 16) || !aligned(grad_value, 16) || !aligned(gout, 16) || !aligned(loc, 8) ||
+        !aligned(grad_loc, 8) || !aligned(attn, 2) || !aligned(grad_attn, 2))
+        return false;
+    if (read_tune(kKnobMsdaCell).stage == 0) return false;
+    auto r16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
+    size_t o = 0;
+    cp.o_vs = (unsigned)o;
+    o += (size_t)g.Lv * 32;
+    cp.o_stash = (unsigned)o;
+    o += std::max((size_t)S * 16, (size_t)E * 64);
+    cp.o_rec = (unsigned)o;
+    o += r16((size_t)S * 2);
+    cp.o_cnt = (unsigned)o;
+    o += r16((size_t)E * 4);
+    cp.o_off = (unsigned)o;
+    o += r16((size_t)(E + 1) * 4);
+    cp.o_pois = (unsigned)o;
+    o += r16((size_t)g.Lv * 4);
+    cp.smem = o;
+    return cp.smem <= (size_t)optin;
+}
+
+template <int P>
+int launch_backward_cell(const Geom &g, const CellPlan &cp, const void *value, const float *loc, const void *attn,
+                         const void *gout, void *gv, float *gl, void *ga, cudaStream_t s) {
+    auto k = msda_backward_cell_kernel<P>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cp.smem) != cudaSuccess)
+        return RFDETR_ERR_CUDA;
+    k<<<(unsigned)(g.B * g.H), kCellThreads, cp.smem, s>>>(
+        static_cast<const bf16 *>(value), loc, static_cast<const bf16 *>(attn), static_cast<const bf16 *>(gout),
+        static_cast<bf16 *>(gv), gl, static_cast<bf16 *>(ga), g, cp);
+    return launch_status();
+}
+
+// bf16 values and weights only (the gradient rows are then bf16 too).
+int try_backward_cell(const Geom &g, const void *value, const float *loc, const void *attn, const void *gout,
+                      void *gv, float *gl, void *ga, cudaStream_t s) {
+    CellPlan cp;
+    if (!plan_backward_cell(g, value, loc, attn, gout, gv, gl, ga, max_smem_optin(), cp)) return -1;
+    switch (g.P) {
+        case 1: return launch_backward_cell<1>(g, cp, value, loc, attn, gout, gv, gl, ga, s);
+        case 2: return launch_backward_cell<2>(g, cp, value, loc, attn, gout, gv, gl, ga, s);
+        case 4: return launch_backward_cell<4>(g, cp, value, loc, attn, gout, gv, gl, ga, s);
+        case 8: return launch_backward_cell<8>(g, cp, value, loc, attn, gout, gv, gl, ga, s);
+    }
+    return -1;
+}
+
+// ------------------------------------------------------------------------------------------
 // Position-tile backward: levels of any size, float32 or bf16 values, no float atomics.
 //
 // K0 (msda_backward_rowsort_kernel), one CTA per (slab, level): a counting sort of the level's
@@ -2941,6 +3251,10 @@ extern "C" int rfdetr_msda_backward(void *stream, const void *value, int value_d
     if (value_dtype == RFDETR_BF16 && g.Lq > 0 && aligned(sampling_locations, 8) && aligned(grad_sampling_locations, 8) &&
         aligned(attention_weights, ws) && aligned(grad_attention_weights, ws)) {
         int st2 = -1;
+        if (weight_dtype == RFDETR_BF16)
+            st2 = try_backward_cell(g, value, sampling_locations, attention_weights, grad_output, grad_value,
+                                    grad_sampling_locations, grad_attention_weights, s);
+        if (st2 >= 0) return st2;
         if (weight_dtype == RFDETR_BF16)
             st2 = try_backward_owner<bf16>(g, value, sampling_locations, attention_weights, grad_output, grad_value,
                                            grad_sampling_locations, grad_attention_weights, s);

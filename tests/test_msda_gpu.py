@@ -218,14 +218,17 @@ def test_unaligned_views_and_entry_points(pkg):
 @pytest.mark.parametrize(
     ("paths", "env"),
     [
-        ("owner, TMA tile loads", {}),
-        ("owner, cp.async tile loads", {"RFDETR_MSDA_OWN": "24,1,0"}),
-        ("owner, full bins refiled", {"RFDETR_MSDA_OWN": "2,1,1"}),
-        ("position tiles, staged", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1"}),
-        ("position tiles, from L2", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1,0"}),
-        ("position tiles, small CTAs, full bins refiled", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "4,1,1,128"}),
-        ("bins", {"RFDETR_MSDA_OWN": "0,0"}),
-        ("float32 workspace", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_BINS": "0,0", "RFDETR_MSDA_TILES": "0,0"}),
+        ("cell owners", {}),
+        ("owner, TMA tile loads", {"RFDETR_MSDA_CELL": "0,0"}),
+        ("owner, cp.async tile loads", {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "24,1,0"}),
+        ("owner, full bins refiled", {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "2,1,1"}),
+        ("position tiles, staged", {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1"}),
+        ("position tiles, from L2", {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1,0"}),
+        ("position tiles, small CTAs, full bins refiled",
+         {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "4,1,1,128"}),
+        ("bins", {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "0,0"}),
+        ("float32 workspace", {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_BINS": "0,0",
+                               "RFDETR_MSDA_TILES": "0,0"}),
     ],
 )
 def test_backward_variants(pkg, tuning, paths, env):
@@ -245,12 +248,45 @@ def test_backward_variants(pkg, tuning, paths, env):
 
 
 @pytest.mark.parametrize(
+    ("shapes", "points", "len_query", "batch", "heads"),
+    [
+        (((24, 24),), 1, 517, 2, 3),   # one point
+        (((13, 7),), 4, 1001, 3, 4),    # four points, a non-square map
+        (((5, 9),), 8, 300, 2, 2),      # eight points
+        (((1, 1),), 2, 70, 1, 2),       # a single position: every corner but one out of range
+        (((24, 25),), 2, 400, 1, 2),    # 650 cells: the next kernel takes it
+        (((24, 24),), 2, 4100, 1, 2),   # a longer query list than the Nano decoder (8200 samples)
+    ],
+)
+def test_cell_backward_shapes(pkg, shapes, points, len_query, batch, heads):
+    """The cell-owner backward (one level, 16 channels, bf16) over point counts, map shapes and
+    sizes at its limits, against the float64 oracle; non-finite attention weights and gradient
+    rows included (a NaN weight poisons every channel of the rows its out-of-range corners clip
+    to)."""
+    value, loc, attn, grad = sampler_inputs(seed=17, batch=batch, len_query=len_query, heads=heads, shapes=shapes,
+                                            points=points, dim=16, lo=-0.15, hi=1.15)
+    value, attn, grad = O.bf16_round(value), O.bf16_round(attn), O.bf16_round(grad)
+    attn[0, 3, 1 % heads, 0] = np.nan
+    grad[0, 5, 0 * 16 + 4] = np.inf
+    with np.errstate(invalid="ignore"):
+        want = (O.ms_deform_attn_forward(value, shapes, loc, attn),) + O.ms_deform_attn_backward(
+            value, shapes, loc, attn, grad)
+    got = _run(pkg, value, shapes, loc, attn, grad, torch.bfloat16)
+    for g, w, n in zip(got, want, ("out", "grad_value", "grad_loc", "grad_attn"), strict=True):
+        fw, fg = np.isfinite(w), np.isfinite(g)
+        np.testing.assert_array_equal(fg, fw, err_msg=f"{n} finiteness")
+        assert_bf16_close(np.where(fw, g, 0.0), np.where(fw, w, 0.0), n)
+    assert pkg._native.lib().rfdetr_take_device_fault(torch.cuda.current_stream().cuda_stream) == 0
+
+
+@pytest.mark.parametrize(
     ("paths", "env"),
     [
-        ("owner, TMA tile loads", {}),
-        ("owner, cp.async tile loads", {"RFDETR_MSDA_OWN": "24,1,0"}),
-        ("position tiles, staged", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1"}),
-        ("position tiles, from L2", {"RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1,0"}),
+        ("cell owners", {}),
+        ("owner, TMA tile loads", {"RFDETR_MSDA_CELL": "0,0"}),
+        ("owner, cp.async tile loads", {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "24,1,0"}),
+        ("position tiles, staged", {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1"}),
+        ("position tiles, from L2", {"RFDETR_MSDA_CELL": "0,0", "RFDETR_MSDA_OWN": "0,0", "RFDETR_MSDA_TILES": "0,1,0"}),
     ],
 )
 def test_backward_non_finite_rows(pkg, tuning, paths, env):
