@@ -838,6 +838,15 @@ def run_ours(args):
     barrier = ranks.barrier
 
     lib = N.lib()
+    if args.part == "decoder":
+        # The config-5 stand-in alone (for a kernel launch list of the step); prints its record.
+        decoder = run_decoder_step(torch, dist, device, ranks, N, lib, max(3, args.steps), args.warmup)
+        if rank == 0:
+            print(json.dumps({"decoder_step": decoder}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     stream = torch.cuda.Stream(device)
     fwd_bytes, bwd_bytes = algorithmic_bytes()
     ring = ring_size()
@@ -1061,7 +1070,7 @@ def run_ours(args):
         "config": workload_config(world),
         "timing": f"median of {reps_step} timed regions of exactly {args.steps} steps, one CUDA-graph replay "
                   "per step",
-        "roofline": {"bound": "hbm", "kernel": "msda_backward_owner_kernel", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": "msda_backward_cell_kernel", "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "peak_source": peak_src, "algorithmic_bytes": bwd_bytes, "ms_per_launch": ms_bwd},
         "kernels": {"msda_forward": {"ms": ms_fwd, "GB/s": fwd_bytes / (ms_fwd * 1e-3) / 1e9,
@@ -1099,6 +1108,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--part", choices=("all", "decoder"), default="all",
+                    help="'decoder': only the config-5 stand-in step (for profiling its launches)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
