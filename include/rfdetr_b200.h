@@ -153,14 +153,13 @@ int rfdetr_msda_backward(void *stream,
  * enough slabs -- the Nano decoder's among them) never touch the array and have no extra limit;
  * nor do float32 values.  The entry point itself allocates nothing.
  *
- * The first call on each device looks up the array's device address (cudaGetSymbolAddress, with
- * that device current) and caches it per device index; make that first call before any stream
- * capture.  The address belongs to the device's primary context, the one the CUDA runtime uses:
- * call from threads whose current context is that primary context, and not across a
- * cudaDeviceReset (which destroys it and would leave the cached address dangling).  Every call on
- * a device shares the one array: the call clears it before use, but calls whose work overlaps on
- * the GPU (different streams, or different host threads, on the same device) race on it and must
- * be serialised by the caller.  Arguments and results are those of rfdetr_msda_backward.
+ * Each call looks up the array's device address in the current context (cudaGetSymbolAddress, a
+ * host-side query): nothing is cached, so a context that was reset or recreated is simply looked
+ * up again.  The first lookup may load the library's device code; make one call before any stream
+ * capture.  Every call on a device shares the one array: the call clears it before use, but calls
+ * whose work overlaps on the GPU (different streams, or different host threads, on the same
+ * device) race on it and must be serialised by the caller.  Arguments and results are those of
+ * rfdetr_msda_backward.
  */
 #define RFDETR_MSDA_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
 int rfdetr_msda_backward_noalloc(void *stream,

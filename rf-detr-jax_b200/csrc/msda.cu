@@ -24,7 +24,6 @@
 #include <type_traits>
 #include <cmath>
 #include <cstdio>
-#include <mutex>
 #include <cstdlib>
 #include <cstring>
 
@@ -3347,14 +3346,12 @@ extern "C" int rfdetr_msda_backward(void *stream, const void *value, int value_d
 // ------------------------------------------------------------------------------------------
 // Backward without a workspace argument (see rfdetr_msda_backward_noalloc in the header).
 // The float32 accumulator of the bf16 path lives in this static device array.  In host code
-// the name is only a host-side stand-in, so its device address is looked up per device with
-// cudaGetSymbolAddress and passed to the kernels like a caller's workspace.
+// the name is only a host-side stand-in, so its device address (in the current context) is
+// looked up with cudaGetSymbolAddress on every call and passed to the kernels like a caller's
+// workspace.
 // ------------------------------------------------------------------------------------------
 namespace {
 constexpr size_t kNoAllocScratchBytes = RFDETR_MSDA_NOALLOC_SCRATCH_BYTES;
-constexpr int kNoAllocMaxDevices = 64;
-std::mutex g_noalloc_mutex;
-void *g_noalloc_address[kNoAllocMaxDevices] = {nullptr};
 }  // namespace
 
 static __device__ __align__(256) float g_msda_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
@@ -3385,18 +3382,9 @@ extern "C" int rfdetr_msda_backward_noalloc(void *stream, const void *value, int
                                                  len_query, n_levels, n_points);
             return st2 == RFDETR_ERR_WORKSPACE ? RFDETR_ERR_CAPACITY : st2;
         }
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return RFDETR_ERR_CUDA;
-        {
-            std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-            if (!g_noalloc_address[dev]) {
-                void *address = nullptr;
-                if (cudaGetSymbolAddress(&address, g_msda_noalloc_scratch) != cudaSuccess || !address)
-                    return RFDETR_ERR_CUDA;
-                g_noalloc_address[dev] = address;
-            }
-            scratch = g_noalloc_address[dev];
-        }
+        // The array's address in the current context, looked up on every call (a host-side query,
+        // no allocation): nothing cached can outlive a context that was reset or recreated.
+        if (cudaGetSymbolAddress(&scratch, g_msda_noalloc_scratch) != cudaSuccess || !scratch) return RFDETR_ERR_CUDA;
         scratch_bytes = kNoAllocScratchBytes;
     }
     return rfdetr_msda_backward(stream, value, value_dtype, spatial_shapes, level_start_index, sampling_locations,
