@@ -476,6 +476,7 @@ def run_config3(torch, device, N, lib, peak):
 # figure published for RF-DETR Nano.
 NANO_PARAMS = 30_500_000
 AR_BUCKETS = 4
+AR_CTAS = 64  # CTAs per rank of the peer all-reduce
 
 
 def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
@@ -555,7 +556,9 @@ def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
     g_giou = torch.empty_like(dec_boxes)
     shapes = N.int64_array([24, 24])
     grads = torch.randn(NANO_PARAMS, generator=g, device=device)
-    buckets = list(torch.chunk(grads, AR_BUCKETS))
+    # Gradient buckets: 4-element-aligned ranges of one registered buffer.
+    per_bucket = ((NANO_PARAMS + AR_BUCKETS - 1) // AR_BUCKETS + 3) & ~3
+    buckets = [(o, min(per_bucket, NANO_PARAMS - o)) for o in range(0, NANO_PARAMS, per_bucket)]
 
     def forward_and_losses():
         st = st_of()
@@ -616,8 +619,20 @@ def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
     ev_a, ev_b = torch.cuda.Event(), torch.cuda.Event()
     multi = ranks.world > 1
 
+    # The gradient sum: the repository's NVLink peer-memory all-reduce (NCCL's is timed beside it).
+    peer = None
+    if multi:
+        from rfdetr_jax_b200.collective import PeerAllReduce
+
+        peer = PeerAllReduce(grads, ctas=int(os.environ.get("RFDETR_BENCH_AR_CTAS", AR_CTAS)))
+    use_nccl = [False]
+
     def all_reduce(bucket):
-        dist.all_reduce(bucket)
+        offset, count = bucket
+        if use_nccl[0]:
+            dist.all_reduce(grads[offset:offset + count])
+        else:
+            peer(torch.cuda.current_stream(device), offset, count)
 
     def step(compute=True, reduce=True):
         with torch.cuda.stream(comp):
@@ -658,20 +673,33 @@ def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
     ms_step = timed(True, True)
     ms_compute = timed(True, False)
     ms_reduce = timed(False, True) if multi else 0.0
+    ms_step_nccl = ms_reduce_nccl = None
+    if multi:
+        peer.check()
+        use_nccl[0] = True
+        ms_step_nccl = timed(True, True)
+        ms_reduce_nccl = timed(False, True)
+        use_nccl[0] = False
+        torch.cuda.synchronize()
+        ranks.barrier()
+        peer.close()
     N.check(int(m_status.item()), "decoder step: assignment status")
     del graph_a, graph_b
     world = ranks.world
+    busbw = lambda ms: (2 * (world - 1) / world * NANO_PARAMS * 4 / (ms * 1e-3) / 1e9) if ms else None  # noqa: E731
     return {
-        "workload": "config5 stand-in: decoder-side hot path of the Nano train step per GPU (8 images) + NCCL "
-                    f"all-reduce of {NANO_PARAMS / 1e6:.1f}M fp32 gradients in {AR_BUCKETS} buckets",
+        "workload": "config5 stand-in: decoder-side hot path of the Nano train step per GPU (8 images) + the "
+                    f"gradient all-reduce of {NANO_PARAMS / 1e6:.1f}M fp32 gradients in {AR_BUCKETS} buckets",
+        "allreduce": "rfdetr_allreduce_sum_f32 (NVLink peer memory, this repository)" if multi else None,
         "images_per_s": B * world / (ms_step * 1e-3),
         "ms_per_step": ms_step,
         "ms_compute_only": ms_compute,
         "ms_allreduce_only": ms_reduce,
         "ms_allreduce_exposed": max(ms_step - ms_compute, 0.0),
         "allreduce_bytes": NANO_PARAMS * 4 if multi else 0,
-        "allreduce_busbw_GBps": (2 * (world - 1) / world * NANO_PARAMS * 4 / (ms_reduce * 1e-3) / 1e9)
-        if multi and ms_reduce > 0 else None,
+        "allreduce_busbw_GBps": busbw(ms_reduce) if multi else None,
+        "nccl": {"ms_per_step": ms_step_nccl, "ms_allreduce_only": ms_reduce_nccl,
+                 "allreduce_busbw_GBps": busbw(ms_reduce_nccl)} if multi else None,
         "steps": steps,
         "limiter": ("all-reduce" if multi and ms_step - ms_compute > 0.5 * ms_compute else "kernels"),
         "not_run": "backbone, projector, FFN, self-attention, value/output projections (dense layers outside "

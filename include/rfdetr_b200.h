@@ -319,6 +319,35 @@ int rfdetr_set_losses(void *stream, const float *pred_logits, const float *pred_
                       float focal_alpha, int32_t ia_bce, float *losses_out, float *grad_logits,
                       float *grad_boxes_l1, float *grad_boxes_giou);
 
+/* ---------------------------------------------------------------------------------------
+ * Data-parallel gradient all-reduce over NVLink peer memory.
+ *
+ * Replaces the train step's gradient `psum` over the batch axis (trainer.py:462-469), which XLA
+ * lowers to an NCCL all-reduce: one process per GPU on one node, each rank's float32 buffer
+ * summed elementwise across ranks in place.  Setup, once per buffer: every rank allocates a
+ * zeroed flag buffer of rfdetr_allreduce_flag_bytes(), exports it and its buffer with
+ * rfdetr_ipc_get_handle (an rfdetr_ipc_handle_bytes()-byte handle of the allocation holding the
+ * pointer, and the pointer's offset in it), the ranks exchange handles and offsets (any host
+ * channel), and each rank maps its peers' allocations with rfdetr_ipc_open_handle (peer pointer =
+ * mapped base + offset) and releases them with rfdetr_ipc_close_handle.
+ *
+ * rfdetr_allreduce_sum_f32: `buffers` and `flags` are host arrays of `world` device pointers in
+ * rank order (this rank's own and the mapped peers'), 16- and 4-byte aligned; every rank calls it
+ * with the same n, world and epoch, epoch starting at 1 and increasing by one per call, after the
+ * work that writes its buffer on `stream`.  When every rank's launch has completed, every buffer
+ * holds the sum, identical on all ranks (rank-order summation).  `ctas` CTAs per rank (<= 1024;
+ * 0 = 64).  A bounded wait for a peer that runs out (about a second) sets the device int32
+ * *status_out to RFDETR_ERR_LIMIT, which the caller reads when it chooses (the buffers are then
+ * not reduced).  Limits: 1 <= world <= 8 (world 1 returns at once).
+ * ------------------------------------------------------------------------------------- */
+size_t rfdetr_ipc_handle_bytes(void);
+size_t rfdetr_allreduce_flag_bytes(void);
+int rfdetr_ipc_get_handle(const void *device_ptr, void *handle_out, size_t *offset_out);
+int rfdetr_ipc_open_handle(const void *handle, void **base_out);
+int rfdetr_ipc_close_handle(void *base);
+int rfdetr_allreduce_sum_f32(void *stream, float *const *buffers, unsigned *const *flags, int rank, int world,
+                             int64_t n, uint32_t epoch, int ctas, int32_t *status_out);
+
 #ifdef __cplusplus
 }
 #endif

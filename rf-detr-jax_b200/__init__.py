@@ -10,11 +10,13 @@ Components (each a thin host wrapper over ``librfdetr_b200.so``, see ``include/r
 * :mod:`.topk`    -- two-stage query selection (class max + top-k) and ``select_rows``;
 * :mod:`.matcher` -- matching cost and exact batched assignment (SciPy-identical);
 * :mod:`.postprocess` -- inference post-process (top-k over all query/class pairs);
-* :mod:`.losses` -- IA-BCE or focal and matched-pair box losses of stacked layers, with gradients.
+* :mod:`.losses` -- IA-BCE or focal and matched-pair box losses of stacked layers, with gradients;
+* :mod:`.collective` -- the data-parallel gradient all-reduce over NVLink peer memory.
 """
 
 from . import _native
 from ._native import check_device_status, set_tuning
+from .collective import PeerAllReduce
 from .matcher import CriterionConfig, build_cost_matrix, hungarian_match, match_stacked
 from .ops import (MSDeformAttnFunction, MSDeformAttnPrologueFunction, ms_deform_attn, ms_deform_attn_core,
                   ms_deform_attn_core_rows, msda_prologue)
@@ -25,6 +27,7 @@ from .topk import select_rows, top_k, two_stage_topk
 __all__ = [
     "CriterionConfig",
     "MSDeformAttnFunction",
+    "PeerAllReduce",
     "build_cost_matrix",
     "check_device_status",
     "hungarian_match",

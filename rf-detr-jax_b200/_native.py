@@ -44,6 +44,13 @@ SIGNATURES = {
     "rfdetr_set_tuning": (_int, [ctypes.c_char_p, ctypes.c_char_p]),
     "rfdetr_take_device_fault": (_int, [_vp]),
     "rfdetr_selftest_bounded_wait": (_int, [_vp, _int, _vp]),
+    "rfdetr_ipc_handle_bytes": (ctypes.c_size_t, []),
+    "rfdetr_allreduce_flag_bytes": (ctypes.c_size_t, []),
+    "rfdetr_ipc_get_handle": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_size_t)]),
+    "rfdetr_ipc_open_handle": (_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "rfdetr_ipc_close_handle": (_int, [_vp]),
+    "rfdetr_allreduce_sum_f32": (_int, [_vp, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), _int,
+                                        _int, _i64, ctypes.c_uint32, _int, _vp]),
     "rfdetr_msda_forward": (_int, [_vp, _vp, _int, _c_int64_p, _c_int64_p, _vp, _vp, _int, _vp, _int,
                                    _i64, _i64, _i64, _i64, _i64, _i64]),
     "rfdetr_msda_backward_workspace_size": (ctypes.c_size_t, [_int, _i64, _i64, _i64, _i64]),

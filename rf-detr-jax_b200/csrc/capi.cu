@@ -93,7 +93,7 @@ extern "C" const char *rfdetr_status_string(int status) {
     }
 }
 
-extern "C" int rfdetr_abi_version(void) { return 2; }
+extern "C" int rfdetr_abi_version(void) { return 3; }
 
 extern "C" int rfdetr_set_tuning(const char *name, const char *value) {
     using namespace rfdetr;
