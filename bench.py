@@ -406,7 +406,7 @@ def run_prologue(torch, device, N, lib, peak):
     def fused_on_current():
         N.check(lib.rfdetr_msda_prologue(torch.cuda.current_stream(device).cuda_stream, query.data_ptr(), N.BF16,
                                          weight.data_ptr(), bias.data_ptr(), ref.data_ptr(), 4, shapes,
-                                         loc.data_ptr(), attn.data_ptr(), b_, q_, c_, h_, l_, p_), "prologue")
+                                         loc.data_ptr(), attn.data_ptr(), None, b_, q_, c_, h_, l_, p_), "prologue")
 
     ms_fused = graph_ms(fused_on_current)
     ms_composed = graph_ms(composed)
@@ -529,7 +529,8 @@ def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
             "g_value": torch.empty((B * H, LV, D), dtype=torch.bfloat16, device=device),
             "g_loc": torch.empty((B, LQ, H, 1, P, 2), device=device),
             "g_attn": torch.empty((B, LQ, H, P), dtype=torch.bfloat16, device=device),
-            "g_y": torch.empty((B * LQ, 3 * hlp), device=device),
+            "offsets": torch.empty((B * LQ, 2 * hlp), device=device),
+            "g_y": torch.empty((B * LQ, 3 * hlp), dtype=torch.bfloat16, device=device),
             "g_ref": torch.empty((B, LQ, 1, 4), device=device),
         })
     rng = np.random.default_rng(600 + rank)
@@ -569,8 +570,8 @@ def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
         for ly in layers:
             N.check(lib.rfdetr_msda_prologue(st, ly["query"].data_ptr(), N.BF16, ly["weight"].data_ptr(),
                                              ly["bias"].data_ptr(), ly["ref"].data_ptr(), 4, shapes,
-                                             ly["loc"].data_ptr(), ly["attn"].data_ptr(), B, LQ, CH, H, 1, P),
-                    "prologue")
+                                             ly["loc"].data_ptr(), ly["attn"].data_ptr(), ly["offsets"].data_ptr(),
+                                             B, LQ, CH, H, 1, P), "prologue")
             N.check(lib.rfdetr_msda_forward(st, ly["value"].data_ptr(), N.BF16, shapes, None, ly["loc"].data_ptr(),
                                             ly["attn"].data_ptr(), N.BF16, ly["out"].data_ptr(), N.BF16, B, H, D,
                                             LQ, 1, P), "sampler forward")
@@ -584,20 +585,17 @@ def run_decoder_step(torch, dist, device, ranks, N, lib, steps, warmup):
                                       num_boxes.data_ptr(), NL, B, LQ, C, T, slots, 0.25, 1, losses.data_ptr(),
                                       g_logits.data_ptr(), g_l1.data_ptr(), g_giou.data_ptr()), "losses")
 
-    from rfdetr_jax_b200.ops import projection_backward, projection_offsets
+    from rfdetr_jax_b200.ops import projection_backward
 
     def backward_layer(ly):
         st = st_of()
-        # The box form's size gradient needs the forward's biased offsets (one GEMM, as the host
-        # API's backward recomputes them).
-        ly["offsets"] = projection_offsets(ly["query"], ly["weight"], ly["bias"], hlp)
         N.check(lib.rfdetr_msda_backward(st, ly["value"].data_ptr(), N.BF16, shapes, None, ly["loc"].data_ptr(),
                                          ly["attn"].data_ptr(), N.BF16, ly["g_out"].data_ptr(), N.BF16,
                                          ly["g_value"].data_ptr(), ly["g_loc"].data_ptr(), ly["g_attn"].data_ptr(),
                                          None, 0, B, H, D, LQ, 1, P), "sampler backward")
         N.check(lib.rfdetr_msda_prologue_backward(st, ly["g_loc"].data_ptr(), ly["g_attn"].data_ptr(),
                                                   ly["attn"].data_ptr(), N.BF16, ly["ref"].data_ptr(), 4,
-                                                  ly["offsets"].data_ptr(), shapes, ly["g_y"].data_ptr(),
+                                                  ly["offsets"].data_ptr(), shapes, ly["g_y"].data_ptr(), N.BF16,
                                                   ly["g_ref"].data_ptr(), B, LQ, H, 1, P), "prologue backward")
         ly["g_query"], ly["g_weight"], ly["g_bias"] = projection_backward(ly["g_y"], ly["query"], ly["weight"])
 

@@ -241,16 +241,18 @@ int rfdetr_lsap_batched(void *stream, const float *cost, const int32_t *sizes, i
  *   sampling_offsets.weight, then attention_weights.weight); bias [H*L*P*3] f32 (likewise);
  *   reference_points [B, Lq, L, ref_dim] f32 with ref_dim 2 (points) or 4 (boxes);
  *   spatial_shapes [L][2] = (H_l, W_l), host memory.
- *   sampling_locations [B, Lq, H, L, P, 2] f32; attention_weights [B, Lq, H, L*P] in the query
- *   dtype.  The projection and bias are rounded to the query dtype as the reference's Linear
- *   does (layers.py:276-279); the softmax runs in f32.
+ *   sampling_locations [B, Lq, H, L, P, 2] f32 (8-byte aligned); attention_weights
+ *   [B, Lq, H, L*P] in the query dtype; offsets_out (may be NULL) [B*Lq, H*L*P*2] f32, 8-byte
+ *   aligned, receives the biased offsets (the projection's offsets part, as rounded) -- what the
+ *   box form's backward needs.  The projection and bias are rounded to the query dtype as the
+ *   reference's Linear does (layers.py:276-279); the softmax runs in f32.
  * Limits: L <= 8, C <= 4096, H*L*P <= 1024; bf16 needs C % 16 == 0 and H*L*P % 8 == 0.
  * ------------------------------------------------------------------------------------- */
 int rfdetr_msda_prologue(void *stream, const void *query, int query_dtype, const void *weight,
                          const float *bias, const float *reference_points, int64_t ref_dim,
                          const int64_t *spatial_shapes, float *sampling_locations,
-                         void *attention_weights, int64_t batch, int64_t len_query, int64_t channels,
-                         int64_t n_heads, int64_t n_levels, int64_t n_points);
+                         void *attention_weights, float *offsets_out, int64_t batch, int64_t len_query,
+                         int64_t channels, int64_t n_heads, int64_t n_levels, int64_t n_points);
 
 /* Backward of the prologue's elementwise part (the derivatives of the softmax and of the
  * location arithmetic, ops.py:388-404), for the autodiff of MSDeformAttn's query side:
@@ -258,15 +260,17 @@ int rfdetr_msda_prologue(void *stream, const void *query, int query_dtype, const
  *   (weights_dtype, the forward's attention output), reference_points as in the forward,
  *   offsets [B*Lq, H*L*P*2] f32 (the forward's biased projection, offsets part; box form only,
  *   else may be NULL), spatial_shapes as in the forward.
- *   grad_projection [B*Lq, H*L*P*3] f32 receives the gradient of the projection (offsets part,
- *   then logits part), grad_reference_points [B, Lq, L, ref_dim] f32 that of the reference
- *   points.  The query / weight gradients are then two GEMMs with grad_projection. */
+ *   grad_projection [B*Lq, H*L*P*3] (grad_projection_dtype: f32, or bf16 -- the cotangent
+ *   dtype of a bf16 query's projection in the reference's autodiff) receives the gradient of the
+ *   projection (offsets part, then logits part), grad_reference_points [B, Lq, L, ref_dim] f32
+ *   that of the reference points.  The query / weight gradients are then two GEMMs with
+ *   grad_projection, the bias gradient its column sum. */
 int rfdetr_msda_prologue_backward(void *stream, const float *grad_locations, const void *grad_weights,
                                   const void *attention_weights, int weights_dtype,
                                   const float *reference_points, int64_t ref_dim, const float *offsets,
-                                  const int64_t *spatial_shapes, float *grad_projection,
-                                  float *grad_reference_points, int64_t batch, int64_t len_query,
-                                  int64_t n_heads, int64_t n_levels, int64_t n_points);
+                                  const int64_t *spatial_shapes, void *grad_projection,
+                                  int grad_projection_dtype, float *grad_reference_points, int64_t batch,
+                                  int64_t len_query, int64_t n_heads, int64_t n_levels, int64_t n_points);
 
 /* ---------------------------------------------------------------------------------------
  * Matching cost and exact assignment of stacked layers in one call.

@@ -135,7 +135,9 @@ def prologue_forward(query, reference_points, shapes, w_off, b_off, w_att, b_att
     """``ops.py:381-404``: returns a dict with ``loc`` (float32 ``[B, Lq, H, L, P, 2]``),
     ``loc_alt`` (the other admissible rounding, see the module docstring), ``attn`` (float32
     values of the query dtype, ``[B, Lq, H, L*P]``), ``attn_tie`` (bf16 rounding not determined
-    by a float32 evaluation), ``attn_f64`` (the unrounded softmax) and the float32 ``offsets``."""
+    by a float32 evaluation), ``attn_f64`` (the unrounded softmax) and the float32 ``offsets``
+    (the biased projection's offsets part, ``[B, Lq, H, L, P, 2]``) with ``offsets_alt``, their other
+    admissible rounding."""
     batch, len_query, _ = np.shape(query)
     hlp = n_heads * n_levels * n_points
     y, y_alt, amb = projection(query, np.concatenate([w_off, w_att], 0), np.concatenate([b_off, b_att], 0), dtype)
@@ -152,6 +154,7 @@ def prologue_forward(query, reference_points, shapes, w_off, b_off, w_att, b_att
     loc = _locations(off, reference_points, shapes, n_points, dtype)
     loc_alt = _locations(off_alt, reference_points, shapes, n_points, dtype)
     return {"loc": loc, "loc_alt": loc_alt, "attn": attn, "attn_tie": tie, "attn_f64": attn64, "offsets": off,
+            "offsets_alt": off_alt,
             "logits_ambiguous": amb[..., 2 * hlp:].reshape(logits.shape)}
 
 

@@ -65,10 +65,10 @@ SIGNATURES = {
     "rfdetr_match_cost": (_int, [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                  _f32, _f32, _f32, _f32]),
     "rfdetr_lsap_batched": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
-    "rfdetr_msda_prologue": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _i64, _c_int64_p, _vp, _vp, _i64, _i64, _i64,
-                                    _i64, _i64, _i64]),
-    "rfdetr_msda_prologue_backward": (_int, [_vp, _vp, _vp, _vp, _int, _vp, _i64, _vp, _c_int64_p, _vp, _vp, _i64,
-                                             _i64, _i64, _i64, _i64]),
+    "rfdetr_msda_prologue": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _i64, _c_int64_p, _vp, _vp, _vp, _i64, _i64,
+                                    _i64, _i64, _i64, _i64]),
+    "rfdetr_msda_prologue_backward": (_int, [_vp, _vp, _vp, _vp, _int, _vp, _i64, _vp, _c_int64_p, _vp, _int, _vp,
+                                             _i64, _i64, _i64, _i64, _i64]),
     "rfdetr_match_stacked": (_int, [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                     _i64, _f32, _f32, _f32, _f32, _vp, _vp, _vp, _vp, _vp]),
     "rfdetr_set_losses": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -154,7 +154,8 @@ __device__ __forceinline__ void project_f32(const float *__restrict__ x, const f
 template <typename TQ>
 __global__ void __launch_bounds__(kProThreads)
 msda_prologue_kernel(const TQ *__restrict__ query, const TQ *__restrict__ weight, const float *__restrict__ bias,
-                     const float *__restrict__ ref, float *__restrict__ loc, TQ *__restrict__ attn, const ProGeom g) {
+                     const float *__restrict__ ref, float *__restrict__ loc, TQ *__restrict__ attn,
+                     float *__restrict__ offsets_out, const ProGeom g) {
     extern __shared__ __align__(16) float psm[];
     const int ys_stride = g.cout + 1;
     float *ys = psm;
@@ -221,6 +222,8 @@ msda_prologue_kernel(const TQ *__restrict__ query, const TQ *__restrict__ weight
                 for (int p = 0; p < g.P; ++p) {
                     const int o = ((h * g.L + l) * g.P + p) * 2;
                     const float ox = y[o], oy = y[o + 1];
+                    if (offsets_out)  // the biased offsets, kept for the box form's backward
+                        *reinterpret_cast<float2 *>(offsets_out + (size_t)n * hlp2 + o) = make_float2(ox, oy);
                     float lx, ly;
                     if (g.R == 2) {
                         lx = __fadd_rn(rx, __fdiv_rn(ox, s_lw[l]));
@@ -248,15 +251,15 @@ msda_prologue_kernel(const TQ *__restrict__ query, const TQ *__restrict__ weight
 //   points:   d off = g_loc / (W_l, H_l);        d ref_xy = sum over heads and points of g_loc
 //   boxes:    d off = g_loc * (ref_wh * 0.5) / P; d ref_xy likewise; d ref_wh = sum g_loc * off / P * 0.5
 // `offsets` (the forward's biased projection, offsets part) is needed by the box form only.
-template <typename TA>
+template <typename TA, typename TY>
 __global__ void __launch_bounds__(256)
 msda_prologue_bwd_kernel(const float *__restrict__ g_loc, const TA *__restrict__ g_attn, const TA *__restrict__ attn,
-                         const float *__restrict__ ref, const float *__restrict__ offsets, float *__restrict__ g_y,
+                         const float *__restrict__ ref, const float *__restrict__ offsets, TY *__restrict__ g_y,
                          float *__restrict__ g_ref, const ProGeom g) {
     const int LP = g.L * g.P;
     const int hlp = g.H * LP;
     for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < g.N; n += gridDim.x * blockDim.x) {
-        float *gy = g_y + (size_t)n * g.cout;
+        TY *gy = g_y + (size_t)n * g.cout;
         const float *gl = g_loc + (size_t)n * hlp * 2;
         const float *rr = ref + (size_t)n * g.L * g.R;
         for (int h = 0; h < g.H; ++h) {
@@ -264,7 +267,7 @@ msda_prologue_bwd_kernel(const float *__restrict__ g_loc, const TA *__restrict__
             const TA *gh = g_attn + ((size_t)n * g.H + h) * LP;
             float dot = 0.f;
             for (int k = 0; k < LP; ++k) dot += to_f32(ah[k]) * to_f32(gh[k]);
-            for (int k = 0; k < LP; ++k) gy[2 * hlp + h * LP + k] = to_f32(ah[k]) * (to_f32(gh[k]) - dot);
+            for (int k = 0; k < LP; ++k) gy[2 * hlp + h * LP + k] = from_f32<TY>(to_f32(ah[k]) * (to_f32(gh[k]) - dot));
         }
         for (int l = 0; l < g.L; ++l) {
             float sx = 0.f, sy = 0.f, sw = 0.f, sh = 0.f;
@@ -276,11 +279,11 @@ msda_prologue_bwd_kernel(const float *__restrict__ g_loc, const TA *__restrict__
                     sx += gx;
                     sy += gyv;
                     if (g.R == 2) {
-                        gy[o] = __fdiv_rn(gx, g.lw[l]);
-                        gy[o + 1] = __fdiv_rn(gyv, g.lh[l]);
+                        gy[o] = from_f32<TY>(__fdiv_rn(gx, g.lw[l]));
+                        gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv, g.lh[l]));
                     } else {
-                        gy[o] = __fdiv_rn(gx * (rw * 0.5f), (float)g.P);
-                        gy[o + 1] = __fdiv_rn(gyv * (rh * 0.5f), (float)g.P);
+                        gy[o] = from_f32<TY>(__fdiv_rn(gx * (rw * 0.5f), (float)g.P));
+                        gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv * (rh * 0.5f), (float)g.P));
                         const float *off = offsets + (size_t)n * hlp * 2;
                         sw += gx * (off[o] / (float)g.P) * 0.5f;
                         sh += gyv * (off[o + 1] / (float)g.P) * 0.5f;
@@ -304,11 +307,11 @@ msda_prologue_bwd_kernel(const float *__restrict__ g_loc, const TA *__restrict__
 // warp, and the reference points' gradient (a sum over heads and points) is a shuffle reduction
 // over the row's lanes.  Same formulas as msda_prologue_bwd_kernel; the sum over heads is a
 // butterfly instead of a loop, so float32 rounding may differ in the last bits.
-template <typename TA>
+template <typename TA, typename TY>
 __global__ void __launch_bounds__(256)
 msda_prologue_bwd_head_kernel(const float *__restrict__ g_loc, const TA *__restrict__ g_attn,
                               const TA *__restrict__ attn, const float *__restrict__ ref,
-                              const float *__restrict__ offsets, float *__restrict__ g_y, float *__restrict__ g_ref,
+                              const float *__restrict__ offsets, TY *__restrict__ g_y, float *__restrict__ g_ref,
                               const ProGeom g) {
     const int LP = g.L * g.P;
     const int hlp = g.H * LP;
@@ -320,13 +323,13 @@ msda_prologue_bwd_head_kernel(const float *__restrict__ g_loc, const TA *__restr
         const bool act = it < total;
         const long long n = act ? it / g.H : 0;
         const int h = act ? (int)(it - n * g.H) : 0;
-        float *gy = g_y + n * g.cout;
+        TY *gy = g_y + n * g.cout;
         if (act) {
             const TA *ah = attn + n * hlp + h * LP;
             const TA *gh = g_attn + n * hlp + h * LP;
             float dot = 0.f;
             for (int k = 0; k < LP; ++k) dot += to_f32(ah[k]) * to_f32(gh[k]);
-            for (int k = 0; k < LP; ++k) gy[2 * hlp + h * LP + k] = to_f32(ah[k]) * (to_f32(gh[k]) - dot);
+            for (int k = 0; k < LP; ++k) gy[2 * hlp + h * LP + k] = from_f32<TY>(to_f32(ah[k]) * (to_f32(gh[k]) - dot));
         }
         const float *gl = g_loc + n * hlp * 2;
         const float *rr = ref + n * g.L * g.R;
@@ -341,11 +344,11 @@ msda_prologue_bwd_head_kernel(const float *__restrict__ g_loc, const TA *__restr
                     sx += gx;
                     sy += gyv;
                     if (g.R == 2) {
-                        gy[o] = __fdiv_rn(gx, g.lw[l]);
-                        gy[o + 1] = __fdiv_rn(gyv, g.lh[l]);
+                        gy[o] = from_f32<TY>(__fdiv_rn(gx, g.lw[l]));
+                        gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv, g.lh[l]));
                     } else {
-                        gy[o] = __fdiv_rn(gx * (rw * 0.5f), (float)g.P);
-                        gy[o + 1] = __fdiv_rn(gyv * (rh * 0.5f), (float)g.P);
+                        gy[o] = from_f32<TY>(__fdiv_rn(gx * (rw * 0.5f), (float)g.P));
+                        gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv * (rh * 0.5f), (float)g.P));
                         sw += gx * (off[o] / (float)g.P) * 0.5f;
                         sh += gyv * (off[o + 1] / (float)g.P) * 0.5f;
                     }
@@ -378,8 +381,8 @@ using namespace rfdetr;
 extern "C" int rfdetr_msda_prologue(void *stream, const void *query, int query_dtype, const void *weight,
                                     const float *bias, const float *reference_points, int64_t ref_dim,
                                     const int64_t *spatial_shapes, float *sampling_locations,
-                                    void *attention_weights, int64_t batch, int64_t len_query, int64_t channels,
-                                    int64_t n_heads, int64_t n_levels, int64_t n_points) {
+                                    void *attention_weights, float *offsets_out, int64_t batch, int64_t len_query,
+                                    int64_t channels, int64_t n_heads, int64_t n_levels, int64_t n_points) {
     if (query_dtype != RFDETR_F32 && query_dtype != RFDETR_BF16) return RFDETR_ERR_DTYPE;
     if (batch < 0 || len_query < 0 || channels <= 0 || n_heads <= 0 || n_levels <= 0 || n_levels > kProMaxLevels ||
         n_points <= 0 || (ref_dim != 2 && ref_dim != 4) || channels > 4096 || n_heads * n_levels * n_points > 1024 ||
@@ -393,7 +396,8 @@ extern "C" int rfdetr_msda_prologue(void *stream, const void *query, int query_d
         return RFDETR_ERR_SHAPE;
     const int es = dtype_size(query_dtype);
     if (!aligned(query, query_dtype == RFDETR_BF16 ? 16 : 4) || !aligned(weight, 4) || !aligned(bias, 4) ||
-        !aligned(reference_points, 4) || !aligned(sampling_locations, 4) || !aligned(attention_weights, es))
+        !aligned(reference_points, 4) || !aligned(sampling_locations, 8) || !aligned(attention_weights, es) ||
+        !aligned(offsets_out, 8))
         return RFDETR_ERR_ALIGN;
     ProGeom g;
     g.N = (int)(batch * len_query);
@@ -442,7 +446,7 @@ extern "C" int rfdetr_msda_prologue(void *stream, const void *query, int query_d
         const unsigned grid = grid_for(reinterpret_cast<const void *>(k));
         k<<<grid, kProThreads, smem, s>>>(static_cast<const bf16 *>(query), static_cast<const bf16 *>(weight), bias,
                                           reference_points, sampling_locations, static_cast<bf16 *>(attention_weights),
-                                          g);
+                                          offsets_out, g);
     } else {
         auto k = msda_prologue_kernel<float>;
         if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -451,7 +455,7 @@ extern "C" int rfdetr_msda_prologue(void *stream, const void *query, int query_d
         const unsigned grid = grid_for(reinterpret_cast<const void *>(k));
         k<<<grid, kProThreads, smem, s>>>(static_cast<const float *>(query), static_cast<const float *>(weight), bias,
                                           reference_points, sampling_locations,
-                                          static_cast<float *>(attention_weights), g);
+                                          static_cast<float *>(attention_weights), offsets_out, g);
     }
     return launch_status();
 }
@@ -459,10 +463,11 @@ extern "C" int rfdetr_msda_prologue(void *stream, const void *query, int query_d
 extern "C" int rfdetr_msda_prologue_backward(void *stream, const float *grad_locations, const void *grad_weights,
                                              const void *attention_weights, int weights_dtype,
                                              const float *reference_points, int64_t ref_dim, const float *offsets,
-                                             const int64_t *spatial_shapes, float *grad_projection,
-                                             float *grad_reference_points, int64_t batch, int64_t len_query,
-                                             int64_t n_heads, int64_t n_levels, int64_t n_points) {
+                                             const int64_t *spatial_shapes, void *grad_projection,
+                                             int grad_projection_dtype, float *grad_reference_points, int64_t batch,
+                                             int64_t len_query, int64_t n_heads, int64_t n_levels, int64_t n_points) {
     if (weights_dtype != RFDETR_F32 && weights_dtype != RFDETR_BF16) return RFDETR_ERR_DTYPE;
+    if (grad_projection_dtype != RFDETR_F32 && grad_projection_dtype != RFDETR_BF16) return RFDETR_ERR_DTYPE;
     if (batch < 0 || len_query < 0 || n_heads <= 0 || n_levels <= 0 || n_levels > kProMaxLevels || n_points <= 0 ||
         (ref_dim != 2 && ref_dim != 4) || n_heads * n_levels * n_points > 1024 || batch * len_query > (1LL << 31))
         return RFDETR_ERR_SHAPE;
@@ -487,29 +492,25 @@ extern "C" int rfdetr_msda_prologue_backward(void *stream, const float *grad_loc
         g.lw[l] = (float)wid;
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (g.H <= 32 && (g.H & (g.H - 1)) == 0) {
-        const unsigned grid = (unsigned)std::min<long long>(((long long)g.N * g.H + 255) / 256, 148LL * 64);
-        if (weights_dtype == RFDETR_BF16)
-            msda_prologue_bwd_head_kernel<bf16><<<grid, 256, 0, s>>>(
-                grad_locations, static_cast<const bf16 *>(grad_weights), static_cast<const bf16 *>(attention_weights),
-                reference_points, offsets, grad_projection, grad_reference_points, g);
+    const bool head = g.H <= 32 && (g.H & (g.H - 1)) == 0;
+    const unsigned grid = head ? (unsigned)std::min<long long>(((long long)g.N * g.H + 255) / 256, 148LL * 64)
+                               : (unsigned)std::min<long long>((g.N + 255) / 256, 148LL * 8);
+    auto run = [&](auto ta, auto ty) {
+        using TA = decltype(ta);
+        using TY = decltype(ty);
+        const TA *gw = static_cast<const TA *>(grad_weights), *aw = static_cast<const TA *>(attention_weights);
+        TY *gy = static_cast<TY *>(grad_projection);
+        if (head)
+            msda_prologue_bwd_head_kernel<TA, TY><<<grid, 256, 0, s>>>(grad_locations, gw, aw, reference_points,
+                                                                       offsets, gy, grad_reference_points, g);
         else
-            msda_prologue_bwd_head_kernel<float><<<grid, 256, 0, s>>>(
-                grad_locations, static_cast<const float *>(grad_weights),
-                static_cast<const float *>(attention_weights), reference_points, offsets, grad_projection,
-                grad_reference_points, g);
-        return launch_status();
-    }
-    const unsigned grid = (unsigned)std::min<long long>((g.N + 255) / 256, 148LL * 8);
-    if (weights_dtype == RFDETR_BF16)
-        msda_prologue_bwd_kernel<bf16><<<grid, 256, 0, s>>>(grad_locations, static_cast<const bf16 *>(grad_weights),
-                                                             static_cast<const bf16 *>(attention_weights),
-                                                             reference_points, offsets, grad_projection,
-                                                             grad_reference_points, g);
-    else
-        msda_prologue_bwd_kernel<float><<<grid, 256, 0, s>>>(grad_locations, static_cast<const float *>(grad_weights),
-                                                              static_cast<const float *>(attention_weights),
-                                                              reference_points, offsets, grad_projection,
-                                                              grad_reference_points, g);
+            msda_prologue_bwd_kernel<TA, TY><<<grid, 256, 0, s>>>(grad_locations, gw, aw, reference_points, offsets,
+                                                                  gy, grad_reference_points, g);
+    };
+    const bool wb = weights_dtype == RFDETR_BF16, yb = grad_projection_dtype == RFDETR_BF16;
+    if (wb && yb) run(bf16{}, bf16{});
+    else if (wb) run(bf16{}, 0.f);
+    else if (yb) run(0.f, bf16{});
+    else run(0.f, 0.f);
     return launch_status();
 }

@@ -77,34 +77,44 @@ sample_cuda.defvjp(_sample_fwd, _sample_bwd)
 def msda_prologue(query, reference_points, spatial_shapes, weight, bias, n_heads, n_points):
     """``ops.py:381-404``: ``weight`` is ``concat([sampling_offsets.weight, attention_weights.weight])``
     ``[H*L*P*3, C]`` and ``bias`` the concatenated biases."""
-    b, lq, _ = query.shape
+    return _prologue_call(query, reference_points, spatial_shapes, weight, bias, n_heads, n_points)[:2]
+
+
+def _prologue_call(query, reference_points, spatial_shapes, weight, bias, n_heads, n_points):
+    b, lq = query.shape[:2]
     n_levels = len(spatial_shapes)
+    hlp = n_heads * n_levels * n_points
     outs = (jax.ShapeDtypeStruct((b, lq, n_heads, n_levels, n_points, 2), jnp.float32),
-            jax.ShapeDtypeStruct((b, lq, n_heads, n_levels * n_points), query.dtype))
+            jax.ShapeDtypeStruct((b, lq, n_heads, n_levels * n_points), query.dtype),
+            jax.ShapeDtypeStruct((b * lq, 2 * hlp), jnp.float32))
     return jax.ffi.ffi_call("RfdetrMsdaPrologue", outs)(
         query, weight.astype(query.dtype), bias.astype(jnp.float32), reference_points.astype(jnp.float32),
         spatial_shapes=_flat_shapes(spatial_shapes), n_heads=np.int64(n_heads), n_points=np.int64(n_points))
 
 
 def _prologue_fwd(query, reference_points, spatial_shapes, weight, bias, n_heads, n_points):
-    loc, attn = msda_prologue(query, reference_points, spatial_shapes, weight, bias, n_heads, n_points)
-    return (loc, attn), (query, reference_points, weight, bias, attn)
+    loc, attn, offsets = _prologue_call(query, reference_points, spatial_shapes, weight, bias, n_heads, n_points)
+    return (loc, attn), (query, reference_points, weight, bias, attn, offsets)
 
 
 def _prologue_bwd(spatial_shapes, n_heads, n_points, residuals, cotangents):
-    query, ref, weight, bias, attn = residuals
+    query, ref, weight, bias, attn, offsets = residuals
     g_loc, g_attn = cotangents
     b, lq, c = query.shape
     hlp = n_heads * len(spatial_shapes) * n_points
-    x = query.reshape(b * lq, c).astype(jnp.float32)
-    w = weight.astype(jnp.float32)
-    offsets = (x @ w[:2 * hlp].T + bias[:2 * hlp]) if ref.shape[-1] == 4 else jnp.zeros((0,), jnp.float32)
-    outs = (jax.ShapeDtypeStruct((b * lq, 3 * hlp), jnp.float32), jax.ShapeDtypeStruct(ref.shape, jnp.float32))
+    if ref.shape[-1] != 4:
+        offsets = jnp.zeros((0,), jnp.float32)
+    # The projection's cotangent in the query dtype, as JAX's autodiff of the bf16 Linear has it.
+    outs = (jax.ShapeDtypeStruct((b * lq, 3 * hlp), query.dtype), jax.ShapeDtypeStruct(ref.shape, jnp.float32))
     g_y, g_ref = jax.ffi.ffi_call("RfdetrMsdaPrologueBwd", outs)(
         g_loc.astype(jnp.float32), g_attn.astype(attn.dtype), attn, ref.astype(jnp.float32), offsets,
         spatial_shapes=_flat_shapes(spatial_shapes))
-    g_query = (g_y @ w).reshape(b, lq, c).astype(query.dtype)
-    return g_query, g_ref.astype(ref.dtype), (g_y.T @ x).astype(weight.dtype), g_y.sum(0).astype(bias.dtype)
+    x = query.reshape(b * lq, c)
+    w = weight.astype(query.dtype)
+    g_query = jnp.matmul(g_y, w, preferred_element_type=jnp.float32).reshape(b, lq, c).astype(query.dtype)
+    g_weight = jnp.matmul(g_y.T, x, preferred_element_type=jnp.float32).astype(weight.dtype)
+    g_bias = g_y.astype(jnp.float32).sum(0).astype(bias.dtype)
+    return g_query, g_ref.astype(ref.dtype), g_weight, g_bias
 
 
 msda_prologue.defvjp(_prologue_fwd, _prologue_bwd)

@@ -148,17 +148,18 @@ XLA_FFI_DEFINE_HANDLER_SYMBOL(RfdetrMsdaBwdNoAlloc, MsdaBwdNoAlloc,
 
 // ---- sampler prologue --------------------------------------------------------------------------
 // query [B, Lq, C], weight [H*L*P*3, C] (query dtype), bias [H*L*P*3] f32, reference points
-// [B, Lq, L, 2|4] f32 -> loc [B, Lq, H, L, P, 2] f32, attn [B, Lq, H, L*P] (query dtype).
+// [B, Lq, L, 2|4] f32 -> loc [B, Lq, H, L, P, 2] f32, attn [B, Lq, H, L*P] (query dtype), and the
+// biased offsets [B*Lq, H*L*P*2] f32 (the box form's backward residual).
 // Replaces MSDeformAttn.__call__'s query side (ops.py:381-404).
 static ffi::Error MsdaPrologue(cudaStream_t stream, ffi::AnyBuffer query, ffi::AnyBuffer weight,
                                ffi::Buffer<ffi::F32> bias, ffi::Buffer<ffi::F32> ref, ffi::Span<const int64_t> shapes,
                                int64_t n_heads, int64_t n_points, ffi::Result<ffi::Buffer<ffi::F32>> loc,
-                               ffi::Result<ffi::AnyBuffer> attn) {
+                               ffi::Result<ffi::AnyBuffer> attn, ffi::Result<ffi::Buffer<ffi::F32>> offsets) {
     const int64_t B = dim(query, 0), Lq = dim(query, 1), C = dim(query, 2), L = levels_of(shapes);
     return status_error(rfdetr_msda_prologue(stream, query.untyped_data(), dtype_code(query.element_type()),
                                              weight.untyped_data(), bias.typed_data(), ref.typed_data(), dim(ref, 3),
-                                             shapes.begin(), loc->typed_data(), attn->untyped_data(), B, Lq, C,
-                                             n_heads, L, n_points),
+                                             shapes.begin(), loc->typed_data(), attn->untyped_data(),
+                                             offsets->typed_data(), B, Lq, C, n_heads, L, n_points),
                         "RfdetrMsdaPrologue");
 }
 XLA_FFI_DEFINE_HANDLER_SYMBOL(RfdetrMsdaPrologue, MsdaPrologue,
@@ -172,14 +173,15 @@ XLA_FFI_DEFINE_HANDLER_SYMBOL(RfdetrMsdaPrologue, MsdaPrologue,
                                   .Attr<int64_t>("n_heads")
                                   .Attr<int64_t>("n_points")
                                   .Ret<ffi::Buffer<ffi::F32>>()
-                                  .Ret<ffi::AnyBuffer>());
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Ret<ffi::Buffer<ffi::F32>>());
 
 // Elementwise part of the prologue's backward: (grad_loc, grad_attn, attn, ref, offsets) ->
-// (grad_projection [B*Lq, H*L*P*3] f32, grad_ref).  offsets is the forward's biased projection
-// (offsets part) for box references; pass an empty [0] buffer for point references.
+// (grad_projection [B*Lq, H*L*P*3] in f32 or bf16 -- the result's own dtype, grad_ref).  offsets
+// is the forward's third result for box references; pass an empty [0] buffer for point references.
 static ffi::Error MsdaPrologueBwd(cudaStream_t stream, ffi::Buffer<ffi::F32> grad_loc, ffi::AnyBuffer grad_attn,
                                   ffi::AnyBuffer attn, ffi::Buffer<ffi::F32> ref, ffi::Buffer<ffi::F32> offsets,
-                                  ffi::Span<const int64_t> shapes, ffi::Result<ffi::Buffer<ffi::F32>> grad_proj,
+                                  ffi::Span<const int64_t> shapes, ffi::Result<ffi::AnyBuffer> grad_proj,
                                   ffi::Result<ffi::Buffer<ffi::F32>> grad_ref) {
     const int64_t B = dim(grad_loc, 0), Lq = dim(grad_loc, 1), H = dim(grad_loc, 2), L = dim(grad_loc, 3),
                   P = dim(grad_loc, 4);
@@ -189,7 +191,8 @@ static ffi::Error MsdaPrologueBwd(cudaStream_t stream, ffi::Buffer<ffi::F32> gra
     return status_error(rfdetr_msda_prologue_backward(stream, grad_loc.typed_data(), grad_attn.untyped_data(),
                                                       attn.untyped_data(), dtype_code(attn.element_type()),
                                                       ref.typed_data(), dim(ref, 3), off, shapes.begin(),
-                                                      grad_proj->typed_data(), grad_ref->typed_data(), B, Lq, H, L, P),
+                                                      grad_proj->untyped_data(), dtype_code(grad_proj->element_type()),
+                                                      grad_ref->typed_data(), B, Lq, H, L, P),
                         "RfdetrMsdaPrologueBwd");
 }
 XLA_FFI_DEFINE_HANDLER_SYMBOL(RfdetrMsdaPrologueBwd, MsdaPrologueBwd,
@@ -201,7 +204,7 @@ XLA_FFI_DEFINE_HANDLER_SYMBOL(RfdetrMsdaPrologueBwd, MsdaPrologueBwd,
                                   .Arg<ffi::Buffer<ffi::F32>>()
                                   .Arg<ffi::Buffer<ffi::F32>>()
                                   .Attr<ffi::Span<const int64_t>>("spatial_shapes")
-                                  .Ret<ffi::Buffer<ffi::F32>>()
+                                  .Ret<ffi::AnyBuffer>()
                                   .Ret<ffi::Buffer<ffi::F32>>());
 
 // ---- two-stage selection ----------------------------------------------------------------------

@@ -174,60 +174,49 @@ def ms_deform_attn(value: torch.Tensor, spatial_shapes, level_start_index, sampl
     return ms_deform_attn_core_rows(value, shapes, sampling_locations, attention_weights, "cuda")
 
 
-def _prologue_launch(query, reference_points, shapes, weight, bias, n_heads, n_levels, n_points):
+def _prologue_launch(query, reference_points, shapes, weight, bias, n_heads, n_levels, n_points, keep_offsets):
+    """One forward launch; also returns the biased offsets ``[B*Lq, 2*H*L*P]`` (float32) when
+    ``keep_offsets`` (the box form's backward needs them), else None."""
     batch, len_query, channels = query.shape
     dev = query.device
     loc = torch.empty((batch, len_query, n_heads, n_levels, n_points, 2), dtype=torch.float32, device=dev)
     attn = torch.empty((batch, len_query, n_heads, n_levels * n_points), dtype=query.dtype, device=dev)
+    offsets = (torch.empty((batch * len_query, 2 * n_heads * n_levels * n_points), dtype=torch.float32, device=dev)
+               if keep_offsets else None)
     status = N.lib().rfdetr_msda_prologue(
         N.stream_of(query), N.ptr(query), N.dtype_code(query.dtype), N.ptr(weight), N.ptr(bias),
         N.ptr(reference_points), reference_points.shape[-1], N.int64_array([v for hw in shapes for v in hw]),
-        N.ptr(loc), N.ptr(attn), batch, len_query, channels, n_heads, n_levels, n_points)
+        N.ptr(loc), N.ptr(attn), N.ptr(offsets) if offsets is not None else None, batch, len_query, channels,
+        n_heads, n_levels, n_points)
     N.check(status, "rfdetr_msda_prologue")
-    return loc, attn
+    return loc, attn, offsets
 
 
 _ONES: dict = {}
 
 
-def _ones(n: int, device) -> torch.Tensor:
-    """A cached float32 vector of n ones on `device`."""
-    key = (n, str(device))
+def _ones(n: int, device, dtype=torch.float32) -> torch.Tensor:
+    """A cached vector of n ones on `device`."""
+    key = (n, str(device), dtype)
     t = _ONES.get(key)
     if t is None:
-        t = _ONES[key] = torch.ones(n, device=device)
+        t = _ONES[key] = torch.ones(n, device=device, dtype=dtype)
     return t
 
 
-def projection_offsets(query: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, hlp: int) -> torch.Tensor:
-    """The forward's biased offsets ``[B*Lq, 2*H*L*P]`` (float32 values), recomputed for the box
-    form's size gradient in the forward's own arithmetic: the projection rounded to the query
-    dtype, then the bias added in it (``layers.py:276-279``).  bf16 queries: one bf16 tensor-core
-    GEMM (cuBLAS)."""
-    x = query.reshape(-1, query.shape[-1])
-    w = weight[:2 * hlp]
-    if query.dtype == torch.bfloat16:
-        return (torch.matmul(x, w.t()) + bias[:2 * hlp].to(torch.bfloat16)).float().contiguous()
-    return (torch.matmul(x.float(), w.float().t()) + bias[:2 * hlp]).contiguous()
-
-
 def projection_backward(g_y: torch.Tensor, query: torch.Tensor, weight: torch.Tensor):
-    """The Linear layer's gradients from the projection's gradient ``g_y [B*Lq, H*L*P*3]``
-    (float32): ``(d query [B*Lq, C], d weight, d bias)``.  For bf16 queries these are the
-    reference's own bf16 products -- JAX differentiates its bf16 ``einsum`` (``layers.py:276``)
-    into bf16 dot products with float32 accumulation -- so they run as bf16 tensor-core GEMMs
-    (cuBLAS) straight from the bf16 operands; float32 queries keep float32 GEMMs."""
+    """The Linear layer's gradients from the projection's gradient ``g_y [B*Lq, H*L*P*3]`` (in the
+    query dtype, as ``rfdetr_msda_prologue_backward`` writes it): ``(d query [B*Lq, C], d weight,
+    d bias)``.  For bf16 queries these are the reference's own bf16 products -- JAX
+    differentiates its bf16 ``einsum`` (``layers.py:276``) into bf16 dot products with float32
+    accumulation and a bf16 cotangent -- so they run as bf16 tensor-core GEMMs (cuBLAS); the bias
+    gradient is the column sum, as a matrix-vector product (a column reduction of this narrow
+    matrix does not reach full bandwidth).  float32 queries keep float32 GEMMs."""
     x = query.reshape(-1, query.shape[-1])
-    # The column sum as a matrix-vector product (cuBLAS reads the [rows, 3*H*L*P] gradient once at
-    # full bandwidth; a column reduction of this narrow matrix does not).
-    g_bias = torch.mv(g_y.t(), _ones(g_y.shape[0], g_y.device))
-    if query.dtype == torch.bfloat16:
-        gb = g_y.to(torch.bfloat16)
-        g_query = torch.matmul(gb, weight.to(torch.bfloat16))
-        g_weight = torch.matmul(gb.t(), x).to(weight.dtype)
-        return g_query, g_weight, g_bias
-    g_query = torch.matmul(g_y, weight.float()).to(query.dtype)
-    g_weight = torch.matmul(g_y.t(), x.float()).to(weight.dtype)
+    ones = _ones(g_y.shape[0], g_y.device, g_y.dtype)
+    g_bias = torch.mv(g_y.t(), ones).float()
+    g_query = torch.matmul(g_y, weight.to(g_y.dtype)).to(query.dtype)
+    g_weight = torch.matmul(g_y.t(), x.to(g_y.dtype)).to(weight.dtype)
     return g_query, g_weight, g_bias
 
 
@@ -239,14 +228,17 @@ class MSDeformAttnPrologueFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, query, reference_points, weight, bias, shapes, n_heads, n_levels, n_points):
-        loc, attn = _prologue_launch(query, reference_points, shapes, weight, bias, n_heads, n_levels, n_points)
-        ctx.save_for_backward(query, reference_points, weight, bias, attn)
+        # The box form's size gradient needs the forward's biased offsets: the launch keeps them.
+        keep = reference_points.shape[-1] == 4 and any(ctx.needs_input_grad[:4])
+        loc, attn, offsets = _prologue_launch(query, reference_points, shapes, weight, bias, n_heads, n_levels,
+                                              n_points, keep)
+        ctx.save_for_backward(query, reference_points, weight, attn, offsets)
         ctx.geom = (shapes, n_heads, n_levels, n_points)
         return loc, attn
 
     @staticmethod
     def backward(ctx, g_loc, g_attn):
-        query, ref, weight, bias, attn = ctx.saved_tensors
+        query, ref, weight, attn, offsets = ctx.saved_tensors
         shapes, H, L, P = ctx.geom
         B, Lq, C = query.shape
         hlp = H * L * P
@@ -254,15 +246,13 @@ class MSDeformAttnPrologueFunction(torch.autograd.Function):
         g_loc = (torch.zeros((B, Lq, H, L, P, 2), dtype=torch.float32, device=dev) if g_loc is None
                  else g_loc.to(torch.float32).contiguous())
         g_attn = torch.zeros_like(attn) if g_attn is None else g_attn.to(attn.dtype).contiguous()
-        offsets = None
-        if ref.shape[-1] == 4:  # the box form's size gradient needs the offsets
-            offsets = projection_offsets(query, weight, bias, hlp)
-        g_y = torch.empty((B * Lq, 3 * hlp), dtype=torch.float32, device=dev)
+        g_y = torch.empty((B * Lq, 3 * hlp), dtype=query.dtype, device=dev)
         g_ref = torch.empty_like(ref)
         status = N.lib().rfdetr_msda_prologue_backward(
             N.stream_of(g_loc), N.ptr(g_loc), N.ptr(g_attn), N.ptr(attn), N.dtype_code(attn.dtype), N.ptr(ref),
             ref.shape[-1], N.ptr(offsets) if offsets is not None else None,
-            N.int64_array([v for hw in shapes for v in hw]), N.ptr(g_y), N.ptr(g_ref), B, Lq, H, L, P)
+            N.int64_array([v for hw in shapes for v in hw]), N.ptr(g_y), N.dtype_code(g_y.dtype), N.ptr(g_ref), B,
+            Lq, H, L, P)
         N.check(status, "rfdetr_msda_prologue_backward")
         g_query, g_weight, g_bias = projection_backward(g_y, query, weight)
         return g_query.reshape(B, Lq, C), g_ref, g_weight, g_bias, None, None, None, None

@@ -74,10 +74,23 @@ def test_forward(pkg, dtype, ref_dim, case):
     assert loc.shape == (B, Lq, H, L, P, 2) and attn.shape == (B, Lq, H, L * P)
     loc = loc.cpu().numpy()
     attn = attn.float().cpu().numpy()
+    # The biased offsets the launch keeps for the box form's backward (``offsets_out``).
+    from rfdetr_jax_b200 import ops as rops
+
+    weight = torch.cat([dev_args[2], dev_args[4]], 0).to(tdt).contiguous()
+    bias = torch.cat([dev_args[3], dev_args[5]], 0).float().contiguous()
+    _, _, off = rops._prologue_launch(dev_args[0].contiguous(), dev_args[1].contiguous(), shapes, weight, bias, H, L,
+                                      P, True)
+    off = off.cpu().numpy().reshape(want["offsets"].shape)
     if dtype == "f32":
         assert_fp32_close(loc, want["loc"], "loc")
         assert_fp32_close(attn, want["attn"], "attn")
+        # The raw projection: float32 accumulation over C products (the locations divide it by
+        # the map size, so they meet the tighter bound).
+        assert_fp32_close(off, want["offsets"], "offsets", rtol=1e-4, atol=1e-5)
         return
+    ok_off = (off == want["offsets"]) | (off == want["offsets_alt"])
+    assert ok_off.all(), f"offsets: {int((~ok_off).sum())} of {ok_off.size} differ from both admissible roundings"
     ok = (loc == want["loc"]) | (loc == want["loc_alt"])
     assert ok.all(), f"loc: {int((~ok).sum())} of {ok.size} differ from both admissible roundings"
     assert (want["loc"] != want["loc_alt"]).mean() < 0.1
