@@ -1067,7 +1067,33 @@ def run_ours(args):
     barrier()
     d2h_gbps = copy_gbps(lambda: h_res[0][0].copy_(d_res[0][0], non_blocking=True), d2h, s_d2h)
     barrier()
-    copy_bw = ranks.gather_floats([h2d_gbps, d2h_gbps])
+
+    # Both directions at once (what the end-to-end pipeline does in steady state): each copy on its
+    # own stream, bytes of both over the time from the first start to the last end.
+    def duplex_gbps():
+        samples = []
+        for _ in range(6):
+            c0 = torch.cuda.Event(enable_timing=True)
+            a1, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(s_h2d)
+            s_d2h.wait_event(c0)
+            with torch.cuda.stream(s_h2d):
+                dev_slots[0][0].copy_(host_buf, non_blocking=True)
+            with torch.cuda.stream(s_d2h):
+                h_res[0][0].copy_(d_res[0][0], non_blocking=True)
+            a1.record(s_h2d)
+            b1.record(s_d2h)
+            b1.synchronize()
+            a1.synchronize()
+            samples.append(max(c0.elapsed_time(a1), c0.elapsed_time(b1)))
+        ms = statistics.median(samples[1:])
+        return (h2d + d2h) / (ms * 1e-3) / 1e9, ms
+
+    torch.cuda.synchronize()
+    barrier()
+    duplex, duplex_ms = duplex_gbps()
+    barrier()
+    copy_bw = ranks.gather_floats([h2d_gbps, d2h_gbps, duplex, duplex_ms])
 
     decoder = run_decoder_step(torch, dist, device, ranks, N, lib, max(10, min(args.steps, 30)), args.warmup)
 
@@ -1108,7 +1134,10 @@ def run_ours(args):
                 "pipeline": "copy-in / compute / copy-out on three streams, consecutive steps overlapped",
                 "copy_GBps_per_rank": {"h2d": [round(x[0], 2) for x in copy_bw],
                                        "d2h": [round(x[1], 2) for x in copy_bw],
-                                       "how": "one step's transfer alone per direction, pinned host buffer, "
+                                       "duplex_both_directions": [round(x[2], 2) for x in copy_bw],
+                                       "duplex_ms_per_step_of_copies": [round(x[3], 4) for x in copy_bw],
+                                       "how": "one step's transfer per direction, alone and then both "
+                                              "directions at once on two streams, pinned host buffers, "
                                               "CUDA events, median of 5, all ranks at once"}},
         "decoder_step": decoder,
         "gpu_launches": 2 * args.steps,
