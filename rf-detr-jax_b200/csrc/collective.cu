@@ -44,6 +44,8 @@ constexpr int kRingWaitPolls = 1 << 20;  // polls with 64 ns sleeps between: abo
 struct PeerSet {
     float *buf[kRingMaxRanks];         // every rank's buffer, mapped into this process
     unsigned *flags[kRingMaxRanks];    // every rank's flag buffer: [2][kRingMaxRanks][kRingMaxCtas]
+    unsigned *home;                    // flags[rank] (a run-time index into the parameter would copy it
+                                       // to the stack)
 };
 
 __device__ __forceinline__ void store_release_sys(unsigned *p, unsigned v) {
@@ -57,12 +59,14 @@ __device__ __forceinline__ unsigned load_acquire_sys(const unsigned *p) {
 
 // Thread 0 of the CTA: publish `epoch` in slot (rank, cta) of `phase` at every peer, then wait
 // for every peer's slot (peer, cta) at home.  Returns false when a wait ran out.
-__device__ bool ring_handshake(const PeerSet &ps, int rank, int world, int cta, int phase, unsigned epoch) {
+template <int WORLD>
+__device__ bool ring_handshake(const PeerSet &ps, int rank, int cta, int phase, unsigned epoch) {
     const size_t slot_base = (size_t)phase * kRingMaxRanks * kRingMaxCtas;
-    for (int k = 0; k < world; ++k)
+#pragma unroll
+    for (int k = 0; k < WORLD; ++k)
         if (k != rank) store_release_sys(ps.flags[k] + slot_base + (size_t)rank * kRingMaxCtas + cta, epoch);
-    const unsigned *home = ps.flags[rank] + slot_base;
-    for (int k = 0; k < world; ++k) {
+    const unsigned *home = ps.home + slot_base;
+    for (int k = 0; k < WORLD; ++k) {
         if (k == rank) continue;
         int polls = 0;
         while (load_acquire_sys(home + (size_t)k * kRingMaxCtas + cta) != epoch) {
@@ -74,11 +78,11 @@ __device__ bool ring_handshake(const PeerSet &ps, int rank, int world, int cta, 
 }
 
 template <int WORLD>
-__global__ void __launch_bounds__(kRingThreads)
+__global__ void __launch_bounds__(kRingThreads, 1)
 peer_allreduce_kernel(const PeerSet ps, int rank, long long n, long long chunk, unsigned epoch, int32_t *status) {
     __shared__ int ok;
     const int cta = blockIdx.x, G = gridDim.x;
-    if (threadIdx.x == 0) ok = ring_handshake(ps, rank, WORLD, cta, 0, epoch) ? 1 : 0;
+    if (threadIdx.x == 0) ok = ring_handshake<WORLD>(ps, rank, cta, 0, epoch) ? 1 : 0;
     __syncthreads();
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(reinterpret_cast<int *>(status), (int)RFDETR_ERR_LIMIT);
@@ -132,7 +136,7 @@ peer_allreduce_kernel(const PeerSet ps, int rank, long long n, long long chunk, 
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence_system();
-        if (!ring_handshake(ps, rank, WORLD, cta, 1, epoch))
+        if (!ring_handshake<WORLD>(ps, rank, cta, 1, epoch))
             atomicExch(reinterpret_cast<int *>(status), (int)RFDETR_ERR_LIMIT);
     }
 }
@@ -206,6 +210,7 @@ extern "C" int rfdetr_allreduce_sum_f32(void *stream, float *const *buffers, uns
         ps.buf[k] = buffers[k];
         ps.flags[k] = flags[k];
     }
+    ps.home = flags[rank];
     if (!aligned(status_out, 4)) return RFDETR_ERR_ALIGN;
     const long long chunk = ((n + world - 1) / world + 3) & ~3LL;
     int G = ctas > 0 ? ctas : 64;

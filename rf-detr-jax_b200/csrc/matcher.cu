@@ -472,7 +472,7 @@ __device__ __forceinline__ unsigned tie_key(bool free, int pos) {
 // (a row seen by the search, other than the inserted one, owns exactly one retired column) before
 // the path is flipped.
 template <int R>
-__global__ void __launch_bounds__(kLsapThreads) lsap_reg_kernel(const LsapArgs a) {
+__global__ void __launch_bounds__(kLsapThreads, 2) lsap_reg_kernel(const LsapArgs a) {
     extern __shared__ __align__(16) unsigned char sm[];
     const int tid = threadIdx.x;
     const int prob = blockIdx.x;

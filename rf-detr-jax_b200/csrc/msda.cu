@@ -140,7 +140,7 @@ template <typename T> __device__ __forceinline__ float ld_scalar(const T *p) { r
 // Forward
 // ------------------------------------------------------------------------------------------
 template <typename TV, typename TW, int VEC, bool STAGE>
-__global__ void __launch_bounds__(kMaxThreads)
+__global__ void __launch_bounds__(kMaxThreads, 2)
 msda_forward_kernel(const TV *__restrict__ value, const float *__restrict__ loc,
                     const TW *__restrict__ attn, typename OutOf<TV, TW>::T *__restrict__ out,
                     const Geom g, const int team, const int hsub, const int q_tile) {

@@ -53,6 +53,19 @@ __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src)
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// The level sizes copied to shared memory with constant indices, so that the parameter struct
+// stays in the constant bank (a level index that varies at run time would copy it to the stack).
+// Callers read them after a barrier.
+__device__ __forceinline__ void stage_levels(const ProGeom &g, float *s_lw, float *s_lh) {
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int l = 0; l < kProMaxLevels; ++l) {
+            s_lw[l] = g.lw[l];
+            s_lh[l] = g.lh[l];
+        }
+    }
+}
+
 __device__ __forceinline__ void mma_bf16(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -151,8 +164,9 @@ __device__ __forceinline__ void project_f32(const float *__restrict__ x, const f
     }
 }
 
+// Two CTAs per SM (stated, so that ptxas budgets up to 128 registers instead of spilling).
 template <typename TQ>
-__global__ void __launch_bounds__(kProThreads)
+__global__ void __launch_bounds__(kProThreads, 2)
 msda_prologue_kernel(const TQ *__restrict__ query, const TQ *__restrict__ weight, const float *__restrict__ bias,
                      const float *__restrict__ ref, float *__restrict__ loc, TQ *__restrict__ attn,
                      float *__restrict__ offsets_out, const ProGeom g) {
@@ -172,13 +186,7 @@ msda_prologue_kernel(const TQ *__restrict__ query, const TQ *__restrict__ weight
         }
     }
     __shared__ float s_lw[kProMaxLevels], s_lh[kProMaxLevels];
-#pragma unroll
-    for (int l = 0; l < kProMaxLevels; ++l) {  // constant indices: the parameter struct stays in place
-        if (threadIdx.x == l) {
-            s_lw[l] = g.lw[l];
-            s_lh[l] = g.lh[l];
-        }
-    }
+    stage_levels(g, s_lw, s_lh);  // read after the first tile's barrier
     const int LP = g.L * g.P;
     const int hlp2 = g.H * LP * 2;
     const bool lowp = sizeof(TQ) == 2;
@@ -256,6 +264,9 @@ __global__ void __launch_bounds__(256)
 msda_prologue_bwd_kernel(const float *__restrict__ g_loc, const TA *__restrict__ g_attn, const TA *__restrict__ attn,
                          const float *__restrict__ ref, const float *__restrict__ offsets, TY *__restrict__ g_y,
                          float *__restrict__ g_ref, const ProGeom g) {
+    __shared__ float s_lw[kProMaxLevels], s_lh[kProMaxLevels];
+    stage_levels(g, s_lw, s_lh);
+    __syncthreads();
     const int LP = g.L * g.P;
     const int hlp = g.H * LP;
     for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < g.N; n += gridDim.x * blockDim.x) {
@@ -279,8 +290,8 @@ msda_prologue_bwd_kernel(const float *__restrict__ g_loc, const TA *__restrict__
                     sx += gx;
                     sy += gyv;
                     if (g.R == 2) {
-                        gy[o] = from_f32<TY>(__fdiv_rn(gx, g.lw[l]));
-                        gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv, g.lh[l]));
+                        gy[o] = from_f32<TY>(__fdiv_rn(gx, s_lw[l]));
+                        gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv, s_lh[l]));
                     } else {
                         gy[o] = from_f32<TY>(__fdiv_rn(gx * (rw * 0.5f), (float)g.P));
                         gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv * (rh * 0.5f), (float)g.P));
@@ -313,6 +324,9 @@ msda_prologue_bwd_head_kernel(const float *__restrict__ g_loc, const TA *__restr
                               const TA *__restrict__ attn, const float *__restrict__ ref,
                               const float *__restrict__ offsets, TY *__restrict__ g_y, float *__restrict__ g_ref,
                               const ProGeom g) {
+    __shared__ float s_lw[kProMaxLevels], s_lh[kProMaxLevels];
+    stage_levels(g, s_lw, s_lh);
+    __syncthreads();
     const int LP = g.L * g.P;
     const int hlp = g.H * LP;
     const long long total = (long long)g.N * g.H;
@@ -344,8 +358,8 @@ msda_prologue_bwd_head_kernel(const float *__restrict__ g_loc, const TA *__restr
                     sx += gx;
                     sy += gyv;
                     if (g.R == 2) {
-                        gy[o] = from_f32<TY>(__fdiv_rn(gx, g.lw[l]));
-                        gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv, g.lh[l]));
+                        gy[o] = from_f32<TY>(__fdiv_rn(gx, s_lw[l]));
+                        gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv, s_lh[l]));
                     } else {
                         gy[o] = from_f32<TY>(__fdiv_rn(gx * (rw * 0.5f), (float)g.P));
                         gy[o + 1] = from_f32<TY>(__fdiv_rn(gyv * (rh * 0.5f), (float)g.P));
