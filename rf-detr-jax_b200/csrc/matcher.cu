@@ -86,8 +86,6 @@ match_cost_kernel(const TL *__restrict__ logits, const TB *__restrict__ boxes, c
         int nbad = 0;
         for (int c = lane; c < C; c += 32) nbad += isfinite(ldf(lrow + c)) ? 0 : 1;
         nbad = __reduce_add_sync(0xffffffffu, nbad);
-        // Unrolled so that several targets' loads and transcendental chains are in flight at once.
-#pragma unroll 4
         for (int t = lane; t < T; t += 32) {
             float out;
             if (tsm[1 * T + t] == 0.f) {
