@@ -498,9 +498,9 @@ __global__ void __launch_bounds__(kLsapThreads, 2) lsap_reg_kernel(const LsapArg
     int *row4col = col4row + M;
     float *csm = reinterpret_cast<float *>(row4col + M);
     csm = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(csm) + 15) & ~(uintptr_t)15);
-    __shared__ int s_next, s_sink, s_bad;
+    __shared__ int s_bad;
     __shared__ float s_sentinel;
-    __shared__ unsigned s_red[kLsapWarps][4];
+    __shared__ unsigned s_red[2][kLsapWarps][3];  // by step parity: one barrier per step
 
     // Stage the block's first rows (solver orientation) row-major, so a step reads consecutive
     // columns; rows past the stage are read from global memory.  Also find non-finite entries
@@ -557,10 +557,7 @@ __global__ void __launch_bounds__(kLsapThreads, 2) lsap_reg_kernel(const LsapArg
         col4row[r] = -1;
         row4col[r] = -1;
     }
-    if (tid == 0) {
-        s_sink = -1;
-        s_bad = 0;
-    }
+    if (tid == 0) s_bad = 0;
     __syncthreads();
 
     bool fail = false;
@@ -591,7 +588,7 @@ __global__ void __launch_bounds__(kLsapThreads, 2) lsap_reg_kernel(const LsapArg
                     path[c] = i;
                 }
                 const unsigned long long key = dist_key(cd[q]);
-                const unsigned tk = tie_key(cown[q] == -1, cpos[q]);
+                const unsigned tk = (tie_key(cown[q] == -1, cpos[q]) << 9) | (unsigned)c;
                 if (key < bkey || (key == bkey && tk < btie)) {
                     bkey = key;
                     btie = tk;
@@ -603,16 +600,17 @@ __global__ void __launch_bounds__(kLsapThreads, 2) lsap_reg_kernel(const LsapArg
             const unsigned m2 = __reduce_min_sync(0xffffffffu, e1 ? w2 : 0xffffffffu);
             const bool e2 = e1 && w2 == m2;
             const unsigned m3 = __reduce_min_sync(0xffffffffu, e2 ? btie : 0xffffffffu);
+            unsigned(*red)[3] = s_red[step & 1];
             if ((tid & 31) == 0) {
-                s_red[tid >> 5][0] = m1;
-                s_red[tid >> 5][1] = m2;
-                s_red[tid >> 5][2] = m3;
+                red[tid >> 5][0] = m1;
+                red[tid >> 5][1] = m2;
+                red[tid >> 5][2] = m3;
             }
             __syncthreads();
-            unsigned b1 = s_red[0][0], b2 = s_red[0][1], b3 = s_red[0][2];
+            unsigned b1 = red[0][0], b2 = red[0][1], b3 = red[0][2];
 #pragma unroll
             for (int w = 1; w < kLsapWarps; ++w) {
-                const unsigned x1 = s_red[w][0], x2 = s_red[w][1], x3 = s_red[w][2];
+                const unsigned x1 = red[w][0], x2 = red[w][1], x3 = red[w][2];
                 if (x1 < b1 || (x1 == b1 && (x2 < b2 || (x2 == b2 && x3 < b3)))) {
                     b1 = x1;
                     b2 = x2;
@@ -624,7 +622,11 @@ __global__ void __launch_bounds__(kLsapThreads, 2) lsap_reg_kernel(const LsapArg
                 fail = true;
                 break;
             }
-            const int kwin = (b3 & 0x10000u) ? (int)(b3 & 0xffffu) : (int)(0xffffu - b3);
+            // The winner: its work-list position and, in the tie word's low bits, its column --
+            // whose row every thread reads from row4col (fixed during the scan).
+            const unsigned wt = b3 >> 9;
+            const int kwin = (wt & 0x10000u) ? (int)(wt & 0xffffu) : (int)(0xffffu - wt);
+            const int cwin = (int)(b3 & 511u);
             // The winning column leaves the list; the column in the list's last slot takes its
             // position.
 #pragma unroll
@@ -633,18 +635,18 @@ __global__ void __launch_bounds__(kLsapThreads, 2) lsap_reg_kernel(const LsapArg
                 if (cpos[q] == kwin) {
                     live &= ~(1u << q);
                     seen |= 1u << q;
-                    if (cown[q] == -1) s_sink = tid + q * kLsapThreads;
-                    else s_next = cown[q];
                 } else if (cpos[q] == left - 1) {
                     cpos[q] = kwin;
                 }
             }
             --left;
             minv = dist_of_key(wkey);
-            __syncthreads();
-            sink = s_sink;
-            if (sink != -1) break;
-            i = s_next;
+            const int next = row4col[cwin];
+            if (next == -1) {
+                sink = cwin;
+                break;
+            }
+            i = next;
         }
         if (sink == -1) fail = true;  // no reachable column, or the scan cap was reached
         if (fail) break;
@@ -675,7 +677,6 @@ __global__ void __launch_bounds__(kLsapThreads, 2) lsap_reg_kernel(const LsapArg
                 if (r == cur) break;
                 if (hop == nr) s_bad = 1;
             }
-            s_sink = -1;
         }
         __syncthreads();
         if (s_bad) {
