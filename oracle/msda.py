@@ -232,6 +232,64 @@ def ms_deform_attn_backward(value, spatial_shapes, loc, attn, grad_out, compute=
     return grad_value, grad_loc, grad_attn
 
 
+def forward_bf16_gather(value, spatial_shapes, loc, attn):
+    """The reference's ``"gather"`` sampler on bf16 activations with the roundings of its bf16
+    graph (``ops.py:76-135`` per level, ``ops.py:264-292`` across levels), for measuring how far
+    the reference's own bf16 output sits from the exact one (the timed kernels follow the fused
+    kernel, ``deform_pallas.py:91``, and keep these steps in float32):
+
+    * ``wx1 = bf16(ix - floor(ix))``, ``wy1`` likewise (``ops.py:88-89``); ``wx0 = bf16(1 - wx1)``,
+      ``wy0`` likewise (``ops.py:90-91``);
+    * the corner weights ``bf16(wxa * wyb)`` times the 0/1 in-bounds mask (``ops.py:121-127``);
+    * each tap ``bf16(value * weight)`` and the sum of the four (``ops.py:134``);
+    * the points weighted by the bf16 attention weights in one contraction (``ops.py:289``),
+      rounded to bf16 once.
+
+    The two sums are taken in a float32 accumulator and rounded once -- an assumption about how
+    XLA reduces bf16 operands, which this image cannot check (JAX is absent).  ``value`` and
+    ``attn`` must hold bf16 values; locations must be finite.  Returns float32 holding bf16
+    values, ``[B, Lq, H*D]``.
+    """
+    batch, len_query, heads, levels, points, dim = _check(value, spatial_shapes, loc, attn)
+    loc = np.asarray(loc, np.float32)
+    if not np.isfinite(loc).all():
+        raise ValueError("forward_bf16_gather takes finite locations only")
+    value = np.asarray(value, np.float32)
+    attn = np.asarray(attn, np.float32)
+    offsets = _level_offsets(spatial_shapes)
+    one = np.float32(1.0)
+    out = np.empty((batch, len_query, heads * dim), np.float32)
+    for b in range(batch):
+        vb = value[b * heads:(b + 1) * heads]
+        acc = np.zeros((heads, len_query, dim), np.float32)
+        weights = attn[b].reshape(len_query, heads, levels, points).transpose(1, 0, 2, 3)  # [H, Lq, L, P]
+        for level, (height, width) in enumerate(spatial_shapes):
+            level_value = vb[:, offsets[level]:offsets[level + 1], :]
+            xy = loc[b, :, :, level].transpose(1, 0, 2, 3)  # [H, Lq, P, 2]
+            ix, iy = coordinates(xy[..., 0], xy[..., 1], height, width)
+            ix0, iy0 = np.floor(ix), np.floor(iy)
+            wx1, wy1 = bf16_round(ix - ix0), bf16_round(iy - iy0)
+            wx0, wy0 = bf16_round(one - wx1), bf16_round(one - wy1)
+            index, _, _, _ = bilinear_taps(ix, iy, height, width, np.float32)
+            ix0i, iy0i = ix0.astype(np.int64), iy0.astype(np.int64)
+            in_x0 = (ix0i >= 0) & (ix0i < width)
+            in_x1 = (ix0i + 1 >= 0) & (ix0i + 1 < width)
+            in_y0 = (iy0i >= 0) & (iy0i < height)
+            in_y1 = (iy0i + 1 >= 0) & (iy0i + 1 < height)
+            corner_w = [bf16_round(wx0 * wy0) * (in_x0 & in_y0), bf16_round(wx1 * wy0) * (in_x1 & in_y0),
+                        bf16_round(wx0 * wy1) * (in_x0 & in_y1), bf16_round(wx1 * wy1) * (in_x1 & in_y1)]
+            sampled = np.zeros(ix.shape + (dim,), np.float32)
+            for corner in range(4):
+                flat = index[corner].reshape(heads, -1)
+                taken = level_value[np.arange(heads)[:, None], flat].reshape(ix.shape + (dim,))
+                sampled += bf16_round(taken * corner_w[corner].astype(np.float32)[..., None])
+            sampled = bf16_round(sampled)  # [H, Lq, P, D]
+            for p in range(points):
+                acc += weights[:, :, level, p][..., None] * sampled[:, :, p]
+        out[b] = bf16_round(acc).transpose(1, 0, 2).reshape(len_query, heads * dim)
+    return out
+
+
 def bf16_round(x: np.ndarray) -> np.ndarray:
     """Round float32 values to the nearest bfloat16 (ties to even), returned as float32."""
     bits = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
